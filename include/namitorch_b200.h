@@ -1,0 +1,289 @@
+/*
+ * namitorch_b200 — C ABI of the B200 (sm_100a) optimizer-step / mixed-precision hot path.
+ *
+ * The reference (renderityai/NamiTorch) reaches its CUDA kernels through CuPy RawKernel
+ * objects created from source strings (namitorch/backends/cuda/kernels.py:187-203) and
+ * launched on CuPy's current stream. This library is what that seam binds instead: plain
+ * pointers, element counts and a caller-given cudaStream_t passed as `void*` (NULL = the
+ * legacy default stream). No torch, CuPy or Python types cross this boundary.
+ *
+ * Conventions
+ *  - Every entry point returns an nt_status code. On failure, nt_last_error() returns a
+ *    message for the calling thread (thread-local, valid until that thread's next call).
+ *  - All kernel launches are asynchronous on `stream`; nothing here synchronises the host
+ *    except nt_stream_synchronize / nt_memcpy_sync.
+ *  - Device pointers are owned by the caller; the library never frees caller memory.
+ *  - "Workspace" buffers are caller-allocated device memory that a kernel uses for its
+ *    cross-block reduction. They must be zero-filled once after allocation; every call
+ *    leaves them zeroed again. Two launches that share one workspace must not overlap.
+ *  - Kernels never trap. A spin-wait that gives up, an out-of-range step index or a
+ *    malformed table sets a device-side error word that the caller can read.
+ */
+#ifndef NAMITORCH_B200_H
+#define NAMITORCH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NT_ABI_VERSION 1
+#define NT_MAX_GROUPS 32      /* coefficient groups per nt_adamw_mt call */
+#define NT_MAX_FOUND_INF 16   /* optimizers combined by one nt_scaler_update call */
+
+typedef enum nt_status {
+  NT_OK = 0,
+  NT_EINVAL = 1,       /* bad argument: maps to ValueError / TypeError in the Python host */
+  NT_ECUDA = 2,        /* CUDA runtime error (launch failure, invalid device, ...) */
+  NT_ENOMEM = 3,       /* device allocation failed: maps to NamiTorchCUDAOutOfMemoryError */
+  NT_EUNSUPPORTED = 4  /* layout or dtype this entry point does not handle */
+} nt_status;
+
+typedef enum nt_dtype {
+  NT_F32 = 0,
+  NT_F16 = 1,
+  NT_BF16 = 2
+} nt_dtype;
+
+typedef enum nt_reduction {
+  NT_REDUCTION_NONE = 0,
+  NT_REDUCTION_MEAN = 1,
+  NT_REDUCTION_SUM = 2
+} nt_reduction;
+
+/* ------------------------------------------------------------------------------------ */
+/* Library / runtime                                                                     */
+/* ------------------------------------------------------------------------------------ */
+
+int nt_abi_version(void);
+/* Message of the last failing call on this thread ("" when none). */
+const char* nt_last_error(void);
+
+/* Selects `device` for the calling thread and caches its SM count.
+   Replaces CUDABackend.__init__ device selection (namitorch/backends/cuda/__init__.py:24-45). */
+int nt_device_init(int device);
+/* Number of SMs of the current device (148 on B200). */
+int nt_sm_count(int* count);
+
+/* Flat-buffer allocator primitives. Replace the CuPy MemoryPool wrapper
+   (namitorch/backends/_cuda_memory.py:24-94); NT_ENOMEM carries the byte counts that
+   NamiTorchCUDAOutOfMemoryError reports (_cuda_memory.py:8-21) in nt_last_error(). */
+int nt_malloc(void** ptr, size_t bytes);
+int nt_free(void* ptr);
+int nt_mem_info(size_t* free_bytes, size_t* total_bytes);
+int nt_memset_async(void* ptr, int value, size_t bytes, void* stream);
+int nt_memcpy_async(void* dst, const void* src, size_t bytes, void* stream);
+int nt_memcpy_sync(void* dst, const void* src, size_t bytes);
+int nt_stream_synchronize(void* stream);
+
+/* Elementwise dtype conversion (round-to-nearest-even), used to seed and refresh the
+   low-precision model copy. Replaces the per-op autocast casts
+   (namitorch/nn/functional.py:57-60, namitorch/tensor.py:634-636). */
+int nt_cast(void* dst, int dst_dtype, const void* src, int src_dtype, int64_t count, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Per-tensor AdamW — the `backend.adamw` plugin seam                                    */
+/* ------------------------------------------------------------------------------------ */
+
+/* One fp32 AdamW step over `count` elements, bit-identical to the NumPy path.
+   Replaces AdamWCUDAKernel.run (namitorch/backends/cuda/adamw.py:54-73) and its kernel
+   namitorch_adamw_float32 (adamw.py:7-28). `coefficients` are the ten float32 values
+   AdamW._update_parameter builds (namitorch/optim/adam.py:82-86):
+   lr, beta1, beta2, 1-beta1, 1-beta2, eps, weight_decay, 1-lr*wd, 1-beta1^t, 1-beta2^t. */
+int nt_adamw_f32(float* param, const float* grad, float* exp_avg, float* exp_avg_sq,
+                 const float coefficients[10], int maximize, int update_parameter,
+                 uint64_t count, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Multi-tensor fused AdamW + AMP over flat arenas                                       */
+/* ------------------------------------------------------------------------------------ */
+
+/* One parameter (or the part of one that a ZeRO-1 shard owns). */
+typedef struct nt_segment {
+  const void* grad;      /* gradient storage of the segment, dtype = args.grad_dtype */
+  int64_t offset;        /* element offset of the segment in the fp32 arenas and the model copy */
+  int64_t count;         /* elements */
+  int64_t chunk_begin;   /* first work chunk: prefix sum of ceil(count / chunk_elems) */
+  int32_t group;         /* index into args.groups */
+  int32_t step_slot;     /* index into args.steps; each slot appears in at most one segment */
+} nt_segment;
+
+/* Per param-group coefficients, float32 exactly as the reference computes them
+   (_scalar, namitorch/optim/_common.py:39-47; AdamW coefficients adam.py:82-86). */
+typedef struct nt_adamw_group {
+  float lr, beta1, beta2, one_minus_beta1, one_minus_beta2, eps, weight_decay, decay_factor;
+  int32_t maximize;          /* negate the gradient (_common.py:57-62) */
+  int32_t decay_mode;        /* NT_DECAY_*: decided from the unrounded weight decay != 0 */
+  int32_t update_parameter;  /* 0 when lr == 0: moments and step still advance (adam.py:87) */
+  int32_t correction_row;    /* row of this group in the bias-correction table */
+} nt_adamw_group;
+
+enum {
+  NT_DECAY_NONE = 0,
+  NT_DECAY_DECOUPLED = 1,  /* AdamW: p = f32(p * decay_factor) before the update (_common.py:67-73) */
+  NT_DECAY_COUPLED = 2     /* Adam: g = g + f32(wd) * p (_common.py:57-64) */
+};
+
+/* Device-resident gradient statistics (64 bytes). sumsq/nonfinite/nan are consecutive so
+   that a ZeRO-1 process group can sum them with one all-reduce. */
+typedef struct nt_stats {
+  double sumsq;      /* sum of squared unscaled finite gradients */
+  double nonfinite;  /* count of non-finite unscaled gradients */
+  double nan;        /* count of NaN unscaled gradients */
+  double maxabs;     /* max |g| over non-NaN unscaled gradients */
+  double powsum;     /* sum (|g|/maxabs)^p, second pass of a general-p norm */
+  double norm;       /* total norm, namitorch/optim/clip_grad.py:63-79 */
+  double found_inf;  /* 1.0 when any unscaled gradient is non-finite (namitorch/amp.py:276-291) */
+  double error;      /* non-zero when a kernel rejected its input */
+} nt_stats;
+
+typedef struct nt_adamw_mt_args {
+  float* param;                   /* fp32 master arena */
+  float* exp_avg;                 /* fp32 first-moment arena */
+  float* exp_avg_sq;              /* fp32 second-moment arena */
+  void* model_copy;               /* low-precision copy arena (same offsets) or NULL */
+  int32_t model_dtype;            /* NT_F16 / NT_BF16 when model_copy != NULL */
+  int32_t grad_dtype;             /* NT_F32 / NT_F16 / NT_BF16 */
+  const nt_segment* segments;     /* device array */
+  int32_t num_segments;
+  int32_t chunk_elems;            /* elements per work chunk, multiple of 8 */
+  int64_t num_chunks;             /* total chunks over all segments */
+  int32_t* steps;                 /* device step counters, one per slot (state["step"]) */
+  const float* corrections;       /* device [rows][capacity][2]: f32(1-beta1^t), f32(1-beta2^t) */
+  int32_t correction_capacity;    /* t must stay < capacity */
+  const float* scale;             /* device GradScaler scale or NULL: gradients are divided by it */
+  const nt_stats* stats;     /* device stats or NULL */
+  int32_t skip_nonfinite;         /* skip the whole step when stats->found_inf != 0 (amp.py:334-341) */
+  int32_t clip;                   /* multiply by max_norm/(stats->norm+1e-6) when < 1 (clip_grad.py:106-111) */
+  double max_norm;
+  void* workspace;                /* nt_adamw_workspace_size() bytes, zero-filled once */
+  int32_t* error;                 /* device error word (may be NULL) */
+  const nt_adamw_group* groups;   /* host array of num_groups entries */
+  int32_t num_groups;             /* 1..NT_MAX_GROUPS */
+} nt_adamw_mt_args;
+
+size_t nt_adamw_workspace_size(void);
+
+/* Fused AMP optimizer step over every segment: unscale by the device loss scale, skip on a
+   device found_inf flag, global-norm clip, maximize / coupled or decoupled weight decay, the
+   two moment updates, bias correction from the device step counter, the parameter update
+   and the cast into the low-precision model copy, in one read-once / write-once pass.
+   Replaces the chain GradScaler.unscale_ -> clip_grad_norm_ -> GradScaler.step ->
+   _FirstOrderOptimizer.step -> AdamW._update_parameter (namitorch/amp.py:293-341,
+   namitorch/optim/clip_grad.py:96-112, namitorch/optim/_common.py:133-167,
+   namitorch/optim/adam.py:28-42 and :69-94). Step counters of the updated segments advance
+   by one inside the same launch (the last block commits them). */
+int nt_adamw_mt(const nt_adamw_mt_args* args, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Gradient statistics, clipping and loss scaling                                        */
+/* ------------------------------------------------------------------------------------ */
+
+/* A contiguous run of gradient elements for the statistics / transform kernels. */
+typedef struct nt_span {
+  const void* ptr;
+  int64_t count;
+  int64_t chunk_begin;   /* prefix sum of ceil(count / chunk_elems) */
+} nt_span;
+
+typedef struct nt_grad_stats_args {
+  const nt_span* spans;  /* device array */
+  int32_t num_spans;
+  int32_t chunk_elems;   /* multiple of 8 */
+  int64_t num_chunks;
+  int32_t dtype;         /* NT_F32 / NT_F16 / NT_BF16 */
+  const float* scale;    /* device loss scale or NULL */
+  int32_t pass;          /* 0: sumsq / maxabs / counts; 1: powsum (reads stats->maxabs) */
+  double norm_type;      /* p: 2, +inf or any positive value */
+  int32_t finalize;      /* 1: the last block also writes norm and found_inf */
+  nt_stats* stats;  /* device output */
+  void* workspace;       /* nt_grad_stats_workspace_size() bytes, zero-filled once */
+  size_t workspace_bytes;
+} nt_grad_stats_args;
+
+size_t nt_grad_stats_workspace_size(void);
+
+/* One deterministic two-level reduction over all spans: block partials, then the last
+   block reduces them in a fixed order. Replaces GradScaler._finite (namitorch/amp.py:276-291,
+   run after unscale_) and _total_norm (namitorch/optim/clip_grad.py:63-79). Pass 0 gives
+   found_inf, the max |g| and, for p = 2, the norm in one read; a general p needs pass 1. */
+int nt_grad_stats(const nt_grad_stats_args* args, void* stream);
+
+/* Computes norm and found_inf from the reduced fields (after a ZeRO-1 all-reduce). */
+int nt_grad_stats_finalize(nt_stats* stats, double norm_type, void* stream);
+
+/* Rewrites gradients in place: g = dtype(f32(g) / scale) when scale != NULL
+   (GradScaler.unscale_, namitorch/amp.py:310-315), then g = dtype(f64(g) * coef) with
+   coef = max_norm / (stats->norm + 1e-6) when clip != 0 and coef < 1
+   (clip_grad_norm_, namitorch/optim/clip_grad.py:106-111). */
+int nt_grad_transform(const nt_span* spans, int32_t num_spans, int32_t chunk_elems,
+                      int64_t num_chunks, int32_t dtype, const float* scale,
+                      const nt_stats* stats, int32_t clip, double max_norm, void* stream);
+
+/* clip_grad_value_ (namitorch/optim/clip_grad.py:115-121): g = dtype(clip(f64(g), -v, v)). */
+int nt_grad_clip_value(const nt_span* spans, int32_t num_spans, int32_t chunk_elems,
+                       int64_t num_chunks, int32_t dtype, double clip_value, void* stream);
+
+/* Dynamic loss-scale update on the device (GradScaler.update, namitorch/amp.py:343-358):
+   any found_inf -> scale = f32(max(tiny, scale*backoff)), tracker = 0; otherwise
+   tracker += 1 and, at growth_interval, scale = f32(min(f32max, scale*growth)), tracker = 0.
+   `found_inf` is a host array of `count` device pointers (nt_stats.found_inf fields). */
+int nt_scaler_update(float* scale, int32_t* growth_tracker, const double* const* found_inf,
+                     int32_t count, double growth_factor, double backoff_factor,
+                     int32_t growth_interval, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Fused softmax cross-entropy forward + backward                                        */
+/* ------------------------------------------------------------------------------------ */
+
+/* Device-resident summary of the targets (filled by nt_softmax_xent). */
+typedef struct nt_xent_info {
+  double denominator;   /* mean-reduction denominator: valid rows, or sum of their class weights */
+  double weight_sum;    /* sum of all class weights (C without weights) */
+  double loss_sum;      /* sum of the per-row losses */
+  double n_valid;       /* rows whose target != ignore_index */
+  double bad_targets;   /* non-ignored targets outside [0, C) (the reference raises IndexError) */
+  double error;         /* non-zero when a bounded wait gave up */
+  double reserved[2];
+} nt_xent_info;
+
+typedef struct nt_xent_args {
+  const void* logits;        /* [rows, classes] contiguous */
+  int32_t dtype;             /* NT_F32 / NT_F16 / NT_BF16 */
+  int64_t rows;
+  int64_t classes;
+  const int64_t* targets;    /* [rows] */
+  int64_t ignore_index;
+  const float* class_weight; /* [classes] or NULL */
+  float label_smoothing;     /* in [0, 1) */
+  int32_t reduction;         /* nt_reduction */
+  void* dlogits;             /* [rows, classes] same dtype, or NULL for forward only */
+  float* loss;               /* [rows] for NONE, [1] otherwise */
+  float* row_loss;           /* scratch [rows] (may alias loss for NONE) */
+  nt_xent_info* info;        /* device */
+  void* workspace;           /* nt_xent_workspace_size() bytes, zero-filled once */
+  size_t workspace_bytes;
+} nt_xent_args;
+
+size_t nt_xent_workspace_size(void);
+
+/* Cross-entropy of logits against integer targets and, in the same pass, its gradient for
+   a unit upstream gradient: mean over non-ignored rows of -log_softmax(x)[t], with class
+   weights, label smoothing and ignore_index. Replaces F.cross_entropy
+   (namitorch/nn/functional.py:792-863), the log_softmax forward
+   (namitorch/_backend.py:321-354) and its backward (namitorch/autograd.py:538-564).
+   One HBM read of the logits and one write of dlogits. */
+int nt_softmax_xent(const nt_xent_args* args, void* stream);
+
+/* Multiplies dlogits by the upstream gradient read on the device: one scalar (returns
+   without touching memory when it is exactly 1) or one value per row (reduction NONE). */
+int nt_xent_backward_scale(void* dlogits, int32_t dtype, int64_t rows, int64_t classes,
+                           const float* grad_output, int32_t per_row, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NAMITORCH_B200_H */

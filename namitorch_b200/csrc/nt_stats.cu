@@ -1,0 +1,370 @@
+// Gradient statistics (found_inf + total norm), in-place gradient transforms
+// (unscale / clip-by-norm / clip-by-value) and the device-side dynamic loss-scale update.
+#include <cmath>
+
+#include "nt_common.cuh"
+
+namespace nt {
+
+constexpr int kStatsThreads = 512;
+constexpr int kStatsMaxBlocks = 1024;
+
+struct StatsPartial {
+  double sumsq;
+  double powsum;
+  float maxabs;
+  unsigned nonfinite;
+  unsigned nan;
+  unsigned pad;
+};
+
+struct StatsWorkspace {
+  unsigned counter;
+  unsigned pad[63];
+  StatsPartial partials[kStatsMaxBlocks];
+};
+
+struct StatsParams {
+  const nt_span* spans;
+  int nspan;
+  int chunk_elems;
+  int64_t nchunks;
+  const float* scale;
+  int pass;
+  double p;
+  int finalize;
+  nt_stats* stats;
+  StatsWorkspace* ws;
+};
+
+// Norm and found_inf from the reduced fields; the early returns follow _total_norm
+// (namitorch/optim/clip_grad.py:63-79): a NaN / infinite / zero max|g| or p = inf returns
+// max|g| itself. For p = 2 the norm is sqrt(sum g^2) (one read of the gradients); any
+// other p uses max * (sum (|g|/max)^p)^(1/p) with the reference's log-space fallback.
+__device__ void stats_finalize(nt_stats* s, double p) {
+  s->found_inf = s->nonfinite > 0.0 ? 1.0 : 0.0;
+  const double mx = s->maxabs;
+  double norm;
+  if (s->nan > 0.0) norm = __longlong_as_double(0x7ff8000000000000ll);
+  else if (s->nonfinite > 0.0) norm = __longlong_as_double(0x7ff0000000000000ll);
+  else if (mx == 0.0) norm = 0.0;
+  else if (isinf(p)) norm = mx;
+  else if (p == 2.0) norm = sqrt(s->sumsq);
+  else {
+    const double total = s->powsum;
+    norm = mx * pow(total, 1.0 / p);
+    if (!isfinite(norm)) norm = exp(log(mx) + log(total) / p);
+  }
+  s->norm = norm;
+}
+
+template <int DT>
+__device__ __forceinline__ void stats_accumulate(float u, int pass, double p, double maxabs,
+                                                 double& ss, double& ps, float& mx, unsigned& nf,
+                                                 unsigned& nn) {
+  if (pass == 0) {
+    if (isnan(u)) { ++nn; ++nf; return; }
+    mx = fmaxf(mx, fabsf(u));
+    if (isinf(u)) { ++nf; return; }
+    ss += (double)u * (double)u;
+  } else {
+    if (!isfinite(u)) return;
+    const double scaled = __ddiv_rn(fabs((double)u), maxabs);
+    ps += p == 2.0 ? scaled * scaled : pow(scaled, p);
+  }
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kStatsThreads) grad_stats_kernel(const __grid_constant__ StatsParams P) {
+  __shared__ double red_d[kStatsThreads / 32];
+  __shared__ float red_f[kStatsThreads / 32];
+  __shared__ unsigned red_u[kStatsThreads / 32];
+  __shared__ bool last;
+  Unscale un;
+  un.init(P.scale);
+  const double maxabs = P.pass == 1 ? P.stats->maxabs : 0.0;
+  double ss = 0.0, ps = 0.0;
+  float mx = 0.0f;
+  unsigned nf = 0, nn = 0;
+  const int esize = DT == NT_F32 ? 4 : 2;
+
+  for (int64_t chunk = blockIdx.x; chunk < P.nchunks; chunk += gridDim.x) {
+    const int s = find_owner([&](int i) { return P.spans[i].chunk_begin; }, P.nspan, chunk);
+    const nt_span sp = P.spans[s];
+    const int64_t begin = (chunk - sp.chunk_begin) * (int64_t)P.chunk_elems;
+    int64_t end = begin + P.chunk_elems;
+    if (end > sp.count) end = sp.count;
+    int64_t e = begin;
+    if (((reinterpret_cast<uintptr_t>(static_cast<const char*>(sp.ptr) + begin * esize)) & 15u) == 0) {
+      const int64_t body_end = begin + ((end - begin) & ~(int64_t)7);
+      for (int64_t i = begin + (int64_t)threadIdx.x * 8; i < body_end; i += (int64_t)blockDim.x * 8) {
+        float x[8];
+        load8<DT>(sp.ptr, i, x);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) stats_accumulate<DT>(un(x[k]), P.pass, P.p, maxabs, ss, ps, mx, nf, nn);
+      }
+      e = body_end;
+    }
+    for (int64_t i = e + threadIdx.x; i < end; i += blockDim.x)
+      stats_accumulate<DT>(un(load1<DT>(sp.ptr, i)), P.pass, P.p, maxabs, ss, ps, mx, nf, nn);
+  }
+
+  ss = block_reduce(ss, red_d, SumOp(), 0.0);
+  ps = block_reduce(ps, red_d, SumOp(), 0.0);
+  mx = block_reduce(mx, red_f, MaxOp(), 0.0f);
+  nf = block_reduce(nf, red_u, SumOp(), 0u);
+  nn = block_reduce(nn, red_u, SumOp(), 0u);
+  if (threadIdx.x == 0) {
+    StatsPartial& out = P.ws->partials[blockIdx.x];
+    out.sumsq = ss; out.powsum = ps; out.maxabs = mx; out.nonfinite = nf; out.nan = nn;
+  }
+  if (!last_block_ticket(&P.ws->counter, &last)) return;
+
+  // Fixed-order reduction of the block partials.
+  ss = 0.0; ps = 0.0; mx = 0.0f;
+  double nfd = 0.0, nnd = 0.0;
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
+    const StatsPartial q = P.ws->partials[b];
+    ss += q.sumsq; ps += q.powsum; mx = fmaxf(mx, q.maxabs); nfd += q.nonfinite; nnd += q.nan;
+  }
+  ss = block_reduce(ss, red_d, SumOp(), 0.0);
+  ps = block_reduce(ps, red_d, SumOp(), 0.0);
+  nfd = block_reduce(nfd, red_d, SumOp(), 0.0);
+  nnd = block_reduce(nnd, red_d, SumOp(), 0.0);
+  mx = block_reduce(mx, red_f, MaxOp(), 0.0f);
+  if (threadIdx.x == 0) {
+    nt_stats* st = P.stats;
+    if (P.pass == 0) {
+      st->sumsq = ss; st->nonfinite = nfd; st->nan = nnd; st->maxabs = (double)mx;
+    } else {
+      st->powsum = ps;
+    }
+    if (P.finalize) stats_finalize(st, P.p);
+    P.ws->counter = 0u;
+  }
+}
+
+__global__ void stats_finalize_kernel(nt_stats* s, double p) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) stats_finalize(s, p);
+}
+
+// ---- in-place transforms ----------------------------------------------------------------
+struct TransformParams {
+  const nt_span* spans;
+  int nspan;
+  int chunk_elems;
+  int64_t nchunks;
+  const float* scale;
+  const nt_stats* stats;
+  int clip;
+  double max_norm;
+  int mode;          // 0: unscale / clip-by-norm, 1: clip-by-value
+  double clip_value;
+};
+
+template <int DT>
+__device__ __forceinline__ float transform_one(float x, const TransformParams& P, const Unscale& un,
+                                               bool clip, double coef) {
+  if (P.mode == 1) {
+    const double d = (double)x;
+    const double r = d < -P.clip_value ? -P.clip_value : (d > P.clip_value ? P.clip_value : d);
+    return __double2float_rn(r);
+  }
+  float u = un(x);
+  if (clip) u = __double2float_rn(__dmul_rn((double)u, coef));
+  return u;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(256) grad_transform_kernel(const __grid_constant__ TransformParams P) {
+  Unscale un;
+  un.init(P.scale);
+  bool clip = false;
+  double coef = 1.0;
+  if (P.clip && P.stats != nullptr) {
+    const double c = P.max_norm / (P.stats->norm + 1e-6);
+    if (c < 1.0) { clip = true; coef = c; }
+  }
+  if (P.mode == 0 && !un.active && !clip) return;
+  const int esize = DT == NT_F32 ? 4 : 2;
+  for (int64_t chunk = blockIdx.x; chunk < P.nchunks; chunk += gridDim.x) {
+    const int s = find_owner([&](int i) { return P.spans[i].chunk_begin; }, P.nspan, chunk);
+    const nt_span sp = P.spans[s];
+    void* ptr = const_cast<void*>(sp.ptr);
+    const int64_t begin = (chunk - sp.chunk_begin) * (int64_t)P.chunk_elems;
+    int64_t end = begin + P.chunk_elems;
+    if (end > sp.count) end = sp.count;
+    int64_t e = begin;
+    if (((reinterpret_cast<uintptr_t>(static_cast<char*>(ptr) + begin * esize)) & 15u) == 0) {
+      const int64_t body_end = begin + ((end - begin) & ~(int64_t)7);
+      for (int64_t i = begin + (int64_t)threadIdx.x * 8; i < body_end; i += (int64_t)blockDim.x * 8) {
+        float x[8];
+        load8<DT>(ptr, i, x);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] = transform_one<DT>(x[k], P, un, clip, coef);
+        store8<DT>(ptr, i, x);
+      }
+      e = body_end;
+    }
+    for (int64_t i = e + threadIdx.x; i < end; i += blockDim.x)
+      store1<DT>(ptr, i, transform_one<DT>(load1<DT>(ptr, i), P, un, clip, coef));
+  }
+}
+
+// ---- GradScaler.update ------------------------------------------------------------------
+struct ScalerParams {
+  float* scale;
+  int32_t* tracker;
+  const double* found[NT_MAX_FOUND_INF];
+  int count;
+  double growth;
+  double backoff;
+  int interval;
+};
+
+__global__ void scaler_update_kernel(const __grid_constant__ ScalerParams P) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  bool inf = false;
+  for (int i = 0; i < P.count; ++i) inf = inf || (*P.found[i] != 0.0);
+  const double tiny = 1.1754943508222875e-38;     // float32 tiny
+  const double fmax32 = 3.4028234663852886e+38;   // float32 max
+  const double s = (double)*P.scale;
+  if (inf) {
+    double r = __dmul_rn(s, P.backoff);
+    if (r < tiny) r = tiny;
+    *P.scale = __double2float_rn(r);
+    *P.tracker = 0;
+  } else {
+    int t = *P.tracker + 1;
+    if (t == P.interval) {
+      double r = __dmul_rn(s, P.growth);
+      if (r > fmax32) r = fmax32;
+      *P.scale = __double2float_rn(r);
+      t = 0;
+    }
+    *P.tracker = t;
+  }
+}
+
+static int check_spans(const nt_span* spans, int32_t num_spans, int32_t chunk_elems, int64_t num_chunks,
+                       int32_t dtype, const char* who) {
+  if (num_spans < 0 || num_chunks < 0) { set_error("%s: negative sizes", who); return NT_EINVAL; }
+  if (num_spans > 0 && num_chunks > 0 && !spans) { set_error("%s: spans is NULL", who); return NT_EINVAL; }
+  if (chunk_elems <= 0 || (chunk_elems & 7) != 0) {
+    set_error("%s: chunk_elems must be a positive multiple of 8 (got %d)", who, chunk_elems);
+    return NT_EINVAL;
+  }
+  if (dtype_size(dtype) == 0) { set_error("%s: unsupported dtype %d", who, dtype); return NT_EUNSUPPORTED; }
+  return NT_OK;
+}
+
+template <typename K, typename Params>
+static int launch_grid(K kernel, const Params& P, int64_t nchunks, int threads, int per_sm,
+                       int64_t max_blocks, cudaStream_t stream, const char* what) {
+  int64_t grid = (int64_t)current_sm_count() * per_sm;
+  if (grid > max_blocks) grid = max_blocks;
+  if (grid > nchunks) grid = nchunks;
+  if (grid < 1) grid = 1;
+  kernel<<<(unsigned)grid, threads, 0, stream>>>(P);
+  return launch_status(what);
+}
+
+}  // namespace nt
+
+using namespace nt;
+
+extern "C" {
+
+size_t nt_grad_stats_workspace_size(void) { return sizeof(StatsWorkspace); }
+
+int nt_grad_stats(const nt_grad_stats_args* args, void* stream) {
+  if (!args) { set_error("nt_grad_stats: args is NULL"); return NT_EINVAL; }
+  const nt_grad_stats_args& a = *args;
+  int rc = check_spans(a.spans, a.num_spans, a.chunk_elems, a.num_chunks, a.dtype, "nt_grad_stats");
+  if (rc) return rc;
+  if (!a.stats || !a.workspace) { set_error("nt_grad_stats: stats / workspace is NULL"); return NT_EINVAL; }
+  if (a.workspace_bytes < sizeof(StatsWorkspace)) {
+    set_error("nt_grad_stats: workspace needs %zu bytes (got %zu)", sizeof(StatsWorkspace), a.workspace_bytes);
+    return NT_EINVAL;
+  }
+  if (a.pass != 0 && a.pass != 1) { set_error("nt_grad_stats: pass must be 0 or 1"); return NT_EINVAL; }
+  if (!(a.norm_type > 0.0)) { set_error("nt_grad_stats: norm_type must be positive"); return NT_EINVAL; }
+  StatsParams P;
+  P.spans = a.spans; P.nspan = a.num_spans; P.chunk_elems = a.chunk_elems;
+  P.nchunks = (a.num_spans == 0) ? 0 : a.num_chunks;
+  P.scale = a.scale; P.pass = a.pass; P.p = a.norm_type; P.finalize = a.finalize;
+  P.stats = a.stats; P.ws = static_cast<StatsWorkspace*>(a.workspace);
+  cudaStream_t s = as_stream(stream);
+  // An empty gradient list still runs one block so the statistics are written.
+  const int64_t nchunks = P.nchunks > 0 ? P.nchunks : 1;
+  switch (a.dtype) {
+    case NT_F32: return launch_grid(grad_stats_kernel<NT_F32>, P, nchunks, kStatsThreads, 4, kStatsMaxBlocks, s, "nt_stats launch");
+    case NT_F16: return launch_grid(grad_stats_kernel<NT_F16>, P, nchunks, kStatsThreads, 4, kStatsMaxBlocks, s, "nt_stats launch");
+    default: return launch_grid(grad_stats_kernel<NT_BF16>, P, nchunks, kStatsThreads, 4, kStatsMaxBlocks, s, "nt_stats launch");
+  }
+}
+
+int nt_grad_stats_finalize(nt_stats* stats, double norm_type, void* stream) {
+  if (!stats) { set_error("nt_grad_stats_finalize: stats is NULL"); return NT_EINVAL; }
+  if (!(norm_type > 0.0)) { set_error("nt_grad_stats_finalize: norm_type must be positive"); return NT_EINVAL; }
+  stats_finalize_kernel<<<1, 32, 0, as_stream(stream)>>>(stats, norm_type);
+  return launch_status("nt_grad_stats_finalize launch");
+}
+
+static int transform_common(TransformParams& P, int32_t dtype, cudaStream_t s) {
+  if (P.nspan == 0 || P.nchunks == 0) return NT_OK;
+  switch (dtype) {
+    case NT_F32: return launch_grid(grad_transform_kernel<NT_F32>, P, P.nchunks, 256, 8, 1 << 20, s, "nt_grad_transform launch");
+    case NT_F16: return launch_grid(grad_transform_kernel<NT_F16>, P, P.nchunks, 256, 8, 1 << 20, s, "nt_grad_transform launch");
+    default: return launch_grid(grad_transform_kernel<NT_BF16>, P, P.nchunks, 256, 8, 1 << 20, s, "nt_grad_transform launch");
+  }
+}
+
+int nt_grad_transform(const nt_span* spans, int32_t num_spans, int32_t chunk_elems, int64_t num_chunks,
+                      int32_t dtype, const float* scale, const nt_stats* stats, int32_t clip,
+                      double max_norm, void* stream) {
+  int rc = check_spans(spans, num_spans, chunk_elems, num_chunks, dtype, "nt_grad_transform");
+  if (rc) return rc;
+  if (clip && !stats) { set_error("nt_grad_transform: clip needs stats"); return NT_EINVAL; }
+  TransformParams P;
+  P.spans = spans; P.nspan = num_spans; P.chunk_elems = chunk_elems; P.nchunks = num_chunks;
+  P.scale = scale; P.stats = stats; P.clip = clip; P.max_norm = max_norm; P.mode = 0; P.clip_value = 0.0;
+  return transform_common(P, dtype, as_stream(stream));
+}
+
+int nt_grad_clip_value(const nt_span* spans, int32_t num_spans, int32_t chunk_elems, int64_t num_chunks,
+                       int32_t dtype, double clip_value, void* stream) {
+  int rc = check_spans(spans, num_spans, chunk_elems, num_chunks, dtype, "nt_grad_clip_value");
+  if (rc) return rc;
+  if (!(clip_value >= 0.0) || !isfinite(clip_value)) {
+    set_error("clip_value must be finite and nonnegative.");
+    return NT_EINVAL;
+  }
+  TransformParams P;
+  P.spans = spans; P.nspan = num_spans; P.chunk_elems = chunk_elems; P.nchunks = num_chunks;
+  P.scale = nullptr; P.stats = nullptr; P.clip = 0; P.max_norm = 0.0; P.mode = 1; P.clip_value = clip_value;
+  return transform_common(P, dtype, as_stream(stream));
+}
+
+int nt_scaler_update(float* scale, int32_t* growth_tracker, const double* const* found_inf, int32_t count,
+                     double growth_factor, double backoff_factor, int32_t growth_interval, void* stream) {
+  if (!scale || !growth_tracker) { set_error("nt_scaler_update: NULL scale / tracker"); return NT_EINVAL; }
+  if (count < 1 || count > NT_MAX_FOUND_INF || !found_inf) {
+    set_error("nt_scaler_update: count must be in [1, %d]", NT_MAX_FOUND_INF);
+    return NT_EINVAL;
+  }
+  if (!(growth_factor > 1.0) || !isfinite(growth_factor)) { set_error("growth_factor must be greater than 1."); return NT_EINVAL; }
+  if (!(backoff_factor > 0.0 && backoff_factor < 1.0)) { set_error("backoff_factor must be between 0 and 1."); return NT_EINVAL; }
+  if (growth_interval <= 0) { set_error("growth_interval must be positive."); return NT_EINVAL; }
+  ScalerParams P;
+  P.scale = scale; P.tracker = growth_tracker; P.count = count;
+  for (int i = 0; i < NT_MAX_FOUND_INF; ++i) P.found[i] = i < count ? found_inf[i] : nullptr;
+  for (int i = 0; i < count; ++i) {
+    if (!P.found[i]) { set_error("nt_scaler_update: found_inf[%d] is NULL", i); return NT_EINVAL; }
+  }
+  P.growth = growth_factor; P.backoff = backoff_factor; P.interval = growth_interval;
+  scaler_update_kernel<<<1, 32, 0, as_stream(stream)>>>(P);
+  return launch_status("nt_scaler_update launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,500 @@
+// Fused softmax cross-entropy forward + backward.
+//
+// Math (per row i with target t, logits x, class weights w (1 without), smoothing e, V classes):
+//   M = max x,  S = sum exp(x - M),  lse = M + log S,  logp = x - lse,  p = exp(x - M) / S
+//   loss_i = (1-e) * (-w_t * logp_t) + e * (-(1/V) * sum_c w_c * logp_c)
+//   dloss_i/dx_c = (1-e) * w_t * (p_c - [c==t]) + (e/V) * (p_c * W - w_c),   W = sum_c w_c
+// reduced by 'mean' (divide by sum of w_t over non-ignored rows), 'sum' or 'none'
+// (namitorch/nn/functional.py:819-863; log_softmax forward namitorch/_backend.py:321-354;
+// backward namitorch/autograd.py:538-564, whose rows of all -inf get a zero gradient).
+// Non-finite rows follow the reference: a NaN or +inf logit makes the whole row NaN;
+// a row of all -inf has loss +inf and zero gradient.
+//
+// Data movement: each CTA is persistent over rows. A row (V * esize bytes, not 16-byte
+// aligned in general) is fetched with one cp.async.bulk from the 16-byte boundary at or
+// below its start into shared memory, completion tracked by an mbarrier; the few bytes
+// past the last 16-byte boundary of the whole tensor are loaded with plain loads. Three
+// passes then run from shared memory (max, sum of exp, gradient), and the gradient is
+// written with 16-byte streaming stores at the same alignment offset. HBM traffic is one
+// read of the logits and one write of dlogits.
+#include <cmath>
+
+#include "nt_common.cuh"
+
+namespace nt {
+
+constexpr int kXentThreads = 512;
+constexpr int kPrepThreads = 1024;
+
+struct XentWorkspace {
+  unsigned counter;
+  unsigned pad[63];
+};
+
+struct XentParams {
+  const void* logits;
+  void* dl;
+  const int64_t* targets;
+  const float* weight;
+  int64_t rows;
+  int64_t classes;
+  int64_t ignore;
+  float smoothing;
+  int reduction;
+  float* loss;
+  float* row_loss;
+  nt_xent_info* info;
+  XentWorkspace* ws;
+  uintptr_t tensor_end;   // one past the last byte of the logits
+  int staged;
+};
+
+// ---- PTX helpers (mbarrier + bulk async copy; no cluster multicast) ---------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// 2^x on the SFU (approximate, subnormal results kept).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per row: far beyond any real copy
+
+// Unpacks one 16-byte vector of the staged row into fp32 values.
+template <int DT>
+__device__ __forceinline__ void unpack16(const uint4& raw, float* out) {
+  if constexpr (DT == NT_F32) {
+    out[0] = __uint_as_float(raw.x); out[1] = __uint_as_float(raw.y);
+    out[2] = __uint_as_float(raw.z); out[3] = __uint_as_float(raw.w);
+  } else if constexpr (DT == NT_BF16) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      out[2 * k] = __uint_as_float(w[k] << 16);
+      out[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+    }
+  } else {
+    const __half* h = reinterpret_cast<const __half*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) out[k] = __half2float(h[k]);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ uint4 pack16(const float* v) {
+  uint4 raw;
+  if constexpr (DT == NT_F32) {
+    raw.x = __float_as_uint(v[0]); raw.y = __float_as_uint(v[1]);
+    raw.z = __float_as_uint(v[2]); raw.w = __float_as_uint(v[3]);
+  } else {
+    using T = typename Elem<DT>::T;
+    T* h = reinterpret_cast<T*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) h[k] = Elem<DT>::from_f32(v[k]);
+  }
+  return raw;
+}
+
+// Per-row constants of the gradient formula.
+struct RowGrad {
+  int mode;        // 0: zero row, 1: NaN row, 2: regular
+  float invS;      // 1 / S
+  float shift;     // M * log2(e)
+  float a;         // coefficient of p_c
+  float b;         // subtracted at c == t
+  float g;         // coefficient of -w_c (or the constant without weights)
+  int64_t t;
+};
+
+__device__ __forceinline__ float grad_value(float x, int64_t c, const RowGrad& r, const float* weight) {
+  if (r.mode == 0) return 0.0f;
+  if (r.mode == 1) return __int_as_float(0x7fc00000);
+  const float p = ex2(fmaf(x, kLog2e, -r.shift)) * r.invS;
+  float d = r.a * p;
+  if (c == r.t) d -= r.b;
+  if (r.g != 0.0f) d -= weight ? r.g * weight[c] : r.g;
+  return d;
+}
+
+__global__ void __launch_bounds__(kPrepThreads) xent_prepare_kernel(const __grid_constant__ XentParams P) {
+  __shared__ double red[kPrepThreads / 32];
+  double valid = 0.0, bad = 0.0, den = 0.0, wsum = 0.0;
+  for (int64_t i = threadIdx.x; i < P.rows; i += blockDim.x) {
+    const int64_t t = P.targets[i];
+    if (t == P.ignore) continue;
+    if (t < 0 || t >= P.classes) { bad += 1.0; continue; }
+    valid += 1.0;
+    den += P.weight ? (double)P.weight[t] : 1.0;
+  }
+  if (P.weight) {
+    for (int64_t c = threadIdx.x; c < P.classes; c += blockDim.x) wsum += (double)P.weight[c];
+  }
+  valid = block_reduce(valid, red, SumOp(), 0.0);
+  bad = block_reduce(bad, red, SumOp(), 0.0);
+  den = block_reduce(den, red, SumOp(), 0.0);
+  wsum = block_reduce(wsum, red, SumOp(), 0.0);
+  if (threadIdx.x == 0) {
+    nt_xent_info* info = P.info;
+    info->n_valid = valid;
+    info->bad_targets = bad;
+    info->denominator = den;
+    info->weight_sum = P.weight ? wsum : (double)P.classes;
+    info->loss_sum = 0.0;
+    info->error = 0.0;
+    if (P.rows == 0 && P.reduction != NT_REDUCTION_NONE) P.loss[0] = 0.0f;
+  }
+}
+
+template <int DT, bool STAGED>
+__global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constant__ XentParams P) {
+  extern __shared__ __align__(128) unsigned char stage[];
+  __shared__ uint64_t bar;
+  __shared__ float red_f[kXentThreads / 32];
+  __shared__ double red_d[kXentThreads / 32];
+  __shared__ bool last;
+  __shared__ int abort_flag;
+
+  constexpr int ES = DT == NT_F32 ? 4 : 2;
+  constexpr int EPV = 16 / ES;  // elements per 16-byte vector
+  const int64_t V = P.classes;
+  const nt_xent_info* info = P.info;
+  const bool mean = P.reduction == NT_REDUCTION_MEAN;
+  const double D = mean ? info->denominator : 1.0;
+  const bool zero_all = mean && D == 0.0;
+  const double W = info->weight_sum;
+  const float inv_den = zero_all ? 0.0f : (float)(1.0 / D);
+  const float e = P.smoothing;
+  const bool smooth = e != 0.0f;
+
+  if (STAGED) {
+    if (threadIdx.x == 0) {
+      mbar_init(&bar, 1);
+      abort_flag = 0;
+      fence_proxy_async();
+    }
+    __syncthreads();
+  }
+  uint32_t phase = 0;
+
+  for (int64_t row = blockIdx.x; row < P.rows; row += gridDim.x) {
+    const int64_t t = P.targets[row];
+    const bool valid = t != P.ignore && t >= 0 && t < V;
+    const char* row_ptr = static_cast<const char*>(P.logits) + row * V * ES;
+    const uintptr_t start = reinterpret_cast<uintptr_t>(row_ptr);
+    const uintptr_t a = start & ~(uintptr_t)15;
+    const int head = (int)(start - a);
+    const int64_t span = head + V * ES;                  // bytes from a to the row end
+    const int64_t nvec = (span + 15) / 16;
+
+    if (STAGED) {
+      int64_t bulk = nvec * 16;
+      const uintptr_t limit = P.tensor_end & ~(uintptr_t)15;
+      if ((int64_t)(limit - a) < bulk) bulk = (int64_t)(limit - a);
+      if (threadIdx.x == 0) {
+        fence_proxy_async();
+        mbar_arrive_expect_tx(&bar, (uint32_t)bulk);
+        if (bulk > 0) bulk_g2s(stage, reinterpret_cast<const void*>(a), (uint32_t)bulk, &bar);
+      }
+      // Bytes between the last 16-byte boundary of the tensor and its end.
+      for (int64_t k = bulk + threadIdx.x; k < span; k += blockDim.x)
+        stage[k] = *reinterpret_cast<const unsigned char*>(a + k);
+      if (threadIdx.x == 0) {
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(&bar, phase)) {
+          if (globaltimer() - t0 > kWaitLimitNs) { abort_flag = 1; break; }
+        }
+      }
+      __syncthreads();
+      phase ^= 1u;
+      if (abort_flag) {
+        if (threadIdx.x == 0) atomicAdd(&P.info->error, 1.0);
+        return;  // the copy never completed; leave the row untouched
+      }
+    }
+
+    auto vec_at = [&](int64_t k, float* x) {
+      if (STAGED) {
+        unpack16<DT>(reinterpret_cast<const uint4*>(stage)[k], x);
+      } else {
+        const int64_t j0 = (k * 16 - head) / ES;
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) {
+          const int64_t j = j0 + q;
+          x[q] = (j >= 0 && j < V) ? load1<DT>(P.logits, row * V + j) : 0.0f;
+        }
+      }
+    };
+
+    // Pass 1: max (NaN tracked separately) and, for smoothing, sum_c w_c x_c.
+    float mx = -INFINITY;
+    float nan_seen = 0.0f;
+    double swx = 0.0;
+    for (int64_t k = threadIdx.x; k < nvec; k += blockDim.x) {
+      float x[EPV];
+      vec_at(k, x);
+      const int64_t j0 = (k * 16 - head) / ES;
+#pragma unroll
+      for (int q = 0; q < EPV; ++q) {
+        const int64_t j = j0 + q;
+        if (j < 0 || j >= V) continue;
+        if (isnan(x[q])) nan_seen = 1.0f;
+        mx = fmaxf(mx, x[q]);
+        if (smooth) swx += P.weight ? (double)P.weight[j] * (double)x[q] : (double)x[q];
+      }
+    }
+    mx = block_reduce(mx, red_f, MaxOp(), -INFINITY);
+    nan_seen = block_reduce(nan_seen, red_f, MaxOp(), 0.0f);
+    if (smooth) swx = block_reduce(swx, red_d, SumOp(), 0.0);
+    const bool bad_row = nan_seen != 0.0f || mx == INFINITY;
+    const bool neg_row = !bad_row && mx == -INFINITY;
+
+    // Pass 2: S = sum exp(x - M).
+    const float shift = mx * kLog2e;
+    float s = 0.0f;
+    if (!bad_row && !neg_row) {
+      for (int64_t k = threadIdx.x; k < nvec; k += blockDim.x) {
+        float x[EPV];
+        vec_at(k, x);
+        const int64_t j0 = (k * 16 - head) / ES;
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) {
+          const int64_t j = j0 + q;
+          if (j >= 0 && j < V) s += ex2(fmaf(x[q], kLog2e, -shift));
+        }
+      }
+    }
+    s = block_reduce(s, red_f, SumOp(), 0.0f);
+
+    // Row loss and gradient constants.
+    RowGrad rg;
+    rg.t = valid ? t : -1;
+    rg.invS = 1.0f / s;
+    rg.shift = shift;
+    const float wt = valid ? (P.weight ? P.weight[t] : 1.0f) : 0.0f;
+    float loss_i = 0.0f;
+    if (!valid || zero_all) {
+      rg.mode = 0;
+    } else if (bad_row) {
+      rg.mode = 1;
+      loss_i = __int_as_float(0x7fc00000);
+    } else if (neg_row) {
+      rg.mode = 0;
+      loss_i = INFINITY;
+    } else {
+      rg.mode = 2;
+      float xt;
+      if (STAGED) {
+        const int64_t off = head + t * ES;
+        if constexpr (DT == NT_F32) xt = *reinterpret_cast<const float*>(stage + off);
+        else if constexpr (DT == NT_BF16) xt = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(stage + off));
+        else xt = __half2float(*reinterpret_cast<const __half*>(stage + off));
+      } else {
+        xt = load1<DT>(P.logits, row * V + t);
+      }
+      const float lse = mx + logf(s);
+      const float base = -wt * (xt - lse);
+      if (smooth) {
+        const double sm = -(swx - (double)lse * W) / (double)V;
+        loss_i = (1.0f - e) * base + e * (float)sm;
+      } else {
+        loss_i = base;
+      }
+      if (P.weight) {
+        rg.a = ((1.0f - e) * wt + (float)((double)e * W / (double)V)) * inv_den;
+        rg.b = (1.0f - e) * wt * inv_den;
+        rg.g = smooth ? (float)((double)e / (double)V) * inv_den : 0.0f;
+      } else {
+        rg.a = inv_den;
+        rg.b = (1.0f - e) * inv_den;
+        rg.g = smooth ? (float)((double)e / (double)V) * inv_den : 0.0f;
+      }
+    }
+    if (threadIdx.x == 0) P.row_loss[row] = valid ? (zero_all ? 0.0f : loss_i) : 0.0f;
+
+    // Pass 3: gradient.
+    if (P.dl != nullptr) {
+      char* out_row = static_cast<char*>(P.dl) + row * V * ES;
+      const uintptr_t oa = reinterpret_cast<uintptr_t>(out_row) & ~(uintptr_t)15;
+      const int ohead = (int)(reinterpret_cast<uintptr_t>(out_row) - oa);
+      const bool same_phase = STAGED && ohead == head;
+      for (int64_t k = threadIdx.x; k < nvec; k += blockDim.x) {
+        float x[EPV], d[EPV];
+        vec_at(k, x);
+        const int64_t j0 = (k * 16 - head) / ES;
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) d[q] = grad_value(x[q], j0 + q, rg, P.weight);
+        if (same_phase && j0 >= 0 && j0 + EPV <= V) {
+          __stcs(reinterpret_cast<uint4*>(oa + (uintptr_t)k * 16), pack16<DT>(d));
+        } else {
+#pragma unroll
+          for (int q = 0; q < EPV; ++q) {
+            const int64_t j = j0 + q;
+            if (j >= 0 && j < V) store1<DT>(P.dl, row * V + j, d[q]);
+          }
+        }
+      }
+    }
+    if (STAGED) __syncthreads();  // every thread is done with the staged row
+  }
+
+  // Loss reduction over rows, in a fixed order, by the last block.
+  if (P.reduction == NT_REDUCTION_NONE) return;
+  if (!last_block_ticket(&P.ws->counter, &last)) return;
+  double acc = 0.0;
+  for (int64_t r = threadIdx.x; r < P.rows; r += blockDim.x) acc += (double)P.row_loss[r];
+  acc = block_reduce(acc, red_d, SumOp(), 0.0);
+  if (threadIdx.x == 0) {
+    P.info->loss_sum = acc;
+    P.loss[0] = zero_all ? 0.0f : (float)(mean ? acc / D : acc);
+    P.ws->counter = 0u;
+  }
+}
+
+// Upstream-gradient multiply for the autograd backward.
+template <int DT>
+__global__ void __launch_bounds__(256) xent_scale_kernel(void* dl, int64_t rows, int64_t classes,
+                                                         const float* grad, int per_row) {
+  if (!per_row && *grad == 1.0f) return;
+  const int64_t n = rows * classes;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float g = per_row ? grad[i / classes] : *grad;
+    store1<DT>(dl, i, __fmul_rn(load1<DT>(dl, i), g));
+  }
+}
+
+template <int DT>
+static int launch_xent(const XentParams& P0, cudaStream_t stream) {
+  XentParams P = P0;
+  constexpr int ES = DT == NT_F32 ? 4 : 2;
+  const size_t stage_bytes = (size_t)(((P.classes * ES + 15) / 16 + 1) * 16);
+  int max_optin = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const bool can_stage = P.staged && stage_bytes + 4096 <= (size_t)max_optin;
+  int per_sm = 1;
+  if (can_stage) {
+    cudaError_t err = cudaFuncSetAttribute(xent_kernel<DT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)stage_bytes);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(xent)");
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, xent_kernel<DT, true>, kXentThreads, stage_bytes) !=
+            cudaSuccess || per_sm < 1)
+      per_sm = 1;
+  } else {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, xent_kernel<DT, false>, kXentThreads, 0) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+  }
+  int64_t grid = (int64_t)current_sm_count() * per_sm;
+  if (grid > P.rows) grid = P.rows;
+  if (grid < 1) grid = 1;
+  P.staged = can_stage;
+  if (can_stage)
+    xent_kernel<DT, true><<<(unsigned)grid, kXentThreads, stage_bytes, stream>>>(P);
+  else
+    xent_kernel<DT, false><<<(unsigned)grid, kXentThreads, 0, stream>>>(P);
+  return launch_status("nt_softmax_xent launch");
+}
+
+}  // namespace nt
+
+using namespace nt;
+
+extern "C" {
+
+size_t nt_xent_workspace_size(void) { return sizeof(XentWorkspace); }
+
+int nt_softmax_xent(const nt_xent_args* args, void* stream) {
+  if (!args) { set_error("nt_softmax_xent: args is NULL"); return NT_EINVAL; }
+  const nt_xent_args& a = *args;
+  if (a.rows < 0) { set_error("nt_softmax_xent: negative row count"); return NT_EINVAL; }
+  if (a.classes <= 0) {
+    set_error("Classification loss input must have shape [..., C] with C > 0, got C=%lld.", (long long)a.classes);
+    return NT_EINVAL;
+  }
+  if (dtype_size(a.dtype) == 0) { set_error("nt_softmax_xent: unsupported dtype %d", a.dtype); return NT_EUNSUPPORTED; }
+  if (a.reduction < NT_REDUCTION_NONE || a.reduction > NT_REDUCTION_SUM) {
+    set_error("nt_softmax_xent: invalid reduction %d", a.reduction);
+    return NT_EINVAL;
+  }
+  if (!(a.label_smoothing >= 0.0f && a.label_smoothing < 1.0f)) {
+    set_error("label_smoothing must be in [0, 1).");
+    return NT_EINVAL;
+  }
+  if (!a.info || !a.loss || !a.workspace || (a.rows > 0 && (!a.logits || !a.targets || !a.row_loss))) {
+    set_error("nt_softmax_xent: NULL logits/targets/loss/row_loss/info/workspace");
+    return NT_EINVAL;
+  }
+  if (a.workspace_bytes < sizeof(XentWorkspace)) {
+    set_error("nt_softmax_xent: workspace needs %zu bytes", sizeof(XentWorkspace));
+    return NT_EINVAL;
+  }
+  XentParams P;
+  P.logits = a.logits; P.dl = a.dlogits; P.targets = a.targets; P.weight = a.class_weight;
+  P.rows = a.rows; P.classes = a.classes; P.ignore = a.ignore_index; P.smoothing = a.label_smoothing;
+  P.reduction = a.reduction; P.loss = a.loss; P.row_loss = a.row_loss; P.info = a.info;
+  P.ws = static_cast<XentWorkspace*>(a.workspace);
+  const int es = dtype_size(a.dtype);
+  P.tensor_end = reinterpret_cast<uintptr_t>(a.logits) + (uintptr_t)(a.rows * a.classes * es);
+  P.staged = aligned16(a.logits) && (a.dlogits == nullptr || aligned16(a.dlogits));
+  cudaStream_t s = as_stream(stream);
+  xent_prepare_kernel<<<1, kPrepThreads, 0, s>>>(P);
+  int rc = launch_status("nt_softmax_xent prepare launch");
+  if (rc || a.rows == 0) return rc;
+  switch (a.dtype) {
+    case NT_F32: return launch_xent<NT_F32>(P, s);
+    case NT_F16: return launch_xent<NT_F16>(P, s);
+    default: return launch_xent<NT_BF16>(P, s);
+  }
+}
+
+int nt_xent_backward_scale(void* dlogits, int32_t dtype, int64_t rows, int64_t classes, const float* grad_output,
+                           int32_t per_row, void* stream) {
+  if (rows < 0 || classes < 0) { set_error("nt_xent_backward_scale: negative sizes"); return NT_EINVAL; }
+  if (rows == 0 || classes == 0) return NT_OK;
+  if (!dlogits || !grad_output) { set_error("nt_xent_backward_scale: NULL pointer"); return NT_EINVAL; }
+  int64_t blocks = (rows * classes + 255) / 256;
+  const int64_t cap = (int64_t)current_sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t s = as_stream(stream);
+  switch (dtype) {
+    case NT_F32: xent_scale_kernel<NT_F32><<<(unsigned)blocks, 256, 0, s>>>(dlogits, rows, classes, grad_output, per_row); break;
+    case NT_F16: xent_scale_kernel<NT_F16><<<(unsigned)blocks, 256, 0, s>>>(dlogits, rows, classes, grad_output, per_row); break;
+    case NT_BF16: xent_scale_kernel<NT_BF16><<<(unsigned)blocks, 256, 0, s>>>(dlogits, rows, classes, grad_output, per_row); break;
+    default: set_error("nt_xent_backward_scale: unsupported dtype %d", dtype); return NT_EUNSUPPORTED;
+  }
+  return launch_status("nt_xent_backward_scale launch");
+}
+
+}  // extern "C"
