@@ -1,0 +1,480 @@
+#!/usr/bin/env python
+"""Benchmark of the fused AdamW + AMP optimizer step (and the fused softmax cross-entropy).
+
+Default workload (N = 1): BASELINE configuration 3, the 1.3B-parameter GPT-shaped set
+(291 tensors, 1,315,721,216 parameters) with fp32 master weights / moments, a bf16 model
+copy and bf16 gradients. One step is the AMP loop of the reference training runner
+(namitorch/training/runner.py:247-254) through this package's public API:
+    scaler.scale(loss); scaler.unscale_(opt); clip_grad_norm_(params, 1.0);
+    scaler.step(opt); scaler.update()
+which runs three kernels: gradient statistics (found_inf + norm), the fused multi-tensor
+AdamW update (unscale, skip, clip, decoupled decay, moments, bias correction, bf16
+cast-out) and the loss-scale update. With N > 1 (torchrun), the same step runs ZeRO-1
+sharded: bf16 gradients are reduce-scattered, each rank updates its 1/N shard and the bf16
+model copy is all-gathered (NCCL over NVLink); ``value`` is whole-model params/s.
+
+``--workload xent`` times the fused softmax cross-entropy forward + backward on
+configuration 4 ([8192, 50257] bf16 logits).
+
+``--impl reference`` times the reference algorithm on the host CPU (the NumPy oracle port,
+all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "AdamW+AMP step params/s (achieved HBM GB/s vs B200 peak)"
+FALLBACK_HBM_GBS = 6650.0
+BYTES_UPDATE = 28      # adamw_mt: R p4 g2 m4 v4 + W p4 m4 v4 copy2 per parameter
+BYTES_STATS = 2        # grad_stats: R g2 per parameter
+BYTES_STEP = BYTES_UPDATE + BYTES_STATS
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["1p3b", "124m", "small", "xent"], default="1p3b")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-sample", type=int, default=1 << 25, help="parameters in the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args(argv)
+
+
+def dist_env():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def measured_peak():
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            data = json.loads(path.read_text())
+            return float(data["hbm_gbs"]), "measured"
+        except (ValueError, KeyError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def committed_traffic(kernel: str, workload: str):
+    """dram bytes per launch from the committed ncu summary of this kernel/workload, if any."""
+    path = REPO / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    try:
+        return json.loads(path.read_text()).get(f"{kernel}:{workload}")
+    except ValueError:
+        return None
+
+
+# ---- clocks sampling --------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str | None):
+        self.proc = None
+        self.lines: list[str] = []
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if gpu_id:
+            cmd += ["-i", gpu_id]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [[c.strip() for c in line.split(",")] for line in out.splitlines() if line.strip()]
+        rows = [r for r in rows if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower() == "active"})
+        loaded = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---- CPU baseline (reference algorithm on the host) ------------------------------------------
+def cpu_amp_sample(n: int, steps: int, threads: int) -> dict:
+    """The reference AMP step (unscale, finite check, two-pass norm, clip, AdamW) on a sample of
+    ``n`` parameters, split into per-thread chunks (NumPy ufuncs release the GIL)."""
+    from oracle import adamw as oadamw
+    from oracle.casts import round_to_bf16
+    rng = np.random.default_rng(0)
+    p = rng.normal(0, 0.02, n).astype(np.float32)
+    g0 = round_to_bf16((rng.normal(0, 1e-3, n) * 65536.0).astype(np.float32))
+    m = np.zeros_like(p)
+    v = np.zeros_like(p)
+    chunk = max(1 << 20, n // max(threads, 1) // 4)
+    bounds = [(i, min(n, i + chunk)) for i in range(0, n, chunk)]
+    scale = 65536.0
+    pool = ThreadPoolExecutor(max_workers=threads)
+    times = []
+    step = 0
+    for _ in range(steps):
+        g = g0.copy()
+        t0 = time.perf_counter()
+
+        def unscale(b):
+            s, e = b
+            np.divide(g[s:e], scale, out=g[s:e])
+            return bool(np.all(np.isfinite(g[s:e]))), float(np.max(np.abs(g[s:e]), initial=0))
+
+        parts = list(pool.map(unscale, bounds))
+        finite = all(f for f, _ in parts)
+        mx = max(x for _, x in parts)
+
+        def sumsq(b):
+            s, e = b
+            scaled = np.abs(np.asarray(g[s:e], dtype=np.float64)) / mx
+            return float(np.sum(np.power(scaled, 2.0), dtype=np.float64))
+
+        total = sum(pool.map(sumsq, bounds))
+        norm = mx * math.sqrt(total)
+        coef = 1.0 / (norm + 1e-6)
+        if finite:
+            def clip_and_update(b):
+                s, e = b
+                if coef < 1:
+                    g[s:e] = (np.asarray(g[s:e], np.float64) * coef).astype(np.float32)
+                oadamw.adam_update(p[s:e], g[s:e], m[s:e], v[s:e], step, lr=3e-4, beta1=0.9, beta2=0.999,
+                                   eps=1e-8, weight_decay=0.1)
+
+            list(pool.map(clip_and_update, bounds))
+            step += 1
+        times.append(time.perf_counter() - t0)
+    pool.shutdown()
+    t = statistics.median(times)
+    return {"value": n / t, "unit": "params/s", "cores": threads, "kind": "port",
+            "sample": f"{n} parameters of the workload's flat buffer (bf16-valued grads x 65536), "
+                      f"AMP step = unscale + finite + two-pass fp64 norm + clip 1.0 + AdamW, median of {steps} steps"}
+
+
+def cpu_xent_sample(rows: int, threads: int) -> dict:
+    from oracle import xent as oxent
+    from oracle.casts import round_to_bf16
+    from namitorch_b200 import workloads as W
+    logits, targets = W.xent_inputs(rows=rows, seed=0)
+    logits = round_to_bf16(logits)
+    per = max(1, rows // threads)
+    blocks = [(i, min(rows, i + per)) for i in range(0, rows, per)]
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        list(pool.map(lambda b: oxent.cross_entropy(logits[b[0]:b[1]], targets[b[0]:b[1]], reduction="sum"), blocks))
+    t = time.perf_counter() - t0
+    return {"value": rows / t, "unit": "rows/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} rows of [8192, 50257] bf16-valued logits, fwd+bwd, row blocks per thread"}
+
+
+# ---- GPU workloads ---------------------------------------------------------------------------
+def shape_for(name):
+    from namitorch_b200 import workloads as W
+    return {"1p3b": W.CONFIG_1P3B, "124m": W.CONFIG_124M, "small": W.CONFIG_SMALL}[name]
+
+
+def make_params(shape, device, seed=0):
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    params = []
+    for _, s in shape.shapes():
+        t = torch.empty(s, dtype=torch.float32, device=device)
+        t.normal_(0.0, 0.02, generator=gen)
+        params.append(torch.nn.Parameter(t))
+    return params
+
+
+def make_flat_grads(params, device, scale, seed=1):
+    """bf16 gradients N(0,1e-3) * scale as views of one flat buffer (64-element aligned)."""
+    import torch
+    from namitorch_b200.flat import FlatLayout
+    layout = FlatLayout.build([p.numel() for p in params])
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    flat = torch.empty(layout.total, dtype=torch.float32, device=device)
+    flat.normal_(0.0, 1e-3, generator=gen)
+    flat.mul_(scale)
+    flat_bf16 = flat.to(torch.bfloat16)
+    del flat
+    views = [flat_bf16[o:o + p.numel()].view(p.shape) for p, o in zip(params, layout.offsets)]
+    return flat_bf16, views
+
+
+def group_params(shape, params, wd=0.1):
+    decay, no_decay = shape.groups()
+    return [{"params": [params[i] for i in decay], "weight_decay": wd},
+            {"params": [params[i] for i in no_decay], "weight_decay": 0.0}]
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from namitorch_b200 import _native as N
+    from namitorch_b200 import GradScaler
+    from namitorch_b200.optim import AdamW, clip_grad_norm_
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    shape = shape_for(args.workload)
+    P = shape.numel()
+    init_scale = 65536.0
+
+    params = make_params(shape, device)
+    if world > 1:
+        from namitorch_b200.zero import ZeroAdamW
+        opt = ZeroAdamW(group_params(shape, params), lr=3e-4, betas=(0.9, 0.999), eps=1e-8,
+                        model_dtype=torch.bfloat16)
+        flat_grads = opt.flat_grads
+        with torch.no_grad():
+            gen = torch.Generator(device=device)
+            gen.manual_seed(1 + rank)
+            tmp = torch.empty(flat_grads.numel(), dtype=torch.float32, device=device)
+            tmp.normal_(0.0, 1e-3, generator=gen)
+            flat_grads.copy_(tmp.mul_(init_scale))
+            del tmp
+    else:
+        opt = AdamW(group_params(shape, params), lr=3e-4, betas=(0.9, 0.999), eps=1e-8, model_dtype=torch.bfloat16)
+        flat_grads, views = make_flat_grads(params, device, init_scale)
+        for p, g in zip(params, views):
+            p.grad = g
+    scaler = GradScaler(init_scale=init_scale, growth_factor=2.0, backoff_factor=0.5, growth_interval=2000)
+    loss = torch.ones((), device=device)
+    stream = torch.cuda.current_stream()
+    ev = []
+
+    def step(record=False):
+        scaler.scale(loss)
+        if record:
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            e[0].record(stream)
+        scaler.unscale_(opt)
+        clip_grad_norm_(params, 1.0)
+        if record:
+            e[1].record(stream)
+        scaler.step(opt)
+        if record:
+            e[2].record(stream)
+            ev.append(e)
+        scaler.update()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(device)
+    sampler = ClockSampler(f"GPU-{props.uuid}" if getattr(props, "uuid", None) else None) if rank == 0 else None
+    time.sleep(0.3)
+    launches0 = N.launch_count
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start.record(stream)
+    for _ in range(args.steps):
+        step(record=True)
+    end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches = N.launch_count - launches0
+    clocks = sampler.stop() if sampler else None
+    ms = start.elapsed_time(end) / args.steps
+    stats_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    update_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    breakdown = getattr(opt, "last_breakdown", None)
+    if world > 1:
+        t = torch.tensor([ms, update_ms, stats_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, update_ms, stats_ms = t.tolist()
+    peak, peak_kind = measured_peak()
+    shard = P / world
+    result = {
+        "metric": METRIC, "value": P / (ms / 1e3), "unit": "params/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"{shape.name} AdamW+AMP step (BASELINE config 3; fp32 master/moments, bf16 grads "
+                               "and model copy, GradScaler, clip_grad_norm_ 1.0, 2 param groups)",
+                   "params": P, "tensors": len(params), "parallelism": f"zero1-dp{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (30 B/param x 1.3B per step)", "grad_dtype": "bf16",
+                   "model_dtype": "bf16"},
+        "hbm_gbs_step": BYTES_STEP * shard / (ms / 1e3) / 1e9,
+        "kernels_ms": {"grad_stats": stats_ms, "adamw_mt_update": update_ms},
+        "roofline": {"bound": "hbm", "achieved": BYTES_UPDATE * shard / (update_ms / 1e3) / 1e9, "peak": peak,
+                     "unit": "GB/s", "frac": BYTES_UPDATE * shard / (update_ms / 1e3) / 1e9 / peak,
+                     "peak_source": peak_kind, "kernel": "adamw_mt",
+                     "algorithmic_bytes_per_launch": BYTES_UPDATE * shard,
+                     "traffic": committed_traffic("adamw_mt", args.workload)},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if breakdown:
+        result["zero1_breakdown_ms"] = breakdown
+
+    if not args.no_e2e:
+        result["e2e"] = e2e_ours(args, opt, scaler, params, flat_grads, loss, world)
+    if world > 1:
+        dist.barrier()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_amp_sample(args.cpu_sample, 3, os.cpu_count() or 1)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def e2e_ours(args, opt, scaler, params, flat_grads, loss, world):
+    """The same step with this step's gradients copied in from pinned host memory and the
+    result (norm, found_inf) read back, timed on the host clock."""
+    import torch
+    import torch.distributed as dist
+    from namitorch_b200 import _native as N
+    from namitorch_b200.optim import clip_grad_norm_
+    host = torch.empty(flat_grads.shape, dtype=flat_grads.dtype, pin_memory=True)
+    host.copy_(flat_grads)
+    out = torch.empty(2, dtype=torch.float64, pin_memory=True)
+    times = []
+    for i in range(args.e2e_steps + 1):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        flat_grads.copy_(host, non_blocking=True)
+        scaler.scale(loss)
+        found = scaler.unscale_(opt)
+        norm = clip_grad_norm_(params, 1.0)
+        scaler.step(opt)
+        scaler.update()
+        out[0].copy_(norm, non_blocking=True)
+        out[1].copy_(found._tensor, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        if i:
+            times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    if world > 1:
+        tt = torch.tensor([t], dtype=torch.float64, device=flat_grads.device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    return {"value": sum(p.numel() for p in params) / t, "unit": "params/s",
+            "h2d_bytes_per_step": flat_grads.numel() * flat_grads.element_size(), "d2h_bytes_per_step": 16,
+            "ms_per_step": t * 1e3, "path": "pinned host grads -> H2D -> unscale_/clip_grad_norm_/step/update -> "
+                                            "D2H norm+found_inf (public API)"}
+
+
+def run_xent(args):
+    import torch
+    from namitorch_b200 import _native as N
+    from namitorch_b200 import workloads as W
+    from namitorch_b200.nn.functional import softmax_cross_entropy
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    rows, classes = W.XENT_ROWS, W.XENT_CLASSES
+    x = torch.empty(rows, classes, dtype=torch.float32, device=device).normal_(0, 2.0, generator=gen).to(torch.bfloat16)
+    t = torch.randint(0, classes, (rows,), device=device, generator=gen)
+    for _ in range(args.warmup):
+        softmax_cross_entropy(x, t, validate=False)
+    torch.cuda.synchronize()
+    launches0 = N.launch_count
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        loss, dl = softmax_cross_entropy(x, t, validate=False)
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    peak, kind = measured_peak()
+    nbytes = rows * classes * 4 + rows * 8
+    result = {"metric": "fused softmax-CE fwd+bwd rows/s", "value": rows / (ms / 1e3), "unit": "rows/s",
+              "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+              "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+              "config": {"workload": "LM-head logits [8192, 50257] bf16 N(0,2), int64 targets (BASELINE config 4)",
+                         "l2": "inputs larger than L2 (823 MB logits + 823 MB dlogits)"},
+              "roofline": {"bound": "hbm", "achieved": nbytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                           "frac": nbytes / (ms / 1e3) / 1e9 / peak, "peak_source": kind,
+                           "traffic": committed_traffic("xent", "xent")},
+              "gpu_launches": N.launch_count - launches0}
+    if not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_xent_sample(256, os.cpu_count() or 1)
+    print(json.dumps(result), flush=True)
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    if args.workload == "xent":
+        times = []
+        for i in range(args.warmup + args.steps):
+            base = cpu_xent_sample(128, threads)
+            if i >= args.warmup:
+                times.append(base["value"])
+        value = statistics.median(times)
+        base["value"] = value
+        line = {"impl": "reference", "metric": "fused softmax-CE fwd+bwd rows/s", "value": value, "unit": "rows/s",
+                "higher_is_better": True}
+    else:
+        n = min(args.cpu_sample, 1 << 24)
+        base = cpu_amp_sample(n, args.warmup + args.steps, threads)
+        value = base["value"]
+        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "params/s", "higher_is_better": True}
+    line.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                 "config": {"workload": args.workload, "sample": base["sample"]},
+                 "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                 "e2e": {"value": value, "unit": line["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                 "dtype": "f32", "data": "synthetic", "scaling": "strong", "vs_baseline": None})
+    print(json.dumps(line), flush=True)
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    if args.workload == "xent":
+        run_xent(args)
+        return
+    run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -152,7 +152,8 @@ typedef struct nt_adamw_mt_args {
   int64_t num_chunks;             /* total chunks over all segments */
   int32_t* steps;                 /* device step counters, one per slot (state["step"]) */
   const float* corrections;       /* device [rows][capacity][2]: f32(1-beta1^t), f32(1-beta2^t) */
-  int32_t correction_capacity;    /* t must stay < capacity */
+  int32_t correction_capacity;    /* t >= capacity reads row capacity-1, so the caller keeps t below
+                                     capacity until that row holds (1.0f, 1.0f) in every group */
   const float* scale;             /* device GradScaler scale or NULL: gradients are divided by it */
   const nt_stats* stats;     /* device stats or NULL */
   int32_t skip_nonfinite;         /* skip the whole step when stats->found_inf != 0 (amp.py:334-341) */

@@ -1,0 +1,194 @@
+"""ctypes binding of ``libnamitorch_b200.so`` (declared in include/namitorch_b200.h).
+
+This module is the only place that touches the C ABI. It mirrors the header's structs,
+maps status codes to the reference's exception classes and passes CUDA streams as raw
+handles. There is no fallback: if the library cannot be loaded, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+from pathlib import Path
+
+from .errors import NamiTorchCUDAOutOfMemoryError, NativeLibraryError
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libnamitorch_b200.so"
+
+NT_OK, NT_EINVAL, NT_ECUDA, NT_ENOMEM, NT_EUNSUPPORTED = 0, 1, 2, 3, 4
+NT_F32, NT_F16, NT_BF16 = 0, 1, 2
+NT_REDUCTION_NONE, NT_REDUCTION_MEAN, NT_REDUCTION_SUM = 0, 1, 2
+NT_DECAY_NONE, NT_DECAY_DECOUPLED, NT_DECAY_COUPLED = 0, 1, 2
+NT_MAX_GROUPS = 32
+NT_MAX_FOUND_INF = 16
+ABI_VERSION = 1
+
+
+class Segment(C.Structure):
+    _fields_ = [("grad", C.c_void_p), ("offset", C.c_int64), ("count", C.c_int64), ("chunk_begin", C.c_int64),
+                ("group", C.c_int32), ("step_slot", C.c_int32)]
+
+
+class AdamWGroup(C.Structure):
+    _fields_ = [("lr", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float), ("one_minus_beta1", C.c_float),
+                ("one_minus_beta2", C.c_float), ("eps", C.c_float), ("weight_decay", C.c_float),
+                ("decay_factor", C.c_float), ("maximize", C.c_int32), ("decay_mode", C.c_int32),
+                ("update_parameter", C.c_int32), ("correction_row", C.c_int32)]
+
+
+class Stats(C.Structure):
+    _fields_ = [("sumsq", C.c_double), ("nonfinite", C.c_double), ("nan", C.c_double), ("maxabs", C.c_double),
+                ("powsum", C.c_double), ("norm", C.c_double), ("found_inf", C.c_double), ("error", C.c_double)]
+
+
+STATS_FIELDS = [name for name, _ in Stats._fields_]
+STATS_DOUBLES = len(STATS_FIELDS)
+
+
+class AdamWMtArgs(C.Structure):
+    _fields_ = [("param", C.c_void_p), ("exp_avg", C.c_void_p), ("exp_avg_sq", C.c_void_p),
+                ("model_copy", C.c_void_p), ("model_dtype", C.c_int32), ("grad_dtype", C.c_int32),
+                ("segments", C.c_void_p), ("num_segments", C.c_int32), ("chunk_elems", C.c_int32),
+                ("num_chunks", C.c_int64), ("steps", C.c_void_p), ("corrections", C.c_void_p),
+                ("correction_capacity", C.c_int32), ("scale", C.c_void_p), ("stats", C.c_void_p),
+                ("skip_nonfinite", C.c_int32), ("clip", C.c_int32), ("max_norm", C.c_double),
+                ("workspace", C.c_void_p), ("error", C.c_void_p), ("groups", C.POINTER(AdamWGroup)),
+                ("num_groups", C.c_int32)]
+
+
+class Span(C.Structure):
+    _fields_ = [("ptr", C.c_void_p), ("count", C.c_int64), ("chunk_begin", C.c_int64)]
+
+
+class GradStatsArgs(C.Structure):
+    _fields_ = [("spans", C.c_void_p), ("num_spans", C.c_int32), ("chunk_elems", C.c_int32),
+                ("num_chunks", C.c_int64), ("dtype", C.c_int32), ("scale", C.c_void_p), ("pass_", C.c_int32),
+                ("norm_type", C.c_double), ("finalize", C.c_int32), ("stats", C.c_void_p),
+                ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
+
+
+class XentInfo(C.Structure):
+    _fields_ = [("denominator", C.c_double), ("weight_sum", C.c_double), ("loss_sum", C.c_double),
+                ("n_valid", C.c_double), ("bad_targets", C.c_double), ("error", C.c_double),
+                ("reserved0", C.c_double), ("reserved1", C.c_double)]
+
+
+XENT_INFO_FIELDS = [name for name, _ in XentInfo._fields_]
+
+
+class XentArgs(C.Structure):
+    _fields_ = [("logits", C.c_void_p), ("dtype", C.c_int32), ("rows", C.c_int64), ("classes", C.c_int64),
+                ("targets", C.c_void_p), ("ignore_index", C.c_int64), ("class_weight", C.c_void_p),
+                ("label_smoothing", C.c_float), ("reduction", C.c_int32), ("dlogits", C.c_void_p),
+                ("loss", C.c_void_p), ("row_loss", C.c_void_p), ("info", C.c_void_p), ("workspace", C.c_void_p),
+                ("workspace_bytes", C.c_size_t)]
+
+
+# name -> (restype, argtypes). Every symbol of include/namitorch_b200.h.
+SIGNATURES: dict[str, tuple] = {
+    "nt_abi_version": (C.c_int, []),
+    "nt_last_error": (C.c_char_p, []),
+    "nt_device_init": (C.c_int, [C.c_int]),
+    "nt_sm_count": (C.c_int, [C.POINTER(C.c_int)]),
+    "nt_malloc": (C.c_int, [C.POINTER(C.c_void_p), C.c_size_t]),
+    "nt_free": (C.c_int, [C.c_void_p]),
+    "nt_mem_info": (C.c_int, [C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
+    "nt_memset_async": (C.c_int, [C.c_void_p, C.c_int, C.c_size_t, C.c_void_p]),
+    "nt_memcpy_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "nt_memcpy_sync": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    "nt_stream_synchronize": (C.c_int, [C.c_void_p]),
+    "nt_cast": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int64, C.c_void_p]),
+    "nt_adamw_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_float), C.c_int,
+                               C.c_int, C.c_uint64, C.c_void_p]),
+    "nt_adamw_workspace_size": (C.c_size_t, []),
+    "nt_adamw_mt": (C.c_int, [C.POINTER(AdamWMtArgs), C.c_void_p]),
+    "nt_grad_stats_workspace_size": (C.c_size_t, []),
+    "nt_grad_stats": (C.c_int, [C.POINTER(GradStatsArgs), C.c_void_p]),
+    "nt_grad_stats_finalize": (C.c_int, [C.c_void_p, C.c_double, C.c_void_p]),
+    "nt_grad_transform": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_int32, C.c_void_p,
+                                    C.c_void_p, C.c_int32, C.c_double, C.c_void_p]),
+    "nt_grad_clip_value": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_int32, C.c_double,
+                                     C.c_void_p]),
+    "nt_scaler_update": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p), C.c_int32, C.c_double,
+                                   C.c_double, C.c_int32, C.c_void_p]),
+    "nt_xent_workspace_size": (C.c_size_t, []),
+    "nt_softmax_xent": (C.c_int, [C.POINTER(XentArgs), C.c_void_p]),
+    "nt_xent_backward_scale": (C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_int64, C.c_void_p, C.c_int32,
+                                         C.c_void_p]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load(path: str | os.PathLike | None = None):
+    """Loads the shared library once and binds every declared symbol."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        target = Path(path) if path is not None else LIB_PATH
+        if not target.exists():
+            raise NativeLibraryError(
+                f"{target} does not exist: build it with `python -m namitorch_b200._build` "
+                "(namitorch_b200 has no CPU or Python fallback for its CUDA kernels).")
+        try:
+            lib = C.CDLL(str(target))
+        except OSError as error:
+            raise NativeLibraryError(f"cannot load {target}: {error}") from error
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        if lib.nt_abi_version() != ABI_VERSION:
+            raise NativeLibraryError(f"{target} has ABI {lib.nt_abi_version()}, expected {ABI_VERSION}")
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    return (load().nt_last_error() or b"").decode("utf-8", "replace")
+
+
+def check(status: int, what: str = "") -> None:
+    """Raises the exception class the reference uses for this kind of failure."""
+    if status == NT_OK:
+        return
+    message = last_error() or what
+    if status == NT_EINVAL:
+        raise ValueError(message)
+    if status == NT_ENOMEM:
+        raise NamiTorchCUDAOutOfMemoryError.from_message(message)
+    if status == NT_EUNSUPPORTED:
+        raise RuntimeError(message)
+    raise RuntimeError(f"CUDA error in {what or 'namitorch_b200'}: {message}")
+
+
+# Kernel launches issued per successful call of each launching entry point (for the
+# benchmark's launch count; the statistics entry point launches one kernel per call).
+LAUNCHES_PER_CALL = {"nt_adamw_f32": 1, "nt_adamw_mt": 1, "nt_grad_stats": 1, "nt_grad_stats_finalize": 1,
+                     "nt_grad_transform": 1, "nt_grad_clip_value": 1, "nt_scaler_update": 1,
+                     "nt_softmax_xent": 2, "nt_xent_backward_scale": 1, "nt_cast": 1}
+launch_count = 0
+
+
+def call(name: str, *args) -> None:
+    global launch_count
+    check(getattr(load(), name)(*args), name)
+    launch_count += LAUNCHES_PER_CALL.get(name, 0)
+
+
+def stream_handle(stream=None) -> int:
+    """Raw cudaStream_t of a torch stream (default: the current stream of the current device)."""
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return int(stream.cuda_stream)
+
+
+def dtype_code(dtype) -> int:
+    import torch
+    codes = {torch.float32: NT_F32, torch.float16: NT_F16, torch.bfloat16: NT_BF16}
+    if dtype not in codes:
+        raise TypeError(f"namitorch_b200 kernels support float32, float16 and bfloat16, got {dtype}.")
+    return codes[dtype]

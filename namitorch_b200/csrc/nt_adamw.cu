@@ -184,11 +184,14 @@ __global__ void __launch_bounds__(256) adamw_mt_kernel(const __grid_constant__ M
     const nt_segment seg = P.segs[s];
     const nt_adamw_group& gr = P.groups[seg.group];
     const int t = P.steps[seg.step_slot] + 1;
-    if (t <= 0 || t >= P.cap) {
+    if (t <= 0) {
       if (threadIdx.x == 0 && P.error) atomicOr(P.error, 1);
       continue;
     }
-    const float2 corr = P.corr[(int64_t)gr.correction_row * P.cap + t];
+    // Steps past the table use its last row: the host only lets that happen once every
+    // row has saturated at exactly 1.0f, where f32(1 - beta^t) stays for all larger t.
+    const int ti = t < P.cap ? t : P.cap - 1;
+    const float2 corr = P.corr[(int64_t)gr.correction_row * P.cap + ti];
     Coef c;
     c.lr = gr.lr; c.b1 = gr.beta1; c.b2 = gr.beta2; c.c1 = gr.one_minus_beta1; c.c2 = gr.one_minus_beta2;
     c.eps = gr.eps; c.wd = gr.weight_decay; c.decay = gr.decay_factor; c.corr1 = corr.x; c.corr2 = corr.y;

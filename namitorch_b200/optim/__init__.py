@@ -1,0 +1,7 @@
+"""Optimizers and gradient clipping of the hot path (namitorch.optim API)."""
+from .adam import Adam, AdamW
+from .clip_grad import clip_grad_norm_, clip_grad_value_, defer_gradient_transforms, get_grad_norm
+from .optimizer import Optimizer
+
+__all__ = ["Optimizer", "Adam", "AdamW", "clip_grad_norm_", "clip_grad_value_", "get_grad_norm",
+           "defer_gradient_transforms"]

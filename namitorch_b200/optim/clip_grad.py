@@ -1,0 +1,170 @@
+"""Gradient-norm and gradient-value clipping (namitorch/optim/clip_grad.py:12-124).
+
+``clip_grad_norm_`` keeps the reference's signature, validation and return value (a
+float64 0-d tensor holding the pre-clip total norm), computed on the device by one
+reduction kernel. When the parameters are exactly those (with gradients) of a
+namitorch_b200 Adam/AdamW, the multiply by ``max_norm / (norm + 1e-6)`` is deferred into
+that optimizer's next update, which reads the gradients anyway; otherwise the gradients
+are rewritten in place, as the reference does. ``norm.item()`` or
+``error_if_nonfinite=True`` synchronise with the device; nothing else does.
+"""
+from __future__ import annotations
+
+import math
+from numbers import Real
+
+import numpy as np
+import torch
+
+from .. import _native as N
+from ..flat import grad_stats_for, launch_transform
+from .adam import _owner_of
+
+_LAZY = True
+
+
+def defer_gradient_transforms(mode: bool) -> None:
+    """Whether clip_grad_norm_ / GradScaler.unscale_ may fold their factors into the next fused
+    update instead of rewriting gradient storage (default True)."""
+    global _LAZY
+    if type(mode) is not bool:
+        raise TypeError("defer_gradient_transforms mode must be a Python bool.")
+    _LAZY = mode
+
+
+def deferring_gradient_transforms() -> bool:
+    return _LAZY
+
+
+def _nonnegative(value: object, name: str) -> float:
+    """namitorch/optim/clip_grad.py:12-21."""
+    if isinstance(value, (bool, np.bool_)) or not isinstance(value, Real):
+        raise TypeError(f"{name} must be a finite nonnegative real scalar.")
+    try:
+        value = float(value)
+    except OverflowError:
+        raise ValueError(f"{name} must be finite.") from None
+    if not math.isfinite(value) or value < 0:
+        raise ValueError(f"{name} must be finite and nonnegative.")
+    return value
+
+
+def _norm_type(value: object) -> float:
+    """namitorch/optim/clip_grad.py:24-33."""
+    if isinstance(value, (bool, np.bool_)) or not isinstance(value, Real):
+        raise TypeError("norm_type must be a positive real scalar or positive infinity.")
+    try:
+        value = float(value)
+    except OverflowError:
+        raise ValueError("norm_type is outside the supported range.") from None
+    if math.isnan(value) or value <= 0:
+        raise ValueError("norm_type must be positive or positive infinity.")
+    return value
+
+
+def _parameters_and_gradients(parameters) -> tuple[list[torch.Tensor], list[torch.Tensor]]:
+    """namitorch/optim/clip_grad.py:36-60 (gradients de-duplicated by identity)."""
+    if isinstance(parameters, torch.Tensor):
+        parameters = (parameters,)
+    if isinstance(parameters, (dict, str, bytes, set, frozenset)):
+        raise TypeError("parameters must be a Tensor or an ordered iterable of Tensors.")
+    try:
+        parameters = iter(parameters)
+    except TypeError:
+        raise TypeError("parameters must be a Tensor or an ordered iterable of Tensors.") from None
+    params, gradients = [], []
+    seen = set()
+    for parameter in parameters:
+        if not isinstance(parameter, torch.Tensor):
+            raise TypeError("parameters must contain only NamiTorch Tensors.")
+        gradient = parameter.grad
+        if gradient is None or id(gradient) in seen:
+            continue
+        if not isinstance(gradient, torch.Tensor) or not gradient.dtype.is_floating_point:
+            raise TypeError("Gradients must be floating NamiTorch Tensors.")
+        if gradient.shape != parameter.shape:
+            raise ValueError(f"Gradient shape {tuple(gradient.shape)} does not match parameter shape "
+                             f"{tuple(parameter.shape)}.")
+        if gradient.device != parameter.device:
+            raise RuntimeError(f"Operands are on different devices: {parameter.device}, {gradient.device}; "
+                               "use an explicit .to() transfer.")
+        seen.add(id(gradient))
+        params.append(parameter)
+        gradients.append(gradient)
+    devices = {g.device for g in gradients}
+    if len(devices) > 1:
+        raise RuntimeError(f"Operands are on different devices: {', '.join(map(str, devices))}; "
+                           "use an explicit .to() transfer.")
+    if gradients and gradients[0].device.type != "cuda":
+        raise RuntimeError("namitorch_b200 computes gradient norms on CUDA devices only.")
+    return params, gradients
+
+
+def _sole_owner(params: list[torch.Tensor]):
+    """The optimizer whose gradients are exactly these parameters' gradients, if any."""
+    if not params:
+        return None
+    owner = _owner_of(params[0])
+    if owner is None or any(_owner_of(p) is not owner for p in params):
+        return None
+    entries = owner._entries()
+    if {id(p) for _, p, _ in entries} != {id(p) for p in params}:
+        return None
+    return owner
+
+
+def _pending_owners(params: list[torch.Tensor]):
+    owners = {}
+    for p in params:
+        o = _owner_of(p)
+        if o is not None and o._amp is not None:
+            owners[id(o)] = o
+    return list(owners.values())
+
+
+def get_grad_norm(parameters, norm_type: float = 2) -> torch.Tensor:
+    """namitorch/optim/clip_grad.py:86-88."""
+    order = _norm_type(norm_type)
+    params, gradients = _parameters_and_gradients(parameters)
+    for owner in _pending_owners(params):
+        owner._materialize_pending()
+    stats = grad_stats_for(gradients, norm_type=order)
+    return stats[N.STATS_FIELDS.index("norm")]
+
+
+def clip_grad_norm_(parameters, max_norm: float, norm_type: float = 2, error_if_nonfinite: bool = False):
+    """namitorch/optim/clip_grad.py:96-112."""
+    maximum = _nonnegative(max_norm, "max_norm")
+    order = _norm_type(norm_type)
+    if type(error_if_nonfinite) is not bool:
+        raise TypeError("error_if_nonfinite must be a Python bool.")
+    params, gradients = _parameters_and_gradients(parameters)
+    norm_index = N.STATS_FIELDS.index("norm")
+
+    def check(stats):
+        if error_if_nonfinite:
+            value = float(stats[norm_index].item())
+            if not math.isfinite(value):
+                raise RuntimeError(f"Cannot clip gradients with nonfinite total norm {value}.")
+
+    owner = _sole_owner(params) if _LAZY else None
+    stats = owner._lazy_clip(maximum, order, check) if owner is not None else None
+    if stats is None:
+        for o in _pending_owners(params):
+            o._materialize_pending()
+        stats = grad_stats_for(gradients, norm_type=order)
+        check(stats)
+        launch_transform(gradients, stats=stats, max_norm=maximum)
+    return stats[norm_index]
+
+
+def clip_grad_value_(parameters, clip_value: float) -> None:
+    """namitorch/optim/clip_grad.py:115-121."""
+    bound = _nonnegative(clip_value, "clip_value")
+    params, gradients = _parameters_and_gradients(parameters)
+    for owner in _pending_owners(params):
+        owner._materialize_pending()
+    launch_transform(gradients, clip_value=bound)
+
+
+__all__ = ["get_grad_norm", "clip_grad_norm_", "clip_grad_value_", "defer_gradient_transforms"]
