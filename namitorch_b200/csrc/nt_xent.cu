@@ -126,25 +126,10 @@ __device__ __forceinline__ uint4 pack16(const float* v) {
   return raw;
 }
 
-// Per-row constants of the gradient formula.
-struct RowGrad {
-  int mode;        // 0: zero row, 1: NaN row, 2: regular
-  float invS;      // 1 / S
-  float shift;     // M * log2(e)
-  float a;         // coefficient of p_c
-  float b;         // subtracted at c == t
-  float g;         // coefficient of -w_c (or the constant without weights)
-  int64_t t;
-};
-
-__device__ __forceinline__ float grad_value(float x, int64_t c, const RowGrad& r, const float* weight) {
-  if (r.mode == 0) return 0.0f;
-  if (r.mode == 1) return __int_as_float(0x7fc00000);
-  const float p = ex2(fmaf(x, kLog2e, -r.shift)) * r.invS;
-  float d = r.a * p;
-  if (c == r.t) d -= r.b;
-  if (r.g != 0.0f) d -= weight ? r.g * weight[c] : r.g;
-  return d;
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 
 __global__ void __launch_bounds__(kPrepThreads) xent_prepare_kernel(const __grid_constant__ XentParams P) {
@@ -176,7 +161,25 @@ __global__ void __launch_bounds__(kPrepThreads) xent_prepare_kernel(const __grid
   }
 }
 
+// One 16-byte vector k of the row (EPV elements starting at element (16k - head) / ES).
 template <int DT, bool STAGED>
+__device__ __forceinline__ void row_vector(const unsigned char* stage, const void* logits, int64_t row_base,
+                                           int k, int head, int V, float* x) {
+  constexpr int ES = DT == NT_F32 ? 4 : 2;
+  constexpr int EPV = 16 / ES;
+  if (STAGED) {
+    unpack16<DT>(reinterpret_cast<const uint4*>(stage)[k], x);
+  } else {
+    const int j0 = (k * 16 - head) / ES;
+#pragma unroll
+    for (int q = 0; q < EPV; ++q) {
+      const int j = j0 + q;
+      x[q] = (j >= 0 && j < V) ? load1<DT>(logits, row_base + j) : -INFINITY;
+    }
+  }
+}
+
+template <int DT, bool STAGED, bool WEIGHTED>
 __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constant__ XentParams P) {
   extern __shared__ __align__(128) unsigned char stage[];
   __shared__ uint64_t bar;
@@ -187,7 +190,7 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
 
   constexpr int ES = DT == NT_F32 ? 4 : 2;
   constexpr int EPV = 16 / ES;  // elements per 16-byte vector
-  const int64_t V = P.classes;
+  const int V = (int)P.classes;
   const nt_xent_info* info = P.info;
   const bool mean = P.reduction == NT_REDUCTION_MEAN;
   const double D = mean ? info->denominator : 1.0;
@@ -208,17 +211,20 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
   uint32_t phase = 0;
 
   for (int64_t row = blockIdx.x; row < P.rows; row += gridDim.x) {
-    const int64_t t = P.targets[row];
-    const bool valid = t != P.ignore && t >= 0 && t < V;
-    const char* row_ptr = static_cast<const char*>(P.logits) + row * V * ES;
-    const uintptr_t start = reinterpret_cast<uintptr_t>(row_ptr);
+    const int64_t t64 = P.targets[row];
+    const bool valid = t64 != P.ignore && t64 >= 0 && t64 < V;
+    const int t = valid ? (int)t64 : -1;
+    const int64_t row_base = row * (int64_t)V;
+    const uintptr_t start = reinterpret_cast<uintptr_t>(P.logits) + (uintptr_t)(row_base * ES);
     const uintptr_t a = start & ~(uintptr_t)15;
     const int head = (int)(start - a);
-    const int64_t span = head + V * ES;                  // bytes from a to the row end
-    const int64_t nvec = (span + 15) / 16;
+    const int span = head + V * ES;           // bytes from a to the row end
+    const int nvec = (span + 15) >> 4;
+    const int full_lo = head ? 1 : 0;         // vectors [full_lo, full_hi) hold only row elements
+    const int full_hi = span >> 4;
 
     if (STAGED) {
-      int64_t bulk = nvec * 16;
+      int64_t bulk = (int64_t)nvec * 16;
       const uintptr_t limit = P.tensor_end & ~(uintptr_t)15;
       if ((int64_t)(limit - a) < bulk) bulk = (int64_t)(limit - a);
       if (threadIdx.x == 0) {
@@ -227,7 +233,7 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
         if (bulk > 0) bulk_g2s(stage, reinterpret_cast<const void*>(a), (uint32_t)bulk, &bar);
       }
       // Bytes between the last 16-byte boundary of the tensor and its end.
-      for (int64_t k = bulk + threadIdx.x; k < span; k += blockDim.x)
+      for (int k = (int)bulk + threadIdx.x; k < span; k += blockDim.x)
         stage[k] = *reinterpret_cast<const unsigned char*>(a + k);
       if (threadIdx.x == 0) {
         const uint64_t t0 = globaltimer();
@@ -243,124 +249,123 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
       }
     }
 
-    auto vec_at = [&](int64_t k, float* x) {
-      if (STAGED) {
-        unpack16<DT>(reinterpret_cast<const uint4*>(stage)[k], x);
-      } else {
-        const int64_t j0 = (k * 16 - head) / ES;
-#pragma unroll
-        for (int q = 0; q < EPV; ++q) {
-          const int64_t j = j0 + q;
-          x[q] = (j >= 0 && j < V) ? load1<DT>(P.logits, row * V + j) : 0.0f;
-        }
-      }
-    };
-
-    // Pass 1: max (NaN tracked separately) and, for smoothing, sum_c w_c x_c.
-    float mx = -INFINITY;
+    // Pass A: online max / sum of exp per thread (NaN tracked through max.NaN) and, for
+    // label smoothing, sum_c w_c x_c.
+    float m = -INFINITY, s = 0.0f;
     float nan_seen = 0.0f;
     double swx = 0.0;
-    for (int64_t k = threadIdx.x; k < nvec; k += blockDim.x) {
+    for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
       float x[EPV];
-      vec_at(k, x);
-      const int64_t j0 = (k * 16 - head) / ES;
+      row_vector<DT, STAGED>(stage, P.logits, row_base, k, head, V, x);
+      const int j0 = (k * 16 - head) / ES;
+      if (STAGED && (k < full_lo || k >= full_hi)) {
 #pragma unroll
-      for (int q = 0; q < EPV; ++q) {
-        const int64_t j = j0 + q;
-        if (j < 0 || j >= V) continue;
-        if (isnan(x[q])) nan_seen = 1.0f;
-        mx = fmaxf(mx, x[q]);
-        if (smooth) swx += P.weight ? (double)P.weight[j] * (double)x[q] : (double)x[q];
+        for (int q = 0; q < EPV; ++q)
+          if (j0 + q < 0 || j0 + q >= V) x[q] = -INFINITY;
       }
-    }
-    mx = block_reduce(mx, red_f, MaxOp(), -INFINITY);
-    nan_seen = block_reduce(nan_seen, red_f, MaxOp(), 0.0f);
-    if (smooth) swx = block_reduce(swx, red_d, SumOp(), 0.0);
-    const bool bad_row = nan_seen != 0.0f || mx == INFINITY;
-    const bool neg_row = !bad_row && mx == -INFINITY;
-
-    // Pass 2: S = sum exp(x - M).
-    const float shift = mx * kLog2e;
-    float s = 0.0f;
-    if (!bad_row && !neg_row) {
-      for (int64_t k = threadIdx.x; k < nvec; k += blockDim.x) {
-        float x[EPV];
-        vec_at(k, x);
-        const int64_t j0 = (k * 16 - head) / ES;
+      float vmax = x[0];
+#pragma unroll
+      for (int q = 1; q < EPV; ++q) vmax = max_nan(vmax, x[q]);
+      if (vmax != vmax) nan_seen = 1.0f;
+      if (vmax > m) {
+        s = s * ex2((m - vmax) * kLog2e);
+        m = vmax;
+      }
+      if (m > -INFINITY) {
+        const float sh = m * kLog2e;
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) s += ex2(fmaf(x[q], kLog2e, -sh));
+      }
+      if (smooth) {
 #pragma unroll
         for (int q = 0; q < EPV; ++q) {
-          const int64_t j = j0 + q;
-          if (j >= 0 && j < V) s += ex2(fmaf(x[q], kLog2e, -shift));
+          const int j = j0 + q;
+          if (j >= 0 && j < V) swx += WEIGHTED ? (double)P.weight[j] * (double)x[q] : (double)x[q];
         }
       }
     }
-    s = block_reduce(s, red_f, SumOp(), 0.0f);
+    const float M = block_reduce(m, red_f, MaxOp(), -INFINITY);
+    nan_seen = block_reduce(nan_seen, red_f, MaxOp(), 0.0f);
+    const float part = (m > -INFINITY && M < INFINITY) ? s * ex2((m - M) * kLog2e) : 0.0f;
+    const float S = block_reduce(part, red_f, SumOp(), 0.0f);
+    if (smooth) swx = block_reduce(swx, red_d, SumOp(), 0.0);
+    const bool bad_row = nan_seen != 0.0f || M == INFINITY;
+    const bool neg_row = !bad_row && M == -INFINITY;
 
-    // Row loss and gradient constants.
-    RowGrad rg;
-    rg.t = valid ? t : -1;
-    rg.invS = 1.0f / s;
-    rg.shift = shift;
-    const float wt = valid ? (P.weight ? P.weight[t] : 1.0f) : 0.0f;
-    float loss_i = 0.0f;
-    if (!valid || zero_all) {
-      rg.mode = 0;
-    } else if (bad_row) {
-      rg.mode = 1;
-      loss_i = __int_as_float(0x7fc00000);
-    } else if (neg_row) {
-      rg.mode = 0;
-      loss_i = INFINITY;
-    } else {
-      rg.mode = 2;
-      float xt;
-      if (STAGED) {
-        const int64_t off = head + t * ES;
-        if constexpr (DT == NT_F32) xt = *reinterpret_cast<const float*>(stage + off);
-        else if constexpr (DT == NT_BF16) xt = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(stage + off));
-        else xt = __half2float(*reinterpret_cast<const __half*>(stage + off));
+    // Row loss and the gradient coefficients: d_c = e_c * A - G_c, minus B at c == t.
+    const float wt = valid ? (WEIGHTED ? P.weight[t] : 1.0f) : 0.0f;
+    int mode = 0;  // 0: zero row, 1: NaN row, 2: regular
+    float loss_i = 0.0f, A = 0.0f, B = 0.0f, G = 0.0f;
+    if (valid && !zero_all) {
+      if (bad_row) {
+        mode = 1;
+        loss_i = __int_as_float(0x7fc00000);
+      } else if (neg_row) {
+        loss_i = INFINITY;
       } else {
-        xt = load1<DT>(P.logits, row * V + t);
-      }
-      const float lse = mx + logf(s);
-      const float base = -wt * (xt - lse);
-      if (smooth) {
-        const double sm = -(swx - (double)lse * W) / (double)V;
-        loss_i = (1.0f - e) * base + e * (float)sm;
-      } else {
-        loss_i = base;
-      }
-      if (P.weight) {
-        rg.a = ((1.0f - e) * wt + (float)((double)e * W / (double)V)) * inv_den;
-        rg.b = (1.0f - e) * wt * inv_den;
-        rg.g = smooth ? (float)((double)e / (double)V) * inv_den : 0.0f;
-      } else {
-        rg.a = inv_den;
-        rg.b = (1.0f - e) * inv_den;
-        rg.g = smooth ? (float)((double)e / (double)V) * inv_den : 0.0f;
+        mode = 2;
+        float xt;
+        if (STAGED) {
+          const int off = head + t * ES;
+          if constexpr (DT == NT_F32) xt = *reinterpret_cast<const float*>(stage + off);
+          else if constexpr (DT == NT_BF16) xt = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(stage + off));
+          else xt = __half2float(*reinterpret_cast<const __half*>(stage + off));
+        } else {
+          xt = load1<DT>(P.logits, row_base + t);
+        }
+        const float lse = M + logf(S);
+        const float base = -wt * (xt - lse);
+        if (smooth) {
+          const double sm = -(swx - (double)lse * W) / (double)V;
+          loss_i = (1.0f - e) * base + e * (float)sm;
+        } else {
+          loss_i = base;
+        }
+        const float invS = 1.0f / S;
+        const float a_coef = WEIGHTED ? ((1.0f - e) * wt + (float)((double)e * W / (double)V)) * inv_den : inv_den;
+        A = a_coef * invS;
+        B = (1.0f - e) * wt * inv_den;
+        G = smooth ? (float)((double)e / (double)V) * inv_den : 0.0f;
       }
     }
-    if (threadIdx.x == 0) P.row_loss[row] = valid ? (zero_all ? 0.0f : loss_i) : 0.0f;
+    if (threadIdx.x == 0) P.row_loss[row] = loss_i;
 
-    // Pass 3: gradient.
+    // Pass B: gradient.
     if (P.dl != nullptr) {
-      char* out_row = static_cast<char*>(P.dl) + row * V * ES;
-      const uintptr_t oa = reinterpret_cast<uintptr_t>(out_row) & ~(uintptr_t)15;
-      const int ohead = (int)(reinterpret_cast<uintptr_t>(out_row) - oa);
-      const bool same_phase = STAGED && ohead == head;
-      for (int64_t k = threadIdx.x; k < nvec; k += blockDim.x) {
-        float x[EPV], d[EPV];
-        vec_at(k, x);
-        const int64_t j0 = (k * 16 - head) / ES;
+      const uintptr_t out_start = reinterpret_cast<uintptr_t>(P.dl) + (uintptr_t)(row_base * ES);
+      const uintptr_t oa = out_start & ~(uintptr_t)15;
+      const bool vec_out = STAGED && (int)(out_start - oa) == head;
+      const float shM = M * kLog2e;
+      const int kt = valid ? ((head + t * ES) >> 4) : -1;
+      const int lane_t = valid ? (((head + t * ES) & 15) / ES) : 0;
+      const float nanv = __int_as_float(0x7fc00000);
+      for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
+        const int j0 = (k * 16 - head) / ES;
+        float d[EPV];
+        if (mode == 2) {
+          float x[EPV];
+          row_vector<DT, STAGED>(stage, P.logits, row_base, k, head, V, x);
 #pragma unroll
-        for (int q = 0; q < EPV; ++q) d[q] = grad_value(x[q], j0 + q, rg, P.weight);
-        if (same_phase && j0 >= 0 && j0 + EPV <= V) {
+          for (int q = 0; q < EPV; ++q) {
+            const float g = WEIGHTED ? G * ((j0 + q >= 0 && j0 + q < V) ? P.weight[j0 + q] : 0.0f) : G;
+            d[q] = fmaf(ex2(fmaf(x[q], kLog2e, -shM)), A, -g);
+          }
+          if (k == kt) {
+#pragma unroll
+            for (int q = 0; q < EPV; ++q)
+              if (q == lane_t) d[q] -= B;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < EPV; ++q) d[q] = mode == 1 ? nanv : 0.0f;
+        }
+        if (vec_out && k >= full_lo && k < full_hi) {
           __stcs(reinterpret_cast<uint4*>(oa + (uintptr_t)k * 16), pack16<DT>(d));
         } else {
 #pragma unroll
           for (int q = 0; q < EPV; ++q) {
-            const int64_t j = j0 + q;
-            if (j >= 0 && j < V) store1<DT>(P.dl, row * V + j, d[q]);
+            const int j = j0 + q;
+            if (j >= 0 && j < V) store1<DT>(P.dl, row_base + j, d[q]);
           }
         }
       }
@@ -394,7 +399,7 @@ __global__ void __launch_bounds__(256) xent_scale_kernel(void* dl, int64_t rows,
   }
 }
 
-template <int DT>
+template <int DT, bool WEIGHTED>
 static int launch_xent(const XentParams& P0, cudaStream_t stream) {
   XentParams P = P0;
   constexpr int ES = DT == NT_F32 ? 4 : 2;
@@ -405,15 +410,15 @@ static int launch_xent(const XentParams& P0, cudaStream_t stream) {
   const bool can_stage = P.staged && stage_bytes + 4096 <= (size_t)max_optin;
   int per_sm = 1;
   if (can_stage) {
-    cudaError_t err = cudaFuncSetAttribute(xent_kernel<DT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)stage_bytes);
+    cudaError_t err = cudaFuncSetAttribute(xent_kernel<DT, true, WEIGHTED>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)stage_bytes);
     if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(xent)");
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, xent_kernel<DT, true>, kXentThreads, stage_bytes) !=
-            cudaSuccess || per_sm < 1)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, xent_kernel<DT, true, WEIGHTED>, kXentThreads,
+                                                      stage_bytes) != cudaSuccess || per_sm < 1)
       per_sm = 1;
   } else {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, xent_kernel<DT, false>, kXentThreads, 0) != cudaSuccess ||
-        per_sm < 1)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, xent_kernel<DT, false, WEIGHTED>, kXentThreads, 0) !=
+            cudaSuccess || per_sm < 1)
       per_sm = 1;
   }
   int64_t grid = (int64_t)current_sm_count() * per_sm;
@@ -421,10 +426,15 @@ static int launch_xent(const XentParams& P0, cudaStream_t stream) {
   if (grid < 1) grid = 1;
   P.staged = can_stage;
   if (can_stage)
-    xent_kernel<DT, true><<<(unsigned)grid, kXentThreads, stage_bytes, stream>>>(P);
+    xent_kernel<DT, true, WEIGHTED><<<(unsigned)grid, kXentThreads, stage_bytes, stream>>>(P);
   else
-    xent_kernel<DT, false><<<(unsigned)grid, kXentThreads, 0, stream>>>(P);
+    xent_kernel<DT, false, WEIGHTED><<<(unsigned)grid, kXentThreads, 0, stream>>>(P);
   return launch_status("nt_softmax_xent launch");
+}
+
+template <int DT>
+static int launch_xent_dt(const XentParams& P, cudaStream_t stream) {
+  return P.weight ? launch_xent<DT, true>(P, stream) : launch_xent<DT, false>(P, stream);
 }
 
 }  // namespace nt
@@ -444,6 +454,10 @@ int nt_softmax_xent(const nt_xent_args* args, void* stream) {
     return NT_EINVAL;
   }
   if (dtype_size(a.dtype) == 0) { set_error("nt_softmax_xent: unsupported dtype %d", a.dtype); return NT_EUNSUPPORTED; }
+  if (a.classes > (int64_t)(INT32_MAX / 4 - 64)) {
+    set_error("nt_softmax_xent: at most %d classes per row", INT32_MAX / 4 - 64);
+    return NT_EUNSUPPORTED;
+  }
   if (a.reduction < NT_REDUCTION_NONE || a.reduction > NT_REDUCTION_SUM) {
     set_error("nt_softmax_xent: invalid reduction %d", a.reduction);
     return NT_EINVAL;
@@ -473,9 +487,9 @@ int nt_softmax_xent(const nt_xent_args* args, void* stream) {
   int rc = launch_status("nt_softmax_xent prepare launch");
   if (rc || a.rows == 0) return rc;
   switch (a.dtype) {
-    case NT_F32: return launch_xent<NT_F32>(P, s);
-    case NT_F16: return launch_xent<NT_F16>(P, s);
-    default: return launch_xent<NT_BF16>(P, s);
+    case NT_F32: return launch_xent_dt<NT_F32>(P, s);
+    case NT_F16: return launch_xent_dt<NT_F16>(P, s);
+    default: return launch_xent_dt<NT_BF16>(P, s);
   }
 }
 

@@ -90,6 +90,10 @@ class _FirstOrderAdam(Optimizer):
         self._amp: _AmpPending | None = None
         super().__init__(params, defaults)
         self.state = _StateView(self)
+        # The arenas are built now, not at the first step: the parameters must already be
+        # views of the model copy (in its dtype) when the first gradients are assigned.
+        if self._uses_engine():
+            self._ensure_engine()
 
     # ---- options (namitorch/optim/_common.py:83-88, adam.py:17-25, :52-56) -------------------
     def _prepare_options(self, options: dict, path: str) -> dict:

@@ -95,9 +95,12 @@ def _parameters_and_gradients(parameters) -> tuple[list[torch.Tensor], list[torc
     if len(devices) > 1:
         raise RuntimeError(f"Operands are on different devices: {', '.join(map(str, devices))}; "
                            "use an explicit .to() transfer.")
+    return params, gradients
+
+
+def _require_cuda(gradients: list[torch.Tensor]) -> None:
     if gradients and gradients[0].device.type != "cuda":
         raise RuntimeError("namitorch_b200 computes gradient norms on CUDA devices only.")
-    return params, gradients
 
 
 def _sole_owner(params: list[torch.Tensor]):
@@ -126,6 +129,7 @@ def get_grad_norm(parameters, norm_type: float = 2) -> torch.Tensor:
     """namitorch/optim/clip_grad.py:86-88."""
     order = _norm_type(norm_type)
     params, gradients = _parameters_and_gradients(parameters)
+    _require_cuda(gradients)
     for owner in _pending_owners(params):
         owner._materialize_pending()
     stats = grad_stats_for(gradients, norm_type=order)
@@ -150,6 +154,7 @@ def clip_grad_norm_(parameters, max_norm: float, norm_type: float = 2, error_if_
     owner = _sole_owner(params) if _LAZY else None
     stats = owner._lazy_clip(maximum, order, check) if owner is not None else None
     if stats is None:
+        _require_cuda(gradients)
         for o in _pending_owners(params):
             o._materialize_pending()
         stats = grad_stats_for(gradients, norm_type=order)
@@ -162,6 +167,7 @@ def clip_grad_value_(parameters, clip_value: float) -> None:
     """namitorch/optim/clip_grad.py:115-121."""
     bound = _nonnegative(clip_value, "clip_value")
     params, gradients = _parameters_and_gradients(parameters)
+    _require_cuda(gradients)
     for owner in _pending_owners(params):
         owner._materialize_pending()
     launch_transform(gradients, clip_value=bound)
