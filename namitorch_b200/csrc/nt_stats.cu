@@ -6,7 +6,8 @@
 
 namespace nt {
 
-constexpr int kStatsThreads = 512;
+constexpr int kStatsThreads = 256;
+constexpr int kUnroll = 4;  // 16-byte vectors in flight per thread
 constexpr int kStatsMaxBlocks = 1024;
 
 struct StatsPartial {
@@ -63,10 +64,13 @@ __device__ __forceinline__ void stats_accumulate(float u, int pass, double p, do
                                                  double& ss, double& ps, float& mx, unsigned& nf,
                                                  unsigned& nn) {
   if (pass == 0) {
-    if (isnan(u)) { ++nn; ++nf; return; }
-    mx = fmaxf(mx, fabsf(u));
-    if (isinf(u)) { ++nf; return; }
-    ss += (double)u * (double)u;
+    const float a = fabsf(u);
+    const bool finite = a <= 3.402823466e38f;  // false for +-inf and NaN
+    mx = fmaxf(mx, a);                           // fmaxf skips NaN
+    nf += finite ? 0u : 1u;
+    nn += (u != u) ? 1u : 0u;
+    const double d = finite ? (double)u : 0.0;
+    ss = fma(d, d, ss);                          // u*u is exact in double
   } else {
     if (!isfinite(u)) return;
     const double scaled = __ddiv_rn(fabs((double)u), maxabs);
@@ -96,14 +100,24 @@ __global__ void __launch_bounds__(kStatsThreads) grad_stats_kernel(const __grid_
     if (end > sp.count) end = sp.count;
     int64_t e = begin;
     if (((reinterpret_cast<uintptr_t>(static_cast<const char*>(sp.ptr) + begin * esize)) & 15u) == 0) {
-      const int64_t body_end = begin + ((end - begin) & ~(int64_t)7);
-      for (int64_t i = begin + (int64_t)threadIdx.x * 8; i < body_end; i += (int64_t)blockDim.x * 8) {
-        float x[8];
-        load8<DT>(sp.ptr, i, x);
+      const int64_t nv = (end - begin) >> 3;
+      // kUnroll independent 16-byte loads per thread before any arithmetic.
+      for (int64_t v0 = threadIdx.x; v0 < nv; v0 += (int64_t)blockDim.x * kUnroll) {
+        float x[kUnroll][8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) stats_accumulate<DT>(un(x[k]), P.pass, P.p, maxabs, ss, ps, mx, nf, nn);
+        for (int u = 0; u < kUnroll; ++u) {
+          const int64_t v = v0 + (int64_t)u * blockDim.x;
+          if (v < nv) load8<DT>(sp.ptr, begin + v * 8, x[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          if (v0 + (int64_t)u * blockDim.x < nv) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) stats_accumulate<DT>(un(x[u][k]), P.pass, P.p, maxabs, ss, ps, mx, nf, nn);
+          }
+        }
       }
-      e = body_end;
+      e = begin + nv * 8;
     }
     for (int64_t i = e + threadIdx.x; i < end; i += blockDim.x)
       stats_accumulate<DT>(un(load1<DT>(sp.ptr, i)), P.pass, P.p, maxabs, ss, ps, mx, nf, nn);

@@ -81,10 +81,11 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// 2^x on the SFU (approximate, subnormal results kept).
+// 2^x on the SFU. Results below 2^-126 flush to zero: a logit that far below the row max
+// contributes nothing to the sum and its gradient is below 2^-126 times the row scale.
 __device__ __forceinline__ float ex2(float x) {
   float y;
-  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
@@ -184,6 +185,7 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
   extern __shared__ __align__(128) unsigned char stage[];
   __shared__ uint64_t bar;
   __shared__ float red_f[kXentThreads / 32];
+  __shared__ float red_pair[kXentThreads / 32];
   __shared__ double red_d[kXentThreads / 32];
   __shared__ bool last;
   __shared__ int abort_flag;
@@ -249,10 +251,9 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
       }
     }
 
-    // Pass A: online max / sum of exp per thread (NaN tracked through max.NaN) and, for
-    // label smoothing, sum_c w_c x_c.
+    // Pass A: online max / sum of exp per thread. The running max propagates NaN
+    // (max.NaN.f32), so one value carries both; label smoothing also needs sum_c w_c x_c.
     float m = -INFINITY, s = 0.0f;
-    float nan_seen = 0.0f;
     double swx = 0.0;
     for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
       float x[EPV];
@@ -266,10 +267,10 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
       float vmax = x[0];
 #pragma unroll
       for (int q = 1; q < EPV; ++q) vmax = max_nan(vmax, x[q]);
-      if (vmax != vmax) nan_seen = 1.0f;
-      if (vmax > m) {
-        s = s * ex2((m - vmax) * kLog2e);
-        m = vmax;
+      const float mn = max_nan(m, vmax);
+      if (mn != m) {
+        s = m > -INFINITY ? s * ex2((m - mn) * kLog2e) : 0.0f;
+        m = mn;
       }
       if (m > -INFINITY) {
         const float sh = m * kLog2e;
@@ -284,12 +285,36 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
         }
       }
     }
-    const float M = block_reduce(m, red_f, MaxOp(), -INFINITY);
-    nan_seen = block_reduce(nan_seen, red_f, MaxOp(), 0.0f);
-    const float part = (m > -INFINITY && M < INFINITY) ? s * ex2((m - M) * kLog2e) : 0.0f;
-    const float S = block_reduce(part, red_f, SumOp(), 0.0f);
+    // One block-wide merge of the (max, sum) pairs.
+    {
+      const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+        const float mm = max_nan(m, m2);
+        s = mm > -INFINITY ? (m > -INFINITY ? s * ex2((m - mm) * kLog2e) : 0.0f) +
+                                 (m2 > -INFINITY ? s2 * ex2((m2 - mm) * kLog2e) : 0.0f)
+                           : 0.0f;
+        m = mm;
+      }
+      __syncthreads();
+      if (lane == 0) { red_f[warp] = m; red_pair[warp] = s; }
+      __syncthreads();
+      float M0 = -INFINITY;
+      for (int w = 0; w < nwarps; ++w) M0 = max_nan(M0, red_f[w]);
+      float S0 = 0.0f;
+      if (M0 > -INFINITY) {
+        for (int w = 0; w < nwarps; ++w)
+          if (red_f[w] > -INFINITY) S0 += red_pair[w] * ex2((red_f[w] - M0) * kLog2e);
+      }
+      m = M0;
+      s = S0;
+    }
+    const float M = m;
+    const float S = s;
     if (smooth) swx = block_reduce(swx, red_d, SumOp(), 0.0);
-    const bool bad_row = nan_seen != 0.0f || M == INFINITY;
+    const bool bad_row = M != M || M == INFINITY;
     const bool neg_row = !bad_row && M == -INFINITY;
 
     // Row loss and the gradient coefficients: d_c = e_c * A - G_c, minus B at c == t.

@@ -1,0 +1,123 @@
+"""ZeRO-1 on 2+ GPUs over NCCL: one process per GPU, GradScaler + clip_grad_norm_ + AdamW.
+
+The oracle receives the gradients as they come out of the reduce-scatter (gathered from
+every rank), so the comparison isolates the sharded update from the bf16 reduction
+rounding; the reduction itself is checked against a float32 sum within bf16 rounding.
+Skipped when fewer than two GPUs are visible.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out_path):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from namitorch_b200 import GradScaler, workloads as W
+        from namitorch_b200.optim import clip_grad_norm_
+        from namitorch_b200.zero import ZeroAdamW
+        from oracle.casts import round_to_bf16
+        shape = W.CONFIG_SMALL
+        params = [torch.nn.Parameter(torch.from_numpy(a).cuda()) for a in W.init_params(shape, seed=0)]
+        decay, no_decay = shape.groups()
+        groups = [{"params": [params[i] for i in decay], "weight_decay": 0.1},
+                  {"params": [params[i] for i in no_decay], "weight_decay": 0.0}]
+        opt = ZeroAdamW(groups, lr=3e-4, model_dtype=torch.bfloat16)
+        scaler = GradScaler(1024.0, growth_interval=2)
+        reduced, local, norms, stepped = [], [], [], []
+        for step in range(4):
+            opt.zero_grad()
+            grads = [round_to_bf16(g * np.float32(scaler.get_scale()))
+                     for g in W.outlier_grads(shape, seed=10 * step + rank)]
+            if step == 2 and rank == 1:
+                grads[5].reshape(-1)[3] = np.inf
+            for p, g in zip(params, grads):
+                p.grad.copy_(torch.from_numpy(g).to(torch.bfloat16))
+            local.append(opt.flat_grads.float().cpu().numpy())
+            opt._reduce()
+            full = torch.empty(opt.layout.total, dtype=torch.bfloat16, device="cuda")
+            dist.all_gather_into_tensor(full, opt.grad_shard)
+            reduced.append(full.float().cpu().numpy())
+            scaler.scale(torch.ones((), device="cuda"))
+            scaler.unscale_(opt)
+            norms.append(float(clip_grad_norm_(params, 1.0).item()))
+            stepped.append(bool(scaler.step(opt)))
+            scaler.update()
+        sd = opt.state_dict()
+        copies = [p.detach().float().cpu().numpy() for p in params]
+        all_local = [None] * world
+        dist.all_gather_object(all_local, local)
+        if rank == 0:
+            np.savez(out_path, norms=np.array(norms), stepped=np.array(stepped),
+                     offsets=np.array(opt.layout.offsets), reduced=np.stack(reduced),
+                     local=np.stack([np.stack(l) for l in all_local]),
+                     **{f"master{k}": st["master_param"].cpu().numpy() for k, st in sd["state"].items()},
+                     **{f"m{k}": st["exp_avg"].cpu().numpy() for k, st in sd["state"].items()},
+                     steps=np.array([st["step"] for _, st in sorted(sd["state"].items())]),
+                     **{f"copy{k}": c for k, c in enumerate(copies)}, scale=np.array(scaler.get_scale()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_zero1_nccl_matches_oracle(tmp_path):
+    if torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    import torch.multiprocessing as mp
+    from namitorch_b200 import workloads as W
+    from oracle import adamw as oadamw
+    from oracle import amp as oamp
+    from oracle.casts import f32_to_bf16_bits
+    out_path = tmp_path / "zero.npz"
+    mp.spawn(_worker, args=(WORLD, _free_port(), str(out_path)), nprocs=WORLD, join=True)
+    out = np.load(out_path)
+    shape = W.CONFIG_SMALL
+    offsets = out["offsets"]
+    numels = [int(np.prod(s)) for _, s in shape.shapes()]
+    # The reduce-scatter (average) agrees with a float32 mean within bf16 rounding.
+    local = out["local"]
+    with np.errstate(invalid="ignore"):
+        mean = local.mean(axis=0)
+        bound = 2 ** -7 * np.abs(local).mean(axis=0) + 1e-30
+        finite = np.isfinite(mean)
+        assert np.array_equal(finite, np.isfinite(out["reduced"]))
+        assert np.all(np.abs(out["reduced"][finite] - mean[finite]) <= bound[finite])
+    params = W.init_params(shape, seed=0)
+    decay, no_decay = shape.groups()
+    base = {"lr": 3e-4, "betas": (0.9, 0.999), "eps": 1e-8, "maximize": False}
+    # Registration order of the parameters (group by group) -> original index.
+    order = decay + no_decay
+    oracle = oadamw.OracleAdamW(params, [(decay, {**base, "weight_decay": 0.1}),
+                                         (no_decay, {**base, "weight_decay": 0.0})])
+    oscaler = oamp.OracleGradScaler(1024.0, 2.0, 0.5, 2)
+    for step in range(4):
+        flat = out["reduced"][step]
+        grads = [flat[o:o + n].reshape(s).astype(np.float32).copy()
+                 for o, n, (_, s) in zip(offsets, numels, shape.shapes())]
+        r = oamp.amp_step(oracle, oscaler, grads, max_norm=1.0)
+        assert bool(out["stepped"][step]) == r["stepped"]
+        if r["norm"] is not None:
+            assert abs(out["norms"][step] - r["norm"]) <= 1e-12 * r["norm"]
+    assert float(out["scale"]) == oscaler.scale
+    assert out["steps"].tolist() == [3] * len(numels)
+    for k, orig in enumerate(order):
+        np.testing.assert_allclose(out[f"master{k}"], params[orig], rtol=1e-6, atol=1e-12)
+        np.testing.assert_allclose(out[f"m{k}"], oracle.state[orig]["exp_avg"], rtol=1e-6, atol=1e-30)
+        # The all-gathered model copy is the bf16 rounding of the gathered master.
+        assert np.array_equal(f32_to_bf16_bits(out[f"copy{orig}"]), f32_to_bf16_bits(out[f"master{k}"]))
