@@ -212,6 +212,25 @@ size_t nt_grad_stats_workspace_size(void);
    found_inf, the max |g| and, for p = 2, the norm in one read; a general p needs pass 1. */
 int nt_grad_stats(const nt_grad_stats_args* args, void* stream);
 
+/* Allocation-free variant of nt_grad_stats (no counterpart in the reference). For callers
+   that cannot allocate device memory themselves -- a host whose device memory is owned by
+   its own pool, a plugin inside another runtime's allocator, a C/FFI caller without the
+   CUDA allocation calls -- the block partials, the last-block ticket and the span table
+   live in one static device array of nt_grad_stats_noalloc_scratch_bytes() bytes (about
+   33 KB) inside this library; every GPU that loads the library holds it until the process
+   exits. The caller still passes the gradients (`spans`: a HOST array of at most
+   NT_NOALLOC_MAX_SPANS {ptr, count} pairs; chunk_begin is ignored), the device loss scale
+   (or NULL) and the device nt_stats output. More spans are rejected with NT_EINVAL.
+   Same result as nt_grad_stats with finalize = 1 (two passes for a general p).
+   The first call on each device looks up the array's device address with that device
+   current; make that first call before any stream capture. All calls share the one array,
+   so calls that overlap on the GPU (different streams, different host threads) race;
+   serialise them. Nothing here calls cudaMalloc, cudaFree or an allocating library. */
+#define NT_NOALLOC_MAX_SPANS 64
+size_t nt_grad_stats_noalloc_scratch_bytes(void);
+int nt_grad_stats_noalloc(const nt_span* spans, int32_t num_spans, int32_t dtype, const float* scale,
+                          double norm_type, nt_stats* stats, void* stream);
+
 /* Computes norm and found_inf from the reduced fields (after a ZeRO-1 all-reduce). */
 int nt_grad_stats_finalize(nt_stats* stats, double norm_type, void* stream);
 

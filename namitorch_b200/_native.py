@@ -105,6 +105,9 @@ SIGNATURES: dict[str, tuple] = {
     "nt_grad_stats_workspace_size": (C.c_size_t, []),
     "nt_grad_stats": (C.c_int, [C.POINTER(GradStatsArgs), C.c_void_p]),
     "nt_grad_stats_finalize": (C.c_int, [C.c_void_p, C.c_double, C.c_void_p]),
+    "nt_grad_stats_noalloc_scratch_bytes": (C.c_size_t, []),
+    "nt_grad_stats_noalloc": (C.c_int, [C.POINTER(Span), C.c_int32, C.c_int32, C.c_void_p, C.c_double,
+                                        C.c_void_p, C.c_void_p]),
     "nt_grad_transform": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_int32, C.c_void_p,
                                     C.c_void_p, C.c_int32, C.c_double, C.c_void_p]),
     "nt_grad_clip_value": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_int32, C.c_double,
@@ -167,6 +170,7 @@ def check(status: int, what: str = "") -> None:
 # Kernel launches issued per successful call of each launching entry point (for the
 # benchmark's launch count; the statistics entry point launches one kernel per call).
 LAUNCHES_PER_CALL = {"nt_adamw_f32": 1, "nt_adamw_mt": 1, "nt_grad_stats": 1, "nt_grad_stats_finalize": 1,
+                     "nt_grad_stats_noalloc": 2,
                      "nt_grad_transform": 1, "nt_grad_clip_value": 1, "nt_scaler_update": 1,
                      "nt_softmax_xent": 2, "nt_xent_backward_scale": 1, "nt_cast": 1}
 launch_count = 0

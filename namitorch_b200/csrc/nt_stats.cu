@@ -9,6 +9,7 @@ namespace nt {
 constexpr int kStatsThreads = 256;
 constexpr int kUnroll = 4;  // 16-byte vectors in flight per thread
 constexpr int kStatsMaxBlocks = 1024;
+constexpr int kNoAllocChunk = 8192;
 
 struct StatsPartial {
   double sumsq;
@@ -379,6 +380,129 @@ int nt_scaler_update(float* scale, int32_t* growth_tracker, const double* const*
   P.growth = growth_factor; P.backoff = backoff_factor; P.interval = growth_interval;
   scaler_update_kernel<<<1, 32, 0, as_stream(stream)>>>(P);
   return launch_status("nt_scaler_update launch");
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free gradient statistics.
+//
+// Some callers cannot allocate device memory themselves: a host that has handed all of
+// its device memory to its own pool or arena, a plugin that runs inside another
+// runtime's allocator, or a C/FFI caller without access to the CUDA runtime's
+// allocation calls. For them, nt_grad_stats_noalloc keeps the cross-block scratch of the
+// statistics reduction (the block partials and the last-block ticket) and the span table
+// in one file-scope device array. Every GPU that loads this library reserves it
+// (kNoAllocScratchBytes) until the process exits.
+// ---------------------------------------------------------------------------------------------
+namespace nt {
+
+struct NoAllocScratch {
+  StatsWorkspace ws;
+  nt_span spans[NT_NOALLOC_MAX_SPANS];
+};
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[sizeof(NoAllocScratch)];
+
+struct NoAllocSpans {
+  nt_span spans[NT_NOALLOC_MAX_SPANS];
+  int count;
+};
+
+// Writes this call's span table into the scratch and clears the ticket counter (the
+// previous call leaves the array as it was, so nothing is assumed to start at zero).
+__global__ void noalloc_prepare_kernel(const __grid_constant__ NoAllocSpans S) {
+  NoAllocScratch* scratch = reinterpret_cast<NoAllocScratch*>(g_noalloc_scratch);
+  for (int i = threadIdx.x; i < S.count; i += blockDim.x) scratch->spans[i] = S.spans[i];
+  if (threadIdx.x == 0) scratch->ws.counter = 0u;
+}
+
+static void* g_noalloc_address[64] = {nullptr};
+
+// Device address of the scratch array on the current device. The host-side name of a
+// __device__ array is only a stand-in for its device address, so the address is looked
+// up once per device with that device current.
+static int noalloc_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) { set_error("nt_grad_stats_noalloc: device index %d out of range", dev); return NT_EINVAL; }
+  if (g_noalloc_address[dev] == nullptr) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(noalloc scratch)");
+    g_noalloc_address[dev] = ptr;
+  }
+  *out = g_noalloc_address[dev];
+  return NT_OK;
+}
+
+}  // namespace nt
+
+extern "C" {
+
+size_t nt_grad_stats_noalloc_scratch_bytes(void) { return sizeof(nt::NoAllocScratch); }
+
+int nt_grad_stats_noalloc(const nt_span* spans, int32_t num_spans, int32_t dtype, const float* scale,
+                          double norm_type, nt_stats* stats, void* stream) {
+  using namespace nt;
+  if (num_spans < 0) { set_error("nt_grad_stats_noalloc: negative span count"); return NT_EINVAL; }
+  if (num_spans > NT_NOALLOC_MAX_SPANS) {
+    set_error("nt_grad_stats_noalloc: %d spans exceed the maximum of %d (the span table lives in a fixed "
+              "%zu-byte static scratch array); merge gradients into fewer contiguous spans or use nt_grad_stats",
+              num_spans, NT_NOALLOC_MAX_SPANS, sizeof(NoAllocScratch));
+    return NT_EINVAL;
+  }
+  if (num_spans > 0 && !spans) { set_error("nt_grad_stats_noalloc: spans is NULL"); return NT_EINVAL; }
+  if (!stats) { set_error("nt_grad_stats_noalloc: stats is NULL"); return NT_EINVAL; }
+  if (dtype_size(dtype) == 0) { set_error("nt_grad_stats_noalloc: unsupported dtype %d", dtype); return NT_EUNSUPPORTED; }
+  if (!(norm_type > 0.0)) { set_error("nt_grad_stats_noalloc: norm_type must be positive"); return NT_EINVAL; }
+  void* base = nullptr;
+  int rc = noalloc_scratch_address(&base);
+  if (rc) return rc;
+  NoAllocScratch* scratch = static_cast<NoAllocScratch*>(base);
+
+  NoAllocSpans S;
+  int64_t chunks = 0;
+  int used = 0;
+  for (int i = 0; i < num_spans; ++i) {
+    if (spans[i].count < 0) { set_error("nt_grad_stats_noalloc: span %d has a negative count", i); return NT_EINVAL; }
+    if (spans[i].count == 0) continue;
+    if (!spans[i].ptr) { set_error("nt_grad_stats_noalloc: span %d has a NULL pointer", i); return NT_EINVAL; }
+    S.spans[used].ptr = spans[i].ptr;
+    S.spans[used].count = spans[i].count;
+    S.spans[used].chunk_begin = chunks;
+    chunks += (spans[i].count + kNoAllocChunk - 1) / kNoAllocChunk;
+    ++used;
+  }
+  S.count = used;
+  cudaStream_t s = as_stream(stream);
+  noalloc_prepare_kernel<<<1, 64, 0, s>>>(S);
+  rc = launch_status("nt_grad_stats_noalloc prepare launch");
+  if (rc) return rc;
+
+  StatsParams P;
+  P.spans = scratch->spans;
+  P.nspan = used;
+  P.chunk_elems = kNoAllocChunk;
+  P.nchunks = used == 0 ? 0 : chunks;
+  P.scale = scale;
+  P.p = norm_type;
+  P.stats = stats;
+  P.ws = &scratch->ws;
+  const int64_t grid_chunks = P.nchunks > 0 ? P.nchunks : 1;
+  const bool two_pass = !(norm_type == 2.0 || isinf(norm_type));
+  for (int pass = 0; pass <= (two_pass ? 1 : 0); ++pass) {
+    P.pass = pass;
+    P.finalize = pass == (two_pass ? 1 : 0);
+    switch (dtype) {
+      case NT_F32: rc = launch_grid(grad_stats_kernel<NT_F32>, P, grid_chunks, kStatsThreads, 6, kStatsMaxBlocks, s, "nt_grad_stats_noalloc launch"); break;
+      case NT_F16: rc = launch_grid(grad_stats_kernel<NT_F16>, P, grid_chunks, kStatsThreads, 6, kStatsMaxBlocks, s, "nt_grad_stats_noalloc launch"); break;
+      default: rc = launch_grid(grad_stats_kernel<NT_BF16>, P, grid_chunks, kStatsThreads, 6, kStatsMaxBlocks, s, "nt_grad_stats_noalloc launch"); break;
+    }
+    if (rc) return rc;
+  }
+  return NT_OK;
 }
 
 }  // extern "C"
