@@ -137,6 +137,33 @@ struct Unscale {
   }
 };
 
+// NaN-propagating max (the result is NaN if either operand is).
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Unpacks one 16-byte vector into fp32 values (4 for float32, 8 for 16-bit types).
+template <int DT>
+__device__ __forceinline__ void unpack16(const uint4& raw, float* out) {
+  if constexpr (DT == NT_F32) {
+    out[0] = __uint_as_float(raw.x); out[1] = __uint_as_float(raw.y);
+    out[2] = __uint_as_float(raw.z); out[3] = __uint_as_float(raw.w);
+  } else if constexpr (DT == NT_BF16) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      out[2 * k] = __uint_as_float(w[k] << 16);
+      out[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+    }
+  } else {
+    const __half* h = reinterpret_cast<const __half*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) out[k] = __half2float(h[k]);
+  }
+}
+
 // ---- chunk -> span lookup ------------------------------------------------------------
 // `begin(i)` is non-decreasing; returns the last index whose begin <= chunk.
 template <typename Begin>

@@ -60,23 +60,121 @@ __device__ void stats_finalize(nt_stats* s, double p) {
   s->norm = norm;
 }
 
-template <int DT>
-__device__ __forceinline__ void stats_accumulate(float u, int pass, double p, double maxabs,
-                                                 double& ss, double& ps, float& mx, unsigned& nf,
-                                                 unsigned& nn) {
-  if (pass == 0) {
-    const float a = fabsf(u);
-    const bool finite = a <= 3.402823466e38f;  // false for +-inf and NaN
-    mx = fmaxf(mx, a);                           // fmaxf skips NaN
-    nf += finite ? 0u : 1u;
-    nn += (u != u) ? 1u : 0u;
-    const double d = finite ? (double)u : 0.0;
-    ss = fma(d, d, ss);                          // u*u is exact in double
+enum { kScaleNone = 0, kScaleMul = 1, kScaleDiv = 2 };
+
+template <int MODE>
+__device__ __forceinline__ float unscale_by(float g, float scale, float inv) {
+  if constexpr (MODE == kScaleNone) return g;
+  else if constexpr (MODE == kScaleMul) return __fmul_rn(g, inv);
+  else return __fdiv_rn(g, scale);
+}
+
+struct StatsAcc {
+  double ss0, ss1, ps;
+  float mx;
+  unsigned nf, nn;
+};
+
+// One value the slow way: non-finite values are counted, finite ones accumulated.
+__device__ __forceinline__ void stats_one(float u, StatsAcc& a) {
+  const float m = fabsf(u);
+  a.mx = fmaxf(a.mx, m);  // fmaxf skips NaN
+  if (m <= 3.402823466e38f) {
+    const double d = (double)u;
+    a.ss0 = fma(d, d, a.ss0);  // u*u is exact in double
   } else {
-    if (!isfinite(u)) return;
-    const double scaled = __ddiv_rn(fabs((double)u), maxabs);
-    ps += p == 2.0 ? scaled * scaled : pow(scaled, p);
+    ++a.nf;
+    if (u != u) ++a.nn;
   }
+}
+
+template <int N>
+__device__ __forceinline__ void stats_pass0(const float* u, StatsAcc& a) {
+  float m = fabsf(u[0]);
+#pragma unroll
+  for (int q = 1; q < N; ++q) m = max_nan(m, fabsf(u[q]));
+  if (m <= 3.402823466e38f) {  // every value finite (a NaN makes m NaN)
+    a.mx = fmaxf(a.mx, m);
+#pragma unroll
+    for (int q = 0; q < N; ++q) {
+      const double d = (double)u[q];
+      if (q & 1) a.ss1 = fma(d, d, a.ss1);
+      else a.ss0 = fma(d, d, a.ss0);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < N; ++q) stats_one(u[q], a);
+  }
+}
+
+__device__ __forceinline__ void stats_pass1(float u, double p, double maxabs, StatsAcc& a) {
+  if (!(fabsf(u) <= 3.402823466e38f)) return;
+  const double scaled = __ddiv_rn(fabs((double)u), maxabs);
+  a.ps += p == 2.0 ? scaled * scaled : pow(scaled, p);
+}
+
+// One chunk of one span: 16-byte vectors, kUnroll of them in flight per thread.
+template <int DT, int MODE, int PASS>
+__device__ __forceinline__ void stats_chunk(const StatsParams& P, const nt_span& sp, int64_t begin, int64_t end,
+                                            float scale, float inv, double maxabs, StatsAcc& a) {
+  constexpr int ES = DT == NT_F32 ? 4 : 2;
+  constexpr int EPV = 16 / ES;
+  const char* base = static_cast<const char*>(sp.ptr);
+  int64_t e = begin;
+  if (((reinterpret_cast<uintptr_t>(base + begin * ES)) & 15u) == 0) {
+    const uint4* vec = reinterpret_cast<const uint4*>(base + begin * ES);
+    const int64_t nv = (end - begin) / EPV;
+    for (int64_t v0 = threadIdx.x; v0 < nv; v0 += (int64_t)blockDim.x * kUnroll) {
+      uint4 raw[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t v = v0 + (int64_t)u * blockDim.x;
+        if (v < nv) raw[u] = __ldcs(vec + v);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        if (v0 + (int64_t)u * blockDim.x < nv) {
+          float x[EPV];
+          unpack16<DT>(raw[u], x);
+#pragma unroll
+          for (int q = 0; q < EPV; ++q) x[q] = unscale_by<MODE>(x[q], scale, inv);
+          if constexpr (PASS == 0) {
+            stats_pass0<EPV>(x, a);
+          } else {
+#pragma unroll
+            for (int q = 0; q < EPV; ++q) stats_pass1(x[q], P.p, maxabs, a);
+          }
+        }
+      }
+    }
+    e = begin + nv * EPV;
+  }
+  for (int64_t i = e + threadIdx.x; i < end; i += blockDim.x) {
+    const float u = unscale_by<MODE>(load1<DT>(sp.ptr, i), scale, inv);
+    if constexpr (PASS == 0) stats_one(u, a);
+    else stats_pass1(u, P.p, maxabs, a);
+  }
+}
+
+template <int DT, int MODE, int PASS>
+__device__ __forceinline__ void stats_all_chunks(const StatsParams& P, float scale, float inv, double maxabs,
+                                                 StatsAcc& a) {
+  for (int64_t chunk = blockIdx.x; chunk < P.nchunks; chunk += gridDim.x) {
+    const int s = find_owner([&](int i) { return P.spans[i].chunk_begin; }, P.nspan, chunk);
+    const nt_span sp = P.spans[s];
+    const int64_t begin = (chunk - sp.chunk_begin) * (int64_t)P.chunk_elems;
+    int64_t end = begin + P.chunk_elems;
+    if (end > sp.count) end = sp.count;
+    stats_chunk<DT, MODE, PASS>(P, sp, begin, end, scale, inv, maxabs, a);
+  }
+}
+
+template <int DT, int PASS>
+__device__ __forceinline__ void stats_dispatch_scale(const StatsParams& P, const Unscale& un, double maxabs,
+                                                     StatsAcc& a) {
+  if (!un.active) stats_all_chunks<DT, kScaleNone, PASS>(P, 1.0f, 1.0f, maxabs, a);
+  else if (un.pow2) stats_all_chunks<DT, kScaleMul, PASS>(P, un.scale, un.inv, maxabs, a);
+  else stats_all_chunks<DT, kScaleDiv, PASS>(P, un.scale, un.inv, maxabs, a);
 }
 
 template <int DT>
@@ -88,47 +186,15 @@ __global__ void __launch_bounds__(kStatsThreads) grad_stats_kernel(const __grid_
   Unscale un;
   un.init(P.scale);
   const double maxabs = P.pass == 1 ? P.stats->maxabs : 0.0;
-  double ss = 0.0, ps = 0.0;
-  float mx = 0.0f;
-  unsigned nf = 0, nn = 0;
-  const int esize = DT == NT_F32 ? 4 : 2;
+  StatsAcc a{0.0, 0.0, 0.0, 0.0f, 0u, 0u};
+  if (P.pass == 0) stats_dispatch_scale<DT, 0>(P, un, maxabs, a);
+  else stats_dispatch_scale<DT, 1>(P, un, maxabs, a);
 
-  for (int64_t chunk = blockIdx.x; chunk < P.nchunks; chunk += gridDim.x) {
-    const int s = find_owner([&](int i) { return P.spans[i].chunk_begin; }, P.nspan, chunk);
-    const nt_span sp = P.spans[s];
-    const int64_t begin = (chunk - sp.chunk_begin) * (int64_t)P.chunk_elems;
-    int64_t end = begin + P.chunk_elems;
-    if (end > sp.count) end = sp.count;
-    int64_t e = begin;
-    if (((reinterpret_cast<uintptr_t>(static_cast<const char*>(sp.ptr) + begin * esize)) & 15u) == 0) {
-      const int64_t nv = (end - begin) >> 3;
-      // kUnroll independent 16-byte loads per thread before any arithmetic.
-      for (int64_t v0 = threadIdx.x; v0 < nv; v0 += (int64_t)blockDim.x * kUnroll) {
-        float x[kUnroll][8];
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          const int64_t v = v0 + (int64_t)u * blockDim.x;
-          if (v < nv) load8<DT>(sp.ptr, begin + v * 8, x[u]);
-        }
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-          if (v0 + (int64_t)u * blockDim.x < nv) {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) stats_accumulate<DT>(un(x[u][k]), P.pass, P.p, maxabs, ss, ps, mx, nf, nn);
-          }
-        }
-      }
-      e = begin + nv * 8;
-    }
-    for (int64_t i = e + threadIdx.x; i < end; i += blockDim.x)
-      stats_accumulate<DT>(un(load1<DT>(sp.ptr, i)), P.pass, P.p, maxabs, ss, ps, mx, nf, nn);
-  }
-
-  ss = block_reduce(ss, red_d, SumOp(), 0.0);
-  ps = block_reduce(ps, red_d, SumOp(), 0.0);
-  mx = block_reduce(mx, red_f, MaxOp(), 0.0f);
-  nf = block_reduce(nf, red_u, SumOp(), 0u);
-  nn = block_reduce(nn, red_u, SumOp(), 0u);
+  double ss = block_reduce(a.ss0 + a.ss1, red_d, SumOp(), 0.0);
+  double ps = block_reduce(a.ps, red_d, SumOp(), 0.0);
+  float mx = block_reduce(a.mx, red_f, MaxOp(), 0.0f);
+  unsigned nf = block_reduce(a.nf, red_u, SumOp(), 0u);
+  unsigned nn = block_reduce(a.nn, red_u, SumOp(), 0u);
   if (threadIdx.x == 0) {
     StatsPartial& out = P.ws->partials[blockIdx.x];
     out.sumsq = ss; out.powsum = ps; out.maxabs = mx; out.nonfinite = nf; out.nan = nn;

@@ -92,29 +92,24 @@ __device__ __forceinline__ float ex2(float x) {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per row: far beyond any real copy
 
-// Unpacks one 16-byte vector of the staged row into fp32 values.
-template <int DT>
-__device__ __forceinline__ void unpack16(const uint4& raw, float* out) {
-  if constexpr (DT == NT_F32) {
-    out[0] = __uint_as_float(raw.x); out[1] = __uint_as_float(raw.y);
-    out[2] = __uint_as_float(raw.z); out[3] = __uint_as_float(raw.w);
-  } else if constexpr (DT == NT_BF16) {
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      out[2 * k] = __uint_as_float(w[k] << 16);
-      out[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
-    }
-  } else {
-    const __half* h = reinterpret_cast<const __half*>(&raw);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) out[k] = __half2float(h[k]);
-  }
+// Round-to-nearest-even float32 -> bfloat16 bits with integer ALU operations (the
+// conversion instruction issues on the same narrow pipe as exp2). Not used for NaN
+// payloads other than the canonical quiet NaN the kernel writes itself.
+__device__ __forceinline__ uint32_t bf16_rne_bits(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u + 0x7fffu + ((u >> 16) & 1u)) >> 16;
 }
 
 template <int DT>
 __device__ __forceinline__ uint4 pack16(const float* v) {
   uint4 raw;
+  if constexpr (DT == NT_BF16) {
+    raw.x = bf16_rne_bits(v[0]) | (bf16_rne_bits(v[1]) << 16);
+    raw.y = bf16_rne_bits(v[2]) | (bf16_rne_bits(v[3]) << 16);
+    raw.z = bf16_rne_bits(v[4]) | (bf16_rne_bits(v[5]) << 16);
+    raw.w = bf16_rne_bits(v[6]) | (bf16_rne_bits(v[7]) << 16);
+    return raw;
+  }
   if constexpr (DT == NT_F32) {
     raw.x = __float_as_uint(v[0]); raw.y = __float_as_uint(v[1]);
     raw.z = __float_as_uint(v[2]); raw.w = __float_as_uint(v[3]);
@@ -125,12 +120,6 @@ __device__ __forceinline__ uint4 pack16(const float* v) {
     for (int k = 0; k < 8; ++k) h[k] = Elem<DT>::from_f32(v[k]);
   }
   return raw;
-}
-
-__device__ __forceinline__ float max_nan(float a, float b) {
-  float r;
-  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
-  return r;
 }
 
 __global__ void __launch_bounds__(kPrepThreads) xent_prepare_kernel(const __grid_constant__ XentParams P) {
@@ -255,10 +244,11 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
     // (max.NaN.f32), so one value carries both; label smoothing also needs sum_c w_c x_c.
     float m = -INFINITY, s = 0.0f;
     double swx = 0.0;
-    for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
+    const int dj = (int)blockDim.x * EPV;
+    int j0 = ((int)threadIdx.x * 16 - head) / ES;
+    for (int k = threadIdx.x; k < nvec; k += blockDim.x, j0 += dj) {
       float x[EPV];
       row_vector<DT, STAGED>(stage, P.logits, row_base, k, head, V, x);
-      const int j0 = (k * 16 - head) / ES;
       if (STAGED && (k < full_lo || k >= full_hi)) {
 #pragma unroll
         for (int q = 0; q < EPV; ++q)
@@ -364,8 +354,8 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
       const int kt = valid ? ((head + t * ES) >> 4) : -1;
       const int lane_t = valid ? (((head + t * ES) & 15) / ES) : 0;
       const float nanv = __int_as_float(0x7fc00000);
-      for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
-        const int j0 = (k * 16 - head) / ES;
+      int j0 = ((int)threadIdx.x * 16 - head) / ES;
+      for (int k = threadIdx.x; k < nvec; k += blockDim.x, j0 += dj) {
         float d[EPV];
         if (mode == 2) {
           float x[EPV];
