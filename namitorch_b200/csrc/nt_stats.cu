@@ -88,18 +88,46 @@ __device__ __forceinline__ void stats_one(float u, StatsAcc& a) {
   }
 }
 
+// Sum of squares of one vector, exactly as an unevaluated float32 pair (s + e):
+// each square is split error-free as hi + lo (hi = u*u, lo = fma(u, u, -hi)) and the hi
+// terms are added with TwoSum, whose rounding error is exact as well; only the final
+// accumulation into e rounds (relative 2^-24 of a term that is itself ~2^-24 of s).
+// Two float64 conversions per vector replace one per element.
+template <int N>
+__device__ __forceinline__ void sumsq_vector(const float* u, float& s, float& e) {
+  s = __fmul_rn(u[0], u[0]);
+  e = __fmaf_rn(u[0], u[0], -s);
+#pragma unroll
+  for (int q = 1; q < N; ++q) {
+    const float hi = __fmul_rn(u[q], u[q]);
+    const float lo = __fmaf_rn(u[q], u[q], -hi);
+    const float t = __fadd_rn(s, hi);
+    const float bp = __fsub_rn(t, s);
+    const float err = __fadd_rn(__fsub_rn(s, __fsub_rn(t, bp)), __fsub_rn(hi, bp));
+    s = t;
+    e = __fadd_rn(e, __fadd_rn(err, lo));
+  }
+}
+
 template <int N>
 __device__ __forceinline__ void stats_pass0(const float* u, StatsAcc& a) {
   float m = fabsf(u[0]);
 #pragma unroll
   for (int q = 1; q < N; ++q) m = max_nan(m, fabsf(u[q]));
-  if (m <= 3.402823466e38f) {  // every value finite (a NaN makes m NaN)
+  // All values finite (a NaN makes m NaN) and within [1e-15, 1e15], where every square,
+  // its split and the vector sum stay normal float32 numbers: the exact float32 path.
+  if (m <= 1.0e15f && m >= 1.0e-15f) {
+    a.mx = fmaxf(a.mx, m);
+    float s, e;
+    sumsq_vector<N>(u, s, e);
+    a.ss0 += (double)s;
+    a.ss1 += (double)e;
+  } else if (m <= 3.402823466e38f) {
     a.mx = fmaxf(a.mx, m);
 #pragma unroll
     for (int q = 0; q < N; ++q) {
       const double d = (double)u[q];
-      if (q & 1) a.ss1 = fma(d, d, a.ss1);
-      else a.ss0 = fma(d, d, a.ss0);
+      a.ss0 = fma(d, d, a.ss0);
     }
   } else {
 #pragma unroll
@@ -177,7 +205,7 @@ __device__ __forceinline__ void stats_dispatch_scale(const StatsParams& P, const
   else stats_all_chunks<DT, kScaleDiv, PASS>(P, un.scale, un.inv, maxabs, a);
 }
 
-template <int DT>
+template <int DT, int PASS>
 __global__ void __launch_bounds__(kStatsThreads) grad_stats_kernel(const __grid_constant__ StatsParams P) {
   __shared__ double red_d[kStatsThreads / 32];
   __shared__ float red_f[kStatsThreads / 32];
@@ -185,10 +213,9 @@ __global__ void __launch_bounds__(kStatsThreads) grad_stats_kernel(const __grid_
   __shared__ bool last;
   Unscale un;
   un.init(P.scale);
-  const double maxabs = P.pass == 1 ? P.stats->maxabs : 0.0;
+  const double maxabs = PASS == 1 ? P.stats->maxabs : 0.0;
   StatsAcc a{0.0, 0.0, 0.0, 0.0f, 0u, 0u};
-  if (P.pass == 0) stats_dispatch_scale<DT, 0>(P, un, maxabs, a);
-  else stats_dispatch_scale<DT, 1>(P, un, maxabs, a);
+  stats_dispatch_scale<DT, PASS>(P, un, maxabs, a);
 
   double ss = block_reduce(a.ss0 + a.ss1, red_d, SumOp(), 0.0);
   double ps = block_reduce(a.ps, red_d, SumOp(), 0.0);
@@ -215,7 +242,7 @@ __global__ void __launch_bounds__(kStatsThreads) grad_stats_kernel(const __grid_
   mx = block_reduce(mx, red_f, MaxOp(), 0.0f);
   if (threadIdx.x == 0) {
     nt_stats* st = P.stats;
-    if (P.pass == 0) {
+    if (PASS == 0) {
       st->sumsq = ss; st->nonfinite = nfd; st->nan = nnd; st->maxabs = (double)mx;
     } else {
       st->powsum = ps;
@@ -350,6 +377,21 @@ static int launch_grid(K kernel, const Params& P, int64_t nchunks, int threads, 
   return launch_status(what);
 }
 
+static int launch_stats(const StatsParams& P, int32_t dtype, int64_t nchunks, cudaStream_t s, const char* what) {
+  const bool p1 = P.pass == 1;
+  switch (dtype) {
+    case NT_F32:
+      return p1 ? launch_grid(grad_stats_kernel<NT_F32, 1>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what)
+                : launch_grid(grad_stats_kernel<NT_F32, 0>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what);
+    case NT_F16:
+      return p1 ? launch_grid(grad_stats_kernel<NT_F16, 1>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what)
+                : launch_grid(grad_stats_kernel<NT_F16, 0>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what);
+    default:
+      return p1 ? launch_grid(grad_stats_kernel<NT_BF16, 1>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what)
+                : launch_grid(grad_stats_kernel<NT_BF16, 0>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what);
+  }
+}
+
 }  // namespace nt
 
 using namespace nt;
@@ -378,11 +420,7 @@ int nt_grad_stats(const nt_grad_stats_args* args, void* stream) {
   cudaStream_t s = as_stream(stream);
   // An empty gradient list still runs one block so the statistics are written.
   const int64_t nchunks = P.nchunks > 0 ? P.nchunks : 1;
-  switch (a.dtype) {
-    case NT_F32: return launch_grid(grad_stats_kernel<NT_F32>, P, nchunks, kStatsThreads, 4, kStatsMaxBlocks, s, "nt_stats launch");
-    case NT_F16: return launch_grid(grad_stats_kernel<NT_F16>, P, nchunks, kStatsThreads, 4, kStatsMaxBlocks, s, "nt_stats launch");
-    default: return launch_grid(grad_stats_kernel<NT_BF16>, P, nchunks, kStatsThreads, 4, kStatsMaxBlocks, s, "nt_stats launch");
-  }
+  return launch_stats(P, a.dtype, nchunks, s, "nt_grad_stats launch");
 }
 
 int nt_grad_stats_finalize(nt_stats* stats, double norm_type, void* stream) {
@@ -561,11 +599,7 @@ int nt_grad_stats_noalloc(const nt_span* spans, int32_t num_spans, int32_t dtype
   for (int pass = 0; pass <= (two_pass ? 1 : 0); ++pass) {
     P.pass = pass;
     P.finalize = pass == (two_pass ? 1 : 0);
-    switch (dtype) {
-      case NT_F32: rc = launch_grid(grad_stats_kernel<NT_F32>, P, grid_chunks, kStatsThreads, 6, kStatsMaxBlocks, s, "nt_grad_stats_noalloc launch"); break;
-      case NT_F16: rc = launch_grid(grad_stats_kernel<NT_F16>, P, grid_chunks, kStatsThreads, 6, kStatsMaxBlocks, s, "nt_grad_stats_noalloc launch"); break;
-      default: rc = launch_grid(grad_stats_kernel<NT_BF16>, P, grid_chunks, kStatsThreads, 6, kStatsMaxBlocks, s, "nt_grad_stats_noalloc launch"); break;
-    }
+    rc = launch_stats(P, dtype, grid_chunks, s, "nt_grad_stats_noalloc launch");
     if (rc) return rc;
   }
   return NT_OK;

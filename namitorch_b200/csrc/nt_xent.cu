@@ -23,7 +23,6 @@
 
 namespace nt {
 
-constexpr int kXentThreads = 512;
 constexpr int kPrepThreads = 1024;
 
 struct XentWorkspace {
@@ -47,6 +46,7 @@ struct XentParams {
   XentWorkspace* ws;
   uintptr_t tensor_end;   // one past the last byte of the logits
   int staged;
+  int64_t stage_stride;   // bytes per staged row buffer
 };
 
 // ---- PTX helpers (mbarrier + bulk async copy; no cluster multicast) ---------------------
@@ -151,16 +151,36 @@ __global__ void __launch_bounds__(kPrepThreads) xent_prepare_kernel(const __grid
   }
 }
 
-// One 16-byte vector k of the row (EPV elements starting at element (16k - head) / ES).
-template <int DT, bool STAGED>
+// 2^x for x <= 0 on the FMA pipe (Cody-Waite reduction): x = n + f with n = rint(x) and
+// |f| <= 1/2; 2^f comes from a degree-5 polynomial whose coefficients were fitted by
+// iteratively reweighted least squares for minimum relative error on [-1/2, 1/2]
+// (max relative error 2.0e-7 evaluated in float32 Horner form, the same order as the
+// SFU's ex2.approx); 2^n is added to the exponent field. Results below about 2^-125
+// flush to zero. Used for the gradient pass so that the SFU only serves the sum pass.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -127.0f);
+  const float t = __fadd_rn(x, 12582912.0f);  // 1.5 * 2^23: x rounded to an integer in the low bits
+  const float r = __fsub_rn(t, 12582912.0f);
+  const int n = __float_as_int(t) - 0x4B400000;
+  const float f = __fsub_rn(x, r);
+  float q = 1.3276587706059217e-3f;
+  q = fmaf(q, f, 9.6755875274539e-3f);
+  q = fmaf(q, f, 5.550713464617729e-2f);
+  q = fmaf(q, f, 2.4022118747234344e-1f);
+  q = fmaf(q, f, 6.931469440460205e-1f);
+  q = fmaf(q, f, 1.0000001192092896f);
+  const float y = __uint_as_float(__float_as_uint(q) + ((unsigned)n << 23));
+  return n <= -126 ? 0.0f : y;
+}
+
+// One 16-byte vector k of the row (EPV elements starting at element j0).
+template <int DT, int STAGES>
 __device__ __forceinline__ void row_vector(const unsigned char* stage, const void* logits, int64_t row_base,
-                                           int k, int head, int V, float* x) {
-  constexpr int ES = DT == NT_F32 ? 4 : 2;
-  constexpr int EPV = 16 / ES;
-  if (STAGED) {
+                                           int k, int j0, int V, float* x) {
+  constexpr int EPV = DT == NT_F32 ? 4 : 8;
+  if constexpr (STAGES > 0) {
     unpack16<DT>(reinterpret_cast<const uint4*>(stage)[k], x);
   } else {
-    const int j0 = (k * 16 - head) / ES;
 #pragma unroll
     for (int q = 0; q < EPV; ++q) {
       const int j = j0 + q;
@@ -169,13 +189,44 @@ __device__ __forceinline__ void row_vector(const unsigned char* stage, const voi
   }
 }
 
-template <int DT, bool STAGED, bool WEIGHTED>
-__global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constant__ XentParams P) {
-  extern __shared__ __align__(128) unsigned char stage[];
-  __shared__ uint64_t bar;
-  __shared__ float red_f[kXentThreads / 32];
-  __shared__ float red_pair[kXentThreads / 32];
-  __shared__ double red_d[kXentThreads / 32];
+// Issues the bulk copy of `row` into `buf` (thread 0) and loads the bytes between the last
+// 16-byte boundary of the tensor and its end with plain loads (all threads). The copy starts
+// at the 16-byte boundary at or below the row start; the kernel indexes from the offset.
+template <int ES>
+__device__ __forceinline__ void stage_row(const XentParams& P, int64_t row, unsigned char* buf, uint64_t* bar) {
+  const uintptr_t start = reinterpret_cast<uintptr_t>(P.logits) + (uintptr_t)(row * P.classes * ES);
+  const uintptr_t a = start & ~(uintptr_t)15;
+  const int span = (int)(start - a) + (int)P.classes * ES;
+  int64_t bulk = (int64_t)((span + 15) >> 4) * 16;
+  const uintptr_t limit = P.tensor_end & ~(uintptr_t)15;
+  if ((int64_t)(limit - a) < bulk) bulk = (int64_t)(limit - a);
+  if (threadIdx.x == 0) {
+    fence_proxy_async();
+    mbar_arrive_expect_tx(bar, (uint32_t)bulk);
+    if (bulk > 0) bulk_g2s(buf, reinterpret_cast<const void*>(a), (uint32_t)bulk, bar);
+  }
+  for (int k = (int)bulk + threadIdx.x; k < span; k += blockDim.x) buf[k] = *reinterpret_cast<const unsigned char*>(a + k);
+}
+
+// Bounded wait for a staged row; false when the copy did not land within kWaitLimitNs.
+__device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
+}
+
+// STAGES = 2: double-buffered rows (the next row's copy is in flight while this one is
+// processed); 1: one staged row at a time (rows too large for two buffers); 0: no
+// staging (unaligned tensors), values read from global memory.
+template <int DT, int STAGES, bool WEIGHTED, int THREADS>
+__global__ void __launch_bounds__(THREADS) xent_kernel(const __grid_constant__ XentParams P) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t bars[2];
+  __shared__ float red_f[THREADS / 32];
+  __shared__ float red_pair[THREADS / 32];
+  __shared__ double red_d[THREADS / 32];
   __shared__ bool last;
   __shared__ int abort_flag;
 
@@ -191,93 +242,90 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
   const float e = P.smoothing;
   const bool smooth = e != 0.0f;
 
-  if (STAGED) {
+  if (STAGES > 0) {
     if (threadIdx.x == 0) {
-      mbar_init(&bar, 1);
+      mbar_init(&bars[0], 1);
+      mbar_init(&bars[1], 1);
       abort_flag = 0;
       fence_proxy_async();
     }
     __syncthreads();
   }
-  uint32_t phase = 0;
+  uint32_t phase0 = 0, phase1 = 0;
+  int64_t row = blockIdx.x;
+  if (STAGES > 0 && row < P.rows) stage_row<ES>(P, row, smem, &bars[0]);
 
-  for (int64_t row = blockIdx.x; row < P.rows; row += gridDim.x) {
+  for (int it = 0; row < P.rows; row += gridDim.x, ++it) {
+    const int buf = STAGES == 2 ? (it & 1) : 0;
+    const unsigned char* stage = smem + (size_t)buf * P.stage_stride;
+    const int64_t next = row + gridDim.x;
+    if (STAGES == 2 && next < P.rows)
+      stage_row<ES>(P, next, smem + (size_t)(buf ^ 1) * P.stage_stride, &bars[buf ^ 1]);
+    if (STAGES > 0) {
+      if (threadIdx.x == 0 && !wait_stage(&bars[buf], buf ? phase1 : phase0)) abort_flag = 1;
+      __syncthreads();
+      if (buf) phase1 ^= 1u; else phase0 ^= 1u;
+      if (abort_flag) {
+        if (threadIdx.x == 0) {
+          atomicAdd(&P.info->error, 1.0);
+          // Let a copy still in flight into the other buffer land (bounded) before leaving.
+          if (STAGES == 2 && next < P.rows) wait_stage(&bars[buf ^ 1], buf ? phase0 : phase1);
+        }
+        return;
+      }
+    }
+
     const int64_t t64 = P.targets[row];
     const bool valid = t64 != P.ignore && t64 >= 0 && t64 < V;
     const int t = valid ? (int)t64 : -1;
     const int64_t row_base = row * (int64_t)V;
     const uintptr_t start = reinterpret_cast<uintptr_t>(P.logits) + (uintptr_t)(row_base * ES);
-    const uintptr_t a = start & ~(uintptr_t)15;
-    const int head = (int)(start - a);
-    const int span = head + V * ES;           // bytes from a to the row end
+    const int head = (int)(start & 15u);
+    const int span = head + V * ES;           // bytes from the 16-byte boundary to the row end
     const int nvec = (span + 15) >> 4;
     const int full_lo = head ? 1 : 0;         // vectors [full_lo, full_hi) hold only row elements
     const int full_hi = span >> 4;
-
-    if (STAGED) {
-      int64_t bulk = (int64_t)nvec * 16;
-      const uintptr_t limit = P.tensor_end & ~(uintptr_t)15;
-      if ((int64_t)(limit - a) < bulk) bulk = (int64_t)(limit - a);
-      if (threadIdx.x == 0) {
-        fence_proxy_async();
-        mbar_arrive_expect_tx(&bar, (uint32_t)bulk);
-        if (bulk > 0) bulk_g2s(stage, reinterpret_cast<const void*>(a), (uint32_t)bulk, &bar);
-      }
-      // Bytes between the last 16-byte boundary of the tensor and its end.
-      for (int k = (int)bulk + threadIdx.x; k < span; k += blockDim.x)
-        stage[k] = *reinterpret_cast<const unsigned char*>(a + k);
-      if (threadIdx.x == 0) {
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(&bar, phase)) {
-          if (globaltimer() - t0 > kWaitLimitNs) { abort_flag = 1; break; }
-        }
-      }
-      __syncthreads();
-      phase ^= 1u;
-      if (abort_flag) {
-        if (threadIdx.x == 0) atomicAdd(&P.info->error, 1.0);
-        return;  // the copy never completed; leave the row untouched
-      }
-    }
+    const int dj = THREADS * EPV;
 
     // Pass A: online max / sum of exp per thread. The running max propagates NaN
     // (max.NaN.f32), so one value carries both; label smoothing also needs sum_c w_c x_c.
     float m = -INFINITY, s = 0.0f;
     double swx = 0.0;
-    const int dj = (int)blockDim.x * EPV;
-    int j0 = ((int)threadIdx.x * 16 - head) / ES;
-    for (int k = threadIdx.x; k < nvec; k += blockDim.x, j0 += dj) {
-      float x[EPV];
-      row_vector<DT, STAGED>(stage, P.logits, row_base, k, head, V, x);
-      if (STAGED && (k < full_lo || k >= full_hi)) {
+    {
+      int j0 = ((int)threadIdx.x * 16 - head) / ES;
+      for (int k = threadIdx.x; k < nvec; k += THREADS, j0 += dj) {
+        float x[EPV];
+        row_vector<DT, STAGES>(stage, P.logits, row_base, k, j0, V, x);
+        if (STAGES > 0 && (k < full_lo || k >= full_hi)) {
 #pragma unroll
-        for (int q = 0; q < EPV; ++q)
-          if (j0 + q < 0 || j0 + q >= V) x[q] = -INFINITY;
-      }
-      float vmax = x[0];
+          for (int q = 0; q < EPV; ++q)
+            if (j0 + q < 0 || j0 + q >= V) x[q] = -INFINITY;
+        }
+        float vmax = x[0];
 #pragma unroll
-      for (int q = 1; q < EPV; ++q) vmax = max_nan(vmax, x[q]);
-      const float mn = max_nan(m, vmax);
-      if (mn != m) {
-        s = m > -INFINITY ? s * ex2((m - mn) * kLog2e) : 0.0f;
-        m = mn;
-      }
-      if (m > -INFINITY) {
-        const float sh = m * kLog2e;
+        for (int q = 1; q < EPV; ++q) vmax = max_nan(vmax, x[q]);
+        const float mn = max_nan(m, vmax);
+        if (mn != m) {
+          s = m > -INFINITY ? s * ex2((m - mn) * kLog2e) : 0.0f;
+          m = mn;
+        }
+        if (m > -INFINITY) {
+          const float sh = m * kLog2e;
 #pragma unroll
-        for (int q = 0; q < EPV; ++q) s += ex2(fmaf(x[q], kLog2e, -sh));
-      }
-      if (smooth) {
+          for (int q = 0; q < EPV; ++q) s += ex2(fmaf(x[q], kLog2e, -sh));
+        }
+        if (smooth) {
 #pragma unroll
-        for (int q = 0; q < EPV; ++q) {
-          const int j = j0 + q;
-          if (j >= 0 && j < V) swx += WEIGHTED ? (double)P.weight[j] * (double)x[q] : (double)x[q];
+          for (int q = 0; q < EPV; ++q) {
+            const int j = j0 + q;
+            if (j >= 0 && j < V) swx += WEIGHTED ? (double)P.weight[j] * (double)x[q] : (double)x[q];
+          }
         }
       }
     }
-    // One block-wide merge of the (max, sum) pairs.
+    // One block-wide merge of the (max, sum) pairs, in a fixed order.
     {
-      const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+      const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
@@ -288,14 +336,15 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
                            : 0.0f;
         m = mm;
       }
-      __syncthreads();
       if (lane == 0) { red_f[warp] = m; red_pair[warp] = s; }
       __syncthreads();
       float M0 = -INFINITY;
-      for (int w = 0; w < nwarps; ++w) M0 = max_nan(M0, red_f[w]);
+#pragma unroll 4
+      for (int w = 0; w < THREADS / 32; ++w) M0 = max_nan(M0, red_f[w]);
       float S0 = 0.0f;
       if (M0 > -INFINITY) {
-        for (int w = 0; w < nwarps; ++w)
+#pragma unroll 4
+        for (int w = 0; w < THREADS / 32; ++w)
           if (red_f[w] > -INFINITY) S0 += red_pair[w] * ex2((red_f[w] - M0) * kLog2e);
       }
       m = M0;
@@ -320,7 +369,7 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
       } else {
         mode = 2;
         float xt;
-        if (STAGED) {
+        if constexpr (STAGES > 0) {
           const int off = head + t * ES;
           if constexpr (DT == NT_F32) xt = *reinterpret_cast<const float*>(stage + off);
           else if constexpr (DT == NT_BF16) xt = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(stage + off));
@@ -345,25 +394,25 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
     }
     if (threadIdx.x == 0) P.row_loss[row] = loss_i;
 
-    // Pass B: gradient.
+    // Pass B: gradient (exp on the FMA pipe).
     if (P.dl != nullptr) {
       const uintptr_t out_start = reinterpret_cast<uintptr_t>(P.dl) + (uintptr_t)(row_base * ES);
       const uintptr_t oa = out_start & ~(uintptr_t)15;
-      const bool vec_out = STAGED && (int)(out_start - oa) == head;
+      const bool vec_out = STAGES > 0 && (int)(out_start - oa) == head;
       const float shM = M * kLog2e;
       const int kt = valid ? ((head + t * ES) >> 4) : -1;
       const int lane_t = valid ? (((head + t * ES) & 15) / ES) : 0;
       const float nanv = __int_as_float(0x7fc00000);
       int j0 = ((int)threadIdx.x * 16 - head) / ES;
-      for (int k = threadIdx.x; k < nvec; k += blockDim.x, j0 += dj) {
+      for (int k = threadIdx.x; k < nvec; k += THREADS, j0 += dj) {
         float d[EPV];
         if (mode == 2) {
           float x[EPV];
-          row_vector<DT, STAGED>(stage, P.logits, row_base, k, head, V, x);
+          row_vector<DT, STAGES>(stage, P.logits, row_base, k, j0, V, x);
 #pragma unroll
           for (int q = 0; q < EPV; ++q) {
             const float g = WEIGHTED ? G * ((j0 + q >= 0 && j0 + q < V) ? P.weight[j0 + q] : 0.0f) : G;
-            d[q] = fmaf(ex2(fmaf(x[q], kLog2e, -shM)), A, -g);
+            d[q] = fmaf(exp2_poly(fmaf(x[q], kLog2e, -shM)), A, -g);
           }
           if (k == kt) {
 #pragma unroll
@@ -385,14 +434,15 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
         }
       }
     }
-    if (STAGED) __syncthreads();  // every thread is done with the staged row
+    __syncthreads();  // every thread is done with this row's buffer and reduction scratch
+    if (STAGES == 1 && next < P.rows) stage_row<ES>(P, next, smem, &bars[0]);
   }
 
   // Loss reduction over rows, in a fixed order, by the last block.
   if (P.reduction == NT_REDUCTION_NONE) return;
   if (!last_block_ticket(&P.ws->counter, &last)) return;
   double acc = 0.0;
-  for (int64_t r = threadIdx.x; r < P.rows; r += blockDim.x) acc += (double)P.row_loss[r];
+  for (int64_t r = threadIdx.x; r < P.rows; r += THREADS) acc += (double)P.row_loss[r];
   acc = block_reduce(acc, red_d, SumOp(), 0.0);
   if (threadIdx.x == 0) {
     P.info->loss_sum = acc;
@@ -414,37 +464,37 @@ __global__ void __launch_bounds__(256) xent_scale_kernel(void* dl, int64_t rows,
   }
 }
 
+template <int DT, int STAGES, bool WEIGHTED, int THREADS>
+static int launch_variant(const XentParams& P, size_t smem, cudaStream_t stream) {
+  auto kernel = xent_kernel<DT, STAGES, WEIGHTED, THREADS>;
+  if (smem > 0) {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(xent)");
+  }
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, THREADS, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  int64_t grid = (int64_t)current_sm_count() * per_sm;
+  if (grid > P.rows) grid = P.rows;
+  if (grid < 1) grid = 1;
+  kernel<<<(unsigned)grid, THREADS, smem, stream>>>(P);
+  return launch_status("nt_softmax_xent launch");
+}
+
 template <int DT, bool WEIGHTED>
 static int launch_xent(const XentParams& P0, cudaStream_t stream) {
   XentParams P = P0;
   constexpr int ES = DT == NT_F32 ? 4 : 2;
-  const size_t stage_bytes = (size_t)(((P.classes * ES + 15) / 16 + 1) * 16);
+  // Row buffer: the row plus up to 15 leading bytes, rounded to 128 bytes.
+  const size_t stride = (size_t)((P.classes * ES + 16 + 127) / 128 * 128);
+  P.stage_stride = (int64_t)stride;
   int max_optin = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  const bool can_stage = P.staged && stage_bytes + 4096 <= (size_t)max_optin;
-  int per_sm = 1;
-  if (can_stage) {
-    cudaError_t err = cudaFuncSetAttribute(xent_kernel<DT, true, WEIGHTED>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)stage_bytes);
-    if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(xent)");
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, xent_kernel<DT, true, WEIGHTED>, kXentThreads,
-                                                      stage_bytes) != cudaSuccess || per_sm < 1)
-      per_sm = 1;
-  } else {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, xent_kernel<DT, false, WEIGHTED>, kXentThreads, 0) !=
-            cudaSuccess || per_sm < 1)
-      per_sm = 1;
-  }
-  int64_t grid = (int64_t)current_sm_count() * per_sm;
-  if (grid > P.rows) grid = P.rows;
-  if (grid < 1) grid = 1;
-  P.staged = can_stage;
-  if (can_stage)
-    xent_kernel<DT, true, WEIGHTED><<<(unsigned)grid, kXentThreads, stage_bytes, stream>>>(P);
-  else
-    xent_kernel<DT, false, WEIGHTED><<<(unsigned)grid, kXentThreads, 0, stream>>>(P);
-  return launch_status("nt_softmax_xent launch");
+  const size_t budget = (size_t)max_optin > 4096 ? (size_t)max_optin - 4096 : 0;
+  if (P.staged && 2 * stride <= budget) return launch_variant<DT, 2, WEIGHTED, 1024>(P, 2 * stride, stream);
+  if (P.staged && stride <= budget) return launch_variant<DT, 1, WEIGHTED, 512>(P, stride, stream);
+  return launch_variant<DT, 0, WEIGHTED, 512>(P, 0, stream);
 }
 
 template <int DT>
