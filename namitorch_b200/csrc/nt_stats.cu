@@ -7,7 +7,7 @@
 namespace nt {
 
 constexpr int kStatsThreads = 256;
-constexpr int kUnroll = 4;  // 16-byte vectors in flight per thread
+constexpr int kUnroll = 8;  // 16-byte vectors in flight per thread
 constexpr int kStatsMaxBlocks = 1024;
 constexpr int kNoAllocChunk = 8192;
 
@@ -88,46 +88,18 @@ __device__ __forceinline__ void stats_one(float u, StatsAcc& a) {
   }
 }
 
-// Sum of squares of one vector, exactly as an unevaluated float32 pair (s + e):
-// each square is split error-free as hi + lo (hi = u*u, lo = fma(u, u, -hi)) and the hi
-// terms are added with TwoSum, whose rounding error is exact as well; only the final
-// accumulation into e rounds (relative 2^-24 of a term that is itself ~2^-24 of s).
-// Two float64 conversions per vector replace one per element.
-template <int N>
-__device__ __forceinline__ void sumsq_vector(const float* u, float& s, float& e) {
-  s = __fmul_rn(u[0], u[0]);
-  e = __fmaf_rn(u[0], u[0], -s);
-#pragma unroll
-  for (int q = 1; q < N; ++q) {
-    const float hi = __fmul_rn(u[q], u[q]);
-    const float lo = __fmaf_rn(u[q], u[q], -hi);
-    const float t = __fadd_rn(s, hi);
-    const float bp = __fsub_rn(t, s);
-    const float err = __fadd_rn(__fsub_rn(s, __fsub_rn(t, bp)), __fsub_rn(hi, bp));
-    s = t;
-    e = __fadd_rn(e, __fadd_rn(err, lo));
-  }
-}
-
 template <int N>
 __device__ __forceinline__ void stats_pass0(const float* u, StatsAcc& a) {
   float m = fabsf(u[0]);
 #pragma unroll
   for (int q = 1; q < N; ++q) m = max_nan(m, fabsf(u[q]));
-  // All values finite (a NaN makes m NaN) and within [1e-15, 1e15], where every square,
-  // its split and the vector sum stay normal float32 numbers: the exact float32 path.
-  if (m <= 1.0e15f && m >= 1.0e-15f) {
-    a.mx = fmaxf(a.mx, m);
-    float s, e;
-    sumsq_vector<N>(u, s, e);
-    a.ss0 += (double)s;
-    a.ss1 += (double)e;
-  } else if (m <= 3.402823466e38f) {
+  if (m <= 3.402823466e38f) {  // every value finite (a NaN makes m NaN)
     a.mx = fmaxf(a.mx, m);
 #pragma unroll
     for (int q = 0; q < N; ++q) {
-      const double d = (double)u[q];
-      a.ss0 = fma(d, d, a.ss0);
+      const double d = (double)u[q];  // u*u is exact in double
+      if (q & 1) a.ss1 = fma(d, d, a.ss1);
+      else a.ss0 = fma(d, d, a.ss0);
     }
   } else {
 #pragma unroll

@@ -92,22 +92,14 @@ __device__ __forceinline__ float ex2(float x) {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per row: far beyond any real copy
 
-// Round-to-nearest-even float32 -> bfloat16 bits with integer ALU operations (the
-// conversion instruction issues on the same narrow pipe as exp2). Not used for NaN
-// payloads other than the canonical quiet NaN the kernel writes itself.
-__device__ __forceinline__ uint32_t bf16_rne_bits(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u + 0x7fffu + ((u >> 16) & 1u)) >> 16;
-}
-
 template <int DT>
 __device__ __forceinline__ uint4 pack16(const float* v) {
   uint4 raw;
   if constexpr (DT == NT_BF16) {
-    raw.x = bf16_rne_bits(v[0]) | (bf16_rne_bits(v[1]) << 16);
-    raw.y = bf16_rne_bits(v[2]) | (bf16_rne_bits(v[3]) << 16);
-    raw.z = bf16_rne_bits(v[4]) | (bf16_rne_bits(v[5]) << 16);
-    raw.w = bf16_rne_bits(v[6]) | (bf16_rne_bits(v[7]) << 16);
+    __nv_bfloat162 h[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) h[k] = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+    raw = *reinterpret_cast<uint4*>(h);
     return raw;
   }
   if constexpr (DT == NT_F32) {
@@ -149,28 +141,6 @@ __global__ void __launch_bounds__(kPrepThreads) xent_prepare_kernel(const __grid
     info->error = 0.0;
     if (P.rows == 0 && P.reduction != NT_REDUCTION_NONE) P.loss[0] = 0.0f;
   }
-}
-
-// 2^x for x <= 0 on the FMA pipe (Cody-Waite reduction): x = n + f with n = rint(x) and
-// |f| <= 1/2; 2^f comes from a degree-5 polynomial whose coefficients were fitted by
-// iteratively reweighted least squares for minimum relative error on [-1/2, 1/2]
-// (max relative error 2.0e-7 evaluated in float32 Horner form, the same order as the
-// SFU's ex2.approx); 2^n is added to the exponent field. Results below about 2^-125
-// flush to zero. Used for the gradient pass so that the SFU only serves the sum pass.
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -127.0f);
-  const float t = __fadd_rn(x, 12582912.0f);  // 1.5 * 2^23: x rounded to an integer in the low bits
-  const float r = __fsub_rn(t, 12582912.0f);
-  const int n = __float_as_int(t) - 0x4B400000;
-  const float f = __fsub_rn(x, r);
-  float q = 1.3276587706059217e-3f;
-  q = fmaf(q, f, 9.6755875274539e-3f);
-  q = fmaf(q, f, 5.550713464617729e-2f);
-  q = fmaf(q, f, 2.4022118747234344e-1f);
-  q = fmaf(q, f, 6.931469440460205e-1f);
-  q = fmaf(q, f, 1.0000001192092896f);
-  const float y = __uint_as_float(__float_as_uint(q) + ((unsigned)n << 23));
-  return n <= -126 ? 0.0f : y;
 }
 
 // One 16-byte vector k of the row (EPV elements starting at element j0).
@@ -289,38 +259,50 @@ __global__ void __launch_bounds__(THREADS) xent_kernel(const __grid_constant__ X
 
     // Pass A: online max / sum of exp per thread. The running max propagates NaN
     // (max.NaN.f32), so one value carries both; label smoothing also needs sum_c w_c x_c.
+    // Interior vectors need no bounds checks; the <= 2 edge vectors of the row are
+    // masked and taken by the first threads after the interior loop.
     float m = -INFINITY, s = 0.0f;
     double swx = 0.0;
+    auto accumulate = [&](const float* x, int j0, bool edge) {
+      float vmax = x[0];
+#pragma unroll
+      for (int q = 1; q < EPV; ++q) vmax = max_nan(vmax, x[q]);
+      const float mn = max_nan(m, vmax);
+      if (mn != m) {
+        s = m > -INFINITY ? s * ex2((m - mn) * kLog2e) : 0.0f;
+        m = mn;
+      }
+      if (m > -INFINITY) {
+        const float sh = m * kLog2e;
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) s += ex2(fmaf(x[q], kLog2e, -sh));
+      }
+      if (smooth) {
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) {
+          const int j = j0 + q;
+          if (!edge || (j >= 0 && j < V)) swx += WEIGHTED ? (double)P.weight[j] * (double)x[q] : (double)x[q];
+        }
+      }
+    };
     {
-      int j0 = ((int)threadIdx.x * 16 - head) / ES;
-      for (int k = threadIdx.x; k < nvec; k += THREADS, j0 += dj) {
+      int j0 = ((full_lo + (int)threadIdx.x) * 16 - head) / ES;
+      for (int k = full_lo + threadIdx.x; k < full_hi; k += THREADS, j0 += dj) {
         float x[EPV];
         row_vector<DT, STAGES>(stage, P.logits, row_base, k, j0, V, x);
-        if (STAGES > 0 && (k < full_lo || k >= full_hi)) {
+        accumulate(x, j0, false);
+      }
+      // Edge vectors: k = 0 when the row starts inside a vector, k = full_hi when it ends inside one.
+      const int nedge = full_lo + (nvec - full_hi);
+      if ((int)threadIdx.x < nedge) {
+        const int k = (threadIdx.x == 0 && full_lo) ? 0 : full_hi;
+        const int j0e = (k * 16 - head) / ES;
+        float x[EPV];
+        row_vector<DT, STAGES>(stage, P.logits, row_base, k, j0e, V, x);
 #pragma unroll
-          for (int q = 0; q < EPV; ++q)
-            if (j0 + q < 0 || j0 + q >= V) x[q] = -INFINITY;
-        }
-        float vmax = x[0];
-#pragma unroll
-        for (int q = 1; q < EPV; ++q) vmax = max_nan(vmax, x[q]);
-        const float mn = max_nan(m, vmax);
-        if (mn != m) {
-          s = m > -INFINITY ? s * ex2((m - mn) * kLog2e) : 0.0f;
-          m = mn;
-        }
-        if (m > -INFINITY) {
-          const float sh = m * kLog2e;
-#pragma unroll
-          for (int q = 0; q < EPV; ++q) s += ex2(fmaf(x[q], kLog2e, -sh));
-        }
-        if (smooth) {
-#pragma unroll
-          for (int q = 0; q < EPV; ++q) {
-            const int j = j0 + q;
-            if (j >= 0 && j < V) swx += WEIGHTED ? (double)P.weight[j] * (double)x[q] : (double)x[q];
-          }
-        }
+        for (int q = 0; q < EPV; ++q)
+          if (j0e + q < 0 || j0e + q >= V) x[q] = -INFINITY;
+        accumulate(x, j0e, true);
       }
     }
     // One block-wide merge of the (max, sum) pairs, in a fixed order.
@@ -394,7 +376,7 @@ __global__ void __launch_bounds__(THREADS) xent_kernel(const __grid_constant__ X
     }
     if (threadIdx.x == 0) P.row_loss[row] = loss_i;
 
-    // Pass B: gradient (exp on the FMA pipe).
+    // Pass B: gradient.
     if (P.dl != nullptr) {
       const uintptr_t out_start = reinterpret_cast<uintptr_t>(P.dl) + (uintptr_t)(row_base * ES);
       const uintptr_t oa = out_start & ~(uintptr_t)15;
@@ -403,16 +385,14 @@ __global__ void __launch_bounds__(THREADS) xent_kernel(const __grid_constant__ X
       const int kt = valid ? ((head + t * ES) >> 4) : -1;
       const int lane_t = valid ? (((head + t * ES) & 15) / ES) : 0;
       const float nanv = __int_as_float(0x7fc00000);
-      int j0 = ((int)threadIdx.x * 16 - head) / ES;
-      for (int k = threadIdx.x; k < nvec; k += THREADS, j0 += dj) {
-        float d[EPV];
+      auto gradient = [&](int k, int j0, float* d) {
         if (mode == 2) {
           float x[EPV];
           row_vector<DT, STAGES>(stage, P.logits, row_base, k, j0, V, x);
 #pragma unroll
           for (int q = 0; q < EPV; ++q) {
             const float g = WEIGHTED ? G * ((j0 + q >= 0 && j0 + q < V) ? P.weight[j0 + q] : 0.0f) : G;
-            d[q] = fmaf(exp2_poly(fmaf(x[q], kLog2e, -shM)), A, -g);
+            d[q] = fmaf(ex2(fmaf(x[q], kLog2e, -shM)), A, -g);
           }
           if (k == kt) {
 #pragma unroll
@@ -423,15 +403,28 @@ __global__ void __launch_bounds__(THREADS) xent_kernel(const __grid_constant__ X
 #pragma unroll
           for (int q = 0; q < EPV; ++q) d[q] = mode == 1 ? nanv : 0.0f;
         }
-        if (vec_out && k >= full_lo && k < full_hi) {
-          __stcs(reinterpret_cast<uint4*>(oa + (uintptr_t)k * 16), pack16<DT>(d));
-        } else {
+      };
+      auto store_scalar = [&](int j0, const float* d) {
 #pragma unroll
-          for (int q = 0; q < EPV; ++q) {
-            const int j = j0 + q;
-            if (j >= 0 && j < V) store1<DT>(P.dl, row_base + j, d[q]);
-          }
+        for (int q = 0; q < EPV; ++q) {
+          const int j = j0 + q;
+          if (j >= 0 && j < V) store1<DT>(P.dl, row_base + j, d[q]);
         }
+      };
+      int j0 = ((full_lo + (int)threadIdx.x) * 16 - head) / ES;
+      for (int k = full_lo + threadIdx.x; k < full_hi; k += THREADS, j0 += dj) {
+        float d[EPV];
+        gradient(k, j0, d);
+        if (vec_out) __stcs(reinterpret_cast<uint4*>(oa + (uintptr_t)k * 16), pack16<DT>(d));
+        else store_scalar(j0, d);
+      }
+      const int nedge = full_lo + (nvec - full_hi);
+      if ((int)threadIdx.x < nedge) {
+        const int k = (threadIdx.x == 0 && full_lo) ? 0 : full_hi;
+        const int j0e = (k * 16 - head) / ES;
+        float d[EPV];
+        gradient(k, j0e, d);
+        store_scalar(j0e, d);
       }
     }
     __syncthreads();  // every thread is done with this row's buffer and reduction scratch
