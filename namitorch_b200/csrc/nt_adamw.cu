@@ -179,23 +179,36 @@ __global__ void __launch_bounds__(256) adamw_mt_kernel(const __grid_constant__ M
   }
   const int gsize = GDT == NT_F32 ? 4 : 2;
 
-  for (int64_t chunk = blockIdx.x; chunk < P.nchunks; chunk += gridDim.x) {
-    const int s = find_owner([&](int i) { return P.segs[i].chunk_begin; }, P.nseg, chunk);
-    const nt_segment seg = P.segs[s];
-    const nt_adamw_group& gr = P.groups[seg.group];
-    const int t = P.steps[seg.step_slot] + 1;
-    if (t <= 0) {
-      if (threadIdx.x == 0 && P.error) atomicOr(P.error, 1);
-      continue;
+  // Each block takes a contiguous range of chunks: one segment lookup per block, then the
+  // segment's record, coefficients and bias corrections are carried in registers until the
+  // chunks cross into the next segment.
+  const int64_t per = (P.nchunks + gridDim.x - 1) / gridDim.x;
+  const int64_t c0 = (int64_t)blockIdx.x * per;
+  const int64_t c1 = c0 + per < P.nchunks ? c0 + per : P.nchunks;
+  int s = c0 < c1 ? find_owner([&](int i) { return P.segs[i].chunk_begin; }, P.nseg, c0) : 0;
+  int64_t next_begin = -1;  // forces a load of segment s at the first chunk
+  nt_segment seg{};
+  Coef c{};
+  bool seg_ok = false;
+  for (int64_t chunk = c0; chunk < c1; ++chunk) {
+    if (chunk >= next_begin) {
+      if (next_begin >= 0) ++s;
+      while (s + 1 < P.nseg && P.segs[s + 1].chunk_begin <= chunk) ++s;
+      seg = P.segs[s];
+      next_begin = s + 1 < P.nseg ? P.segs[s + 1].chunk_begin : INT64_MAX;
+      const nt_adamw_group& gr = P.groups[seg.group];
+      const int t = P.steps[seg.step_slot] + 1;
+      seg_ok = t > 0;
+      if (!seg_ok && threadIdx.x == 0 && P.error) atomicOr(P.error, 1);
+      // Steps past the table use its last row: the host only lets that happen once every
+      // row has saturated at exactly 1.0f, where f32(1 - beta^t) stays for all larger t.
+      const int ti = t < P.cap ? t : P.cap - 1;
+      const float2 corr = seg_ok ? P.corr[(int64_t)gr.correction_row * P.cap + ti] : make_float2(1.0f, 1.0f);
+      c.lr = gr.lr; c.b1 = gr.beta1; c.b2 = gr.beta2; c.c1 = gr.one_minus_beta1; c.c2 = gr.one_minus_beta2;
+      c.eps = gr.eps; c.wd = gr.weight_decay; c.decay = gr.decay_factor; c.corr1 = corr.x; c.corr2 = corr.y;
+      c.decay_mode = gr.decay_mode; c.maximize = gr.maximize != 0; c.update = gr.update_parameter != 0;
     }
-    // Steps past the table use its last row: the host only lets that happen once every
-    // row has saturated at exactly 1.0f, where f32(1 - beta^t) stays for all larger t.
-    const int ti = t < P.cap ? t : P.cap - 1;
-    const float2 corr = P.corr[(int64_t)gr.correction_row * P.cap + ti];
-    Coef c;
-    c.lr = gr.lr; c.b1 = gr.beta1; c.b2 = gr.beta2; c.c1 = gr.one_minus_beta1; c.c2 = gr.one_minus_beta2;
-    c.eps = gr.eps; c.wd = gr.weight_decay; c.decay = gr.decay_factor; c.corr1 = corr.x; c.corr2 = corr.y;
-    c.decay_mode = gr.decay_mode; c.maximize = gr.maximize != 0; c.update = gr.update_parameter != 0;
+    if (!seg_ok) continue;
 
     const int64_t begin = (chunk - seg.chunk_begin) * (int64_t)P.chunk_elems;
     int64_t end = begin + P.chunk_elems;

@@ -7,7 +7,7 @@
 namespace nt {
 
 constexpr int kStatsThreads = 256;
-constexpr int kUnroll = 8;  // 16-byte vectors in flight per thread
+constexpr int kUnroll = 4;  // 16-byte vectors in flight per thread
 constexpr int kStatsMaxBlocks = 1024;
 constexpr int kNoAllocChunk = 8192;
 
@@ -156,12 +156,24 @@ __device__ __forceinline__ void stats_chunk(const StatsParams& P, const nt_span&
   }
 }
 
+// Each block takes a contiguous range of chunks: one span lookup per block, then the span
+// record is carried in registers and advanced as the chunks cross span boundaries.
 template <int DT, int MODE, int PASS>
 __device__ __forceinline__ void stats_all_chunks(const StatsParams& P, float scale, float inv, double maxabs,
                                                  StatsAcc& a) {
-  for (int64_t chunk = blockIdx.x; chunk < P.nchunks; chunk += gridDim.x) {
-    const int s = find_owner([&](int i) { return P.spans[i].chunk_begin; }, P.nspan, chunk);
-    const nt_span sp = P.spans[s];
+  const int64_t per = (P.nchunks + gridDim.x - 1) / gridDim.x;
+  const int64_t c0 = (int64_t)blockIdx.x * per;
+  const int64_t c1 = c0 + per < P.nchunks ? c0 + per : P.nchunks;
+  if (c0 >= c1) return;
+  int s = find_owner([&](int i) { return P.spans[i].chunk_begin; }, P.nspan, c0);
+  nt_span sp = P.spans[s];
+  int64_t next_begin = s + 1 < P.nspan ? P.spans[s + 1].chunk_begin : INT64_MAX;
+  for (int64_t chunk = c0; chunk < c1; ++chunk) {
+    while (chunk >= next_begin) {
+      ++s;
+      sp = P.spans[s];
+      next_begin = s + 1 < P.nspan ? P.spans[s + 1].chunk_begin : INT64_MAX;
+    }
     const int64_t begin = (chunk - sp.chunk_begin) * (int64_t)P.chunk_elems;
     int64_t end = begin + P.chunk_elems;
     if (end > sp.count) end = sp.count;

@@ -149,7 +149,11 @@ __device__ __forceinline__ void row_vector(const unsigned char* stage, const voi
                                            int k, int j0, int V, float* x) {
   constexpr int EPV = DT == NT_F32 ? 4 : 8;
   if constexpr (STAGES > 0) {
-    unpack16<DT>(reinterpret_cast<const uint4*>(stage)[k], x);
+    uint4 raw;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(raw.x), "=r"(raw.y), "=r"(raw.z), "=r"(raw.w)
+                 : "r"(smem_u32(stage) + (uint32_t)k * 16u));
+    unpack16<DT>(raw, x);
   } else {
 #pragma unroll
     for (int q = 0; q < EPV; ++q) {
@@ -292,8 +296,9 @@ __global__ void __launch_bounds__(THREADS) xent_kernel(const __grid_constant__ X
         row_vector<DT, STAGES>(stage, P.logits, row_base, k, j0, V, x);
         accumulate(x, j0, false);
       }
-      // Edge vectors: k = 0 when the row starts inside a vector, k = full_hi when it ends inside one.
-      const int nedge = full_lo + (nvec - full_hi);
+      // Edge vectors: the head vector when the row starts inside it and the tail vector when the
+      // row ends inside it; one vector when the whole row fits in it.
+      const int nedge = full_lo + ((full_hi < nvec && full_hi >= full_lo) ? 1 : 0);
       if ((int)threadIdx.x < nedge) {
         const int k = (threadIdx.x == 0 && full_lo) ? 0 : full_hi;
         const int j0e = (k * 16 - head) / ES;
@@ -418,7 +423,7 @@ __global__ void __launch_bounds__(THREADS) xent_kernel(const __grid_constant__ X
         if (vec_out) __stcs(reinterpret_cast<uint4*>(oa + (uintptr_t)k * 16), pack16<DT>(d));
         else store_scalar(j0, d);
       }
-      const int nedge = full_lo + (nvec - full_hi);
+      const int nedge = full_lo + ((full_hi < nvec && full_hi >= full_lo) ? 1 : 0);
       if ((int)threadIdx.x < nedge) {
         const int k = (threadIdx.x == 0 && full_lo) ? 0 : full_hi;
         const int j0e = (k * 16 - head) / ES;
@@ -485,6 +490,12 @@ static int launch_xent(const XentParams& P0, cudaStream_t stream) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   const size_t budget = (size_t)max_optin > 4096 ? (size_t)max_optin - 4096 : 0;
+  // Preferred: two CTAs per SM, each with one staged row, so one CTA's copy overlaps the
+  // other's compute. Rows too large for that: one CTA per SM with two buffers.
+  int sm_smem = 0;
+  cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  if (P.staged && 2 * (stride + 4096) <= (size_t)sm_smem && stride <= budget)
+    return launch_variant<DT, 1, WEIGHTED, 512>(P, stride, stream);
   if (P.staged && 2 * stride <= budget) return launch_variant<DT, 2, WEIGHTED, 1024>(P, 2 * stride, stream);
   if (P.staged && stride <= budget) return launch_variant<DT, 1, WEIGHTED, 512>(P, stride, stream);
   return launch_variant<DT, 0, WEIGHTED, 512>(P, 0, stream);
