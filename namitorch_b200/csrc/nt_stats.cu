@@ -190,7 +190,7 @@ __device__ __forceinline__ void stats_dispatch_scale(const StatsParams& P, const
 }
 
 template <int DT, int PASS>
-__global__ void __launch_bounds__(kStatsThreads) grad_stats_kernel(const __grid_constant__ StatsParams P) {
+__global__ void __launch_bounds__(kStatsThreads, 4) grad_stats_kernel(const __grid_constant__ StatsParams P) {
   __shared__ double red_d[kStatsThreads / 32];
   __shared__ float red_f[kStatsThreads / 32];
   __shared__ unsigned red_u[kStatsThreads / 32];
