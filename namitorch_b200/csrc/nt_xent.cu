@@ -449,261 +449,6 @@ __global__ void __launch_bounds__(THREADS) xent_kernel(const __grid_constant__ X
   }
 }
 
-// ---------------------------------------------------------------------------------------------
-// Streaming variant (default for 16-byte aligned tensors): no shared-memory staging. Pass A
-// reads the row from HBM with kStreamUnroll independent 16-byte loads per thread in flight;
-// pass B reads it again, from L2 (the row was fetched a few microseconds earlier and the
-// streaming gradient stores do not displace it), so HBM traffic stays one read of the
-// logits and one write of the gradient, and no copy latency is exposed at row boundaries.
-// ---------------------------------------------------------------------------------------------
-constexpr int kStreamThreads = 512;
-constexpr int kStreamUnroll = 2;
-
-template <int DT, bool WEIGHTED>
-__global__ void __launch_bounds__(kStreamThreads, 2) xent_stream_kernel(const __grid_constant__ XentParams P) {
-  __shared__ float red_m[2][kStreamThreads / 32];
-  __shared__ float red_s[2][kStreamThreads / 32];
-  __shared__ double red_d[kStreamThreads / 32];
-  __shared__ bool last;
-
-  constexpr int ES = DT == NT_F32 ? 4 : 2;
-  constexpr int EPV = 16 / ES;
-  constexpr int T = kStreamThreads;
-  const int V = (int)P.classes;
-  const nt_xent_info* info = P.info;
-  const bool mean = P.reduction == NT_REDUCTION_MEAN;
-  const double D = mean ? info->denominator : 1.0;
-  const bool zero_all = mean && D == 0.0;
-  const double W = info->weight_sum;
-  const float inv_den = zero_all ? 0.0f : (float)(1.0 / D);
-  const float e = P.smoothing;
-  const bool smooth = e != 0.0f;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-
-  int parity = 0;
-  for (int64_t row = blockIdx.x; row < P.rows; row += gridDim.x, parity ^= 1) {
-    const int64_t t64 = P.targets[row];
-    const bool valid = t64 != P.ignore && t64 >= 0 && t64 < V;
-    const int t = valid ? (int)t64 : -1;
-    const int64_t row_base = row * (int64_t)V;
-    const uintptr_t start = reinterpret_cast<uintptr_t>(P.logits) + (uintptr_t)(row_base * ES);
-    const uint4* vec = reinterpret_cast<const uint4*>(start & ~(uintptr_t)15);
-    const int head = (int)(start & 15u);
-    const int span = head + V * ES;
-    const int nvec = (span + 15) >> 4;
-    const int full_lo = head ? 1 : 0;
-    const int full_hi = span >> 4;
-    const int nedge = full_lo + ((full_hi < nvec && full_hi >= full_lo) ? 1 : 0);
-
-    // ---- pass A: online max / sum of exp; NaN and +inf show up as a NaN sum ----
-    float m = -INFINITY, s = 0.0f;
-    double swx = 0.0;
-    auto accumulate = [&](const float* x, int j0, bool edge) {
-      float vmax = x[0];
-#pragma unroll
-      for (int q = 1; q < EPV; ++q) vmax = fmaxf(vmax, x[q]);
-      if (vmax > m) {
-        s = m > -INFINITY ? s * ex2((m - vmax) * kLog2e) : 0.0f;
-        m = vmax;
-      }
-      if (m > -INFINITY) {
-        const float sh = m * kLog2e;
-#pragma unroll
-        for (int q = 0; q < EPV; ++q) s += ex2(fmaf(x[q], kLog2e, -sh));
-      } else {
-#pragma unroll
-        for (int q = 0; q < EPV; ++q) if (x[q] != x[q]) s = x[q];  // NaN in an all -inf prefix
-      }
-      if (smooth) {
-#pragma unroll
-        for (int q = 0; q < EPV; ++q) {
-          const int j = j0 + q;
-          if (!edge || (j >= 0 && j < V)) swx += WEIGHTED ? (double)P.weight[j] * (double)x[q] : (double)x[q];
-        }
-      }
-    };
-    for (int k0 = full_lo + threadIdx.x; k0 < full_hi; k0 += T * kStreamUnroll) {
-      uint4 raw[kStreamUnroll];
-#pragma unroll
-      for (int u = 0; u < kStreamUnroll; ++u)
-        if (k0 + u * T < full_hi) raw[u] = __ldcg(vec + k0 + u * T);
-#pragma unroll
-      for (int u = 0; u < kStreamUnroll; ++u) {
-        const int k = k0 + u * T;
-        if (k < full_hi) {
-          float x[EPV];
-          unpack16<DT>(raw[u], x);
-          accumulate(x, (k * 16 - head) / ES, false);
-        }
-      }
-    }
-    if ((int)threadIdx.x < nedge) {
-      const int k = (threadIdx.x == 0 && full_lo) ? 0 : full_hi;
-      const int j0 = (k * 16 - head) / ES;
-      float x[EPV];
-#pragma unroll
-      for (int q = 0; q < EPV; ++q) {
-        const int j = j0 + q;
-        x[q] = (j >= 0 && j < V) ? load1<DT>(P.logits, row_base + j) : -INFINITY;
-      }
-      accumulate(x, j0, true);
-    }
-    // Merge the (max, sum) pairs in a fixed order; scratch alternates between rows.
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-      const float mm = fmaxf(m, m2);
-      s = mm > -INFINITY ? (m > -INFINITY ? s * ex2((m - mm) * kLog2e) : s) +
-                               (m2 > -INFINITY ? s2 * ex2((m2 - mm) * kLog2e) : s2)
-                         : s + s2;
-      m = mm;
-    }
-    if (lane == 0) { red_m[parity][warp] = m; red_s[parity][warp] = s; }
-    __syncthreads();
-    float M = -INFINITY;
-#pragma unroll 4
-    for (int w = 0; w < T / 32; ++w) M = fmaxf(M, red_m[parity][w]);
-    float S = 0.0f;
-#pragma unroll 4
-    for (int w = 0; w < T / 32; ++w) {
-      const float mw = red_m[parity][w];
-      S += (M > -INFINITY && mw > -INFINITY) ? red_s[parity][w] * ex2((mw - M) * kLog2e) : red_s[parity][w];
-    }
-    if (smooth) swx = block_reduce(swx, red_d, SumOp(), 0.0);
-    const bool bad_row = M == INFINITY || S != S;
-    const bool neg_row = !bad_row && M == -INFINITY;
-
-    // ---- row loss and gradient coefficients: d_c = e_c * A - G_c, minus B at c == t ----
-    const float wt = valid ? (WEIGHTED ? P.weight[t] : 1.0f) : 0.0f;
-    int mode = 0;
-    float loss_i = 0.0f, A = 0.0f, B = 0.0f, G = 0.0f;
-    if (valid && !zero_all) {
-      if (bad_row) {
-        mode = 1;
-        loss_i = __int_as_float(0x7fc00000);
-      } else if (neg_row) {
-        loss_i = INFINITY;
-      } else {
-        mode = 2;
-        const float xt = load1<DT>(P.logits, row_base + t);
-        const float lse = M + logf(S);
-        const float base = -wt * (xt - lse);
-        if (smooth) {
-          const double sm = -(swx - (double)lse * W) / (double)V;
-          loss_i = (1.0f - e) * base + e * (float)sm;
-        } else {
-          loss_i = base;
-        }
-        const float a_coef = WEIGHTED ? ((1.0f - e) * wt + (float)((double)e * W / (double)V)) * inv_den : inv_den;
-        A = a_coef / S;
-        B = (1.0f - e) * wt * inv_den;
-        G = smooth ? (float)((double)e / (double)V) * inv_den : 0.0f;
-      }
-    }
-    if (threadIdx.x == 0) P.row_loss[row] = loss_i;
-
-    // ---- pass B: gradient; the row comes back from L2 ----
-    if (P.dl != nullptr) {
-      const uintptr_t out_start = reinterpret_cast<uintptr_t>(P.dl) + (uintptr_t)(row_base * ES);
-      uint4* ovec = reinterpret_cast<uint4*>(out_start & ~(uintptr_t)15);
-      const bool vec_out = (int)(out_start & 15u) == head;
-      const float shM = M * kLog2e;
-      // 16-bit outputs: A folded into the exponent (one FFMA + one exp2 per element);
-      // float32 outputs keep the separate multiply for full float32 accuracy.
-      const float fold = DT == NT_F32 ? -shM : log2f(A) - shM;
-      const int kt = valid ? ((head + t * ES) >> 4) : -1;
-      const int lane_t = valid ? (((head + t * ES) & 15) / ES) : 0;
-      const float nanv = __int_as_float(0x7fc00000);
-      auto gradient = [&](const float* x, int j0, int k, float* d) {
-        if (mode == 2) {
-#pragma unroll
-          for (int q = 0; q < EPV; ++q) {
-            const float g = WEIGHTED ? G * ((j0 + q >= 0 && j0 + q < V) ? P.weight[j0 + q] : 0.0f) : G;
-            const float ex = ex2(fmaf(x[q], kLog2e, fold));
-            d[q] = DT == NT_F32 ? fmaf(ex, A, -g) : ex - g;
-          }
-          if (k == kt) {
-            // The target keeps the unfolded form: p_t * a - b cancels when p_t is near 1.
-#pragma unroll
-            for (int q = 0; q < EPV; ++q) {
-              if (q == lane_t) {
-                const float g = WEIGHTED ? G * P.weight[t] : G;
-                d[q] = fmaf(ex2(fmaf(x[q], kLog2e, -shM)), A, -(B + g));
-              }
-            }
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < EPV; ++q) d[q] = mode == 1 ? nanv : 0.0f;
-        }
-      };
-      auto store_scalar = [&](int j0, const float* d) {
-#pragma unroll
-        for (int q = 0; q < EPV; ++q) {
-          const int j = j0 + q;
-          if (j >= 0 && j < V) store1<DT>(P.dl, row_base + j, d[q]);
-        }
-      };
-      for (int k0 = full_lo + threadIdx.x; k0 < full_hi; k0 += T * kStreamUnroll) {
-        uint4 raw[kStreamUnroll];
-#pragma unroll
-        for (int u = 0; u < kStreamUnroll; ++u)
-          if (mode == 2 && k0 + u * T < full_hi) raw[u] = __ldcg(vec + k0 + u * T);
-#pragma unroll
-        for (int u = 0; u < kStreamUnroll; ++u) {
-          const int k = k0 + u * T;
-          if (k < full_hi) {
-            const int j0 = (k * 16 - head) / ES;
-            float x[EPV], d[EPV];
-            if (mode == 2) unpack16<DT>(raw[u], x);
-            gradient(x, j0, k, d);
-            if (vec_out) __stcs(ovec + k, pack16<DT>(d));
-            else store_scalar(j0, d);
-          }
-        }
-      }
-      if ((int)threadIdx.x < nedge) {
-        const int k = (threadIdx.x == 0 && full_lo) ? 0 : full_hi;
-        const int j0 = (k * 16 - head) / ES;
-        float x[EPV], d[EPV];
-#pragma unroll
-        for (int q = 0; q < EPV; ++q) {
-          const int j = j0 + q;
-          x[q] = (j >= 0 && j < V) ? load1<DT>(P.logits, row_base + j) : -INFINITY;
-        }
-        gradient(x, j0, k, d);
-        store_scalar(j0, d);
-      }
-    }
-  }
-
-  // Loss reduction over rows, in a fixed order, by the last block.
-  if (P.reduction == NT_REDUCTION_NONE) return;
-  if (!last_block_ticket(&P.ws->counter, &last)) return;
-  double acc = 0.0;
-  for (int64_t r = threadIdx.x; r < P.rows; r += T) acc += (double)P.row_loss[r];
-  acc = block_reduce(acc, red_d, SumOp(), 0.0);
-  if (threadIdx.x == 0) {
-    P.info->loss_sum = acc;
-    P.loss[0] = zero_all ? 0.0f : (float)(mean ? acc / D : acc);
-    P.ws->counter = 0u;
-  }
-}
-
-template <int DT, bool WEIGHTED>
-static int launch_stream(const XentParams& P, cudaStream_t stream) {
-  auto kernel = xent_stream_kernel<DT, WEIGHTED>;
-  int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kStreamThreads, 0) != cudaSuccess || per_sm < 1)
-    per_sm = 1;
-  int64_t grid = (int64_t)current_sm_count() * per_sm;
-  if (grid > P.rows) grid = P.rows;
-  if (grid < 1) grid = 1;
-  kernel<<<(unsigned)grid, kStreamThreads, 0, stream>>>(P);
-  return launch_status("nt_softmax_xent launch");
-}
-
 // Upstream-gradient multiply for the autograd backward.
 template <int DT>
 __global__ void __launch_bounds__(256) xent_scale_kernel(void* dl, int64_t rows, int64_t classes,
@@ -745,20 +490,17 @@ static int launch_xent(const XentParams& P0, cudaStream_t stream) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   const size_t budget = (size_t)max_optin > 4096 ? (size_t)max_optin - 4096 : 0;
-  // Preferred: two CTAs per SM, each with one staged row, so one CTA's copy overlaps the
-  // other's compute. Rows too large for that: one CTA per SM with two buffers.
+  // Each CTA stages one row; where two buffers fit on an SM (bf16 / fp16 rows up to
+  // ~56K classes) two CTAs share it and one's copy overlaps the other's compute.
   int sm_smem = 0;
   cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-  if (P.staged && 2 * (stride + 4096) <= (size_t)sm_smem && stride <= budget)
-    return launch_variant<DT, 1, WEIGHTED, 512>(P, stride, stream);
-  if (P.staged && 2 * stride <= budget) return launch_variant<DT, 2, WEIGHTED, 1024>(P, 2 * stride, stream);
+  (void)sm_smem;
   if (P.staged && stride <= budget) return launch_variant<DT, 1, WEIGHTED, 512>(P, stride, stream);
   return launch_variant<DT, 0, WEIGHTED, 512>(P, 0, stream);
 }
 
 template <int DT>
 static int launch_xent_dt(const XentParams& P, cudaStream_t stream) {
-  if (P.staged) return P.weight ? launch_stream<DT, true>(P, stream) : launch_stream<DT, false>(P, stream);
   return P.weight ? launch_xent<DT, true>(P, stream) : launch_xent<DT, false>(P, stream);
 }
 
