@@ -275,12 +275,15 @@ def run_ours(args):
     loss = torch.ones((), device=device)
     stream = torch.cuda.current_stream()
     ev = []
+    phases = []   # ZeRO-1: the optimizer's own events (reduce-scatter, stats, update, all-gather tail)
 
     def step(record=False):
         scaler.scale(loss)
         if record:
             e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
             e[0].record(stream)
+            if world > 1:
+                opt.timing = True
         scaler.unscale_(opt)
         clip_grad_norm_(params, 1.0)
         if record:
@@ -289,6 +292,9 @@ def run_ours(args):
         if record:
             e[2].record(stream)
             ev.append(e)
+            if world > 1:
+                phases.append(list(opt.last_events))
+                opt.timing = False
         scaler.update()
 
     for _ in range(args.warmup):
@@ -317,11 +323,21 @@ def run_ours(args):
     ms = start.elapsed_time(end) / args.steps
     stats_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
     update_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
-    breakdown = getattr(opt, "last_breakdown", None)
+    breakdown = None
     if world > 1:
-        t = torch.tensor([ms, update_ms, stats_ms], dtype=torch.float64, device=device)
+        # Events: [rs start, rs end, update start, updates issued on the main stream,
+        # all-gathers done, end]; each phase is averaged over the timed steps.
+        def span(a, b):
+            return statistics.mean(e[a].elapsed_time(e[b]) for e in phases)
+        rs_ms, gstats_ms, upd_ms, ag_tail_ms = span(0, 1), span(1, 2), span(2, 3), span(3, 4)
+        t = torch.tensor([ms, update_ms, stats_ms, rs_ms, gstats_ms, upd_ms, ag_tail_ms], dtype=torch.float64,
+                         device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, update_ms, stats_ms = t.tolist()
+        ms, update_ms, stats_ms, rs_ms, gstats_ms, upd_ms, ag_tail_ms = t.tolist()
+        breakdown = {"reduce_scatter": rs_ms, "global_stats": gstats_ms,
+                     "update_with_overlapped_all_gather": upd_ms, "all_gather_tail": ag_tail_ms,
+                     "pieces": opt._pieces}
+        update_ms = upd_ms   # the update kernels alone (all-gathers overlap them on the side stream)
     peak, peak_kind = measured_peak()
     shard = P / world
     result = {
@@ -346,6 +362,12 @@ def run_ours(args):
     }
     if breakdown:
         result["zero1_breakdown_ms"] = breakdown
+        # Reduce-scatter and all-gather each move (N-1)/N of the 2-byte gradient / model copy
+        # per GPU and direction; against the measured 770 GB/s peer copy per direction.
+        link_bytes = 2 * 2.0 * P * (world - 1) / world
+        result["nvlink"] = {"bytes_per_gpu_per_step": link_bytes, "peak_gbs_per_direction": 770.0,
+                            "floor_ms": link_bytes / 770e9 * 1e3,
+                            "frac_of_step": link_bytes / 770e9 * 1e3 / ms}
 
     if not args.no_e2e:
         result["e2e"] = e2e_ours(args, opt, scaler, params, flat_grads, loss, world)

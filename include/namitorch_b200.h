@@ -107,7 +107,9 @@ typedef struct nt_segment {
   int64_t count;         /* elements */
   int64_t chunk_begin;   /* first work chunk: prefix sum of ceil(count / chunk_elems) */
   int32_t group;         /* index into args.groups */
-  int32_t step_slot;     /* index into args.steps; each slot appears in at most one segment */
+  int32_t step_slot;     /* index into args.steps; each slot appears in at most one segment of a
+                            call. A negative value -k-1 reads counter k but leaves it for a later
+                            call (another piece of the same parameter) to advance. */
 } nt_segment;
 
 /* Per param-group coefficients, float32 exactly as the reference computes them

@@ -197,7 +197,8 @@ __global__ void __launch_bounds__(256) adamw_mt_kernel(const __grid_constant__ M
       seg = P.segs[s];
       next_begin = s + 1 < P.nseg ? P.segs[s + 1].chunk_begin : INT64_MAX;
       const nt_adamw_group& gr = P.groups[seg.group];
-      const int t = P.steps[seg.step_slot] + 1;
+      const int slot = seg.step_slot >= 0 ? seg.step_slot : -seg.step_slot - 1;
+      const int t = P.steps[slot] + 1;
       seg_ok = t > 0;
       if (!seg_ok && threadIdx.x == 0 && P.error) atomicOr(P.error, 1);
       // Steps past the table use its last row: the host only lets that happen once every
@@ -230,7 +231,10 @@ __global__ void __launch_bounds__(256) adamw_mt_kernel(const __grid_constant__ M
 
   // The last block advances the step counter of every updated segment.
   if (last_block_ticket(P.counter, &last)) {
-    for (int i = threadIdx.x; i < P.nseg; i += blockDim.x) P.steps[P.segs[i].step_slot] += 1;
+    for (int i = threadIdx.x; i < P.nseg; i += blockDim.x) {
+      const int slot = P.segs[i].step_slot;
+      if (slot >= 0) P.steps[slot] += 1;  // negative: another launch advances this counter
+    }
     __syncthreads();
     if (threadIdx.x == 0) *P.counter = 0u;
   }

@@ -2,24 +2,26 @@
 
 The reference has no distributed code; this extends its AdamW API (namitorch/optim/adam.py)
 with optimizer-state sharding. Every rank builds the same flat layout of all parameters
-(64-element aligned segments, total padded to a multiple of 64 * world). Rank r owns the
-contiguous shard [r*S, (r+1)*S) of that layout:
+(64-element aligned segments). The layout is cut into K pieces ("super-chunks") of N*c
+elements; rank r owns slot r of every piece, i.e. the K ranges
+[j*N*c + r*c, j*N*c + (r+1)*c). That ownership makes every piece contiguous across the
+ranks, so both collectives run per piece on contiguous slices, in place:
 
 * every rank holds the full low-precision model copy (the parameters' storage) and the full
   gradient buffer (the parameters' ``.grad`` views), both in ``model_dtype``;
-* rank r holds only its shard of the fp32 master weights, exp_avg and exp_avg_sq.
+* rank r holds only its K*c elements of the fp32 master weights, exp_avg and exp_avg_sq.
 
 One step:
-1. reduce-scatter the gradient buffer (NCCL, average over ranks) into the rank's shard;
-2. one statistics kernel over the shard, then one all-reduce (SUM) of the 24-byte record
-   {sum g^2, #non-finite, #NaN} (plus a MAX of max|g| for a non-2 norm), and a one-thread
-   finalize kernel — every rank then holds the same found_inf and global norm;
-3. the fused AdamW kernel over the shard's parameter pieces (unscale, skip, clip, update),
-   writing the updated bf16 values into the rank's slice of the model copy;
-4. all-gather of the model copy in place.
+1. reduce-scatter of every piece of the gradient buffer (NCCL, average over ranks);
+2. one statistics kernel over the rank's gradient shard, one all-reduce (SUM) of the
+   24-byte record {sum g^2, #non-finite, #NaN} (plus a MAX of max|g| for a non-2 norm) and a
+   one-thread finalize kernel: every rank then holds the same found_inf and global norm;
+3. per piece: the fused AdamW kernel over the piece's parameter segments (unscale, skip,
+   clip, update, bf16 cast-out into the rank's slice of the model copy), after which the
+   piece's all-gather runs on a side stream while the next piece is updated.
 
-Steps 2-4 use the same C ABI entry points as the single-GPU path; a parameter cut by a
-shard boundary is simply two segments on two ranks that share the same step counter value.
+A parameter cut by a piece or rank boundary is several segments; only its last segment on a
+rank advances its step counter (a negative step slot marks the others).
 """
 from __future__ import annotations
 
@@ -38,20 +40,31 @@ _MAXABS = N.STATS_FIELDS.index("maxabs")
 _POWSUM = N.STATS_FIELDS.index("powsum")
 
 
-def shard_bounds(total: int, world: int, rank: int) -> tuple[int, int]:
-    """[start, stop) of rank's shard of a layout of ``total`` elements (a multiple of world)."""
-    size = total // world
-    return rank * size, (rank + 1) * size
+DEFAULT_PIECES = 8
 
 
-def shard_pieces(offsets: list[int], numels: list[int], start: int, stop: int) -> list[tuple[int, int, int]]:
-    """(parameter index, offset within the shard, count) of every parameter piece in [start, stop)."""
-    pieces = []
-    for i, (off, n) in enumerate(zip(offsets, numels)):
-        lo, hi = max(off, start), min(off + n, stop)
-        if lo < hi:
-            pieces.append((i, lo - start, hi - lo))
-    return pieces
+def interleaved_layout(numels: list[int], world: int, pieces: int = DEFAULT_PIECES):
+    """(offsets, total, c): 64-aligned offsets of every tensor and the piece slot length c,
+    with total = pieces * world * c."""
+    base = FlatLayout.build(numels)
+    c = round_up(-(-base.total // (pieces * world)), ALIGN)
+    return base.offsets, pieces * world * c, c
+
+
+def owned_ranges(world: int, rank: int, pieces: int, c: int) -> list[tuple[int, int, int]]:
+    """(global start, global stop, local start) of every range rank owns."""
+    return [(j * world * c + rank * c, j * world * c + (rank + 1) * c, j * c) for j in range(pieces)]
+
+
+def shard_pieces(offsets: list[int], numels: list[int], ranges) -> list[tuple[int, int, int, int]]:
+    """(parameter index, offset in the rank's shard, count, piece) of every owned parameter piece."""
+    out = []
+    for j, (start, stop, local) in enumerate(ranges):
+        for i, (off, n) in enumerate(zip(offsets, numels)):
+            lo, hi = max(off, start), min(off + n, stop)
+            if lo < hi:
+                out.append((i, local + lo - start, hi - lo, j))
+    return out
 
 
 class CudaShardKernels:
@@ -118,11 +131,16 @@ class ZeroAdamW(_FirstOrderAdam):
 
     def __init__(self, params, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 1e-2,
                  *, maximize: bool = False, model_dtype=torch.bfloat16, process_group=None, average_grads: bool = True,
-                 _kernels=None):
+                 pieces: int = DEFAULT_PIECES, _kernels=None):
         if model_dtype not in (torch.bfloat16, torch.float16, torch.float32):
             raise TypeError("model_dtype must be torch.bfloat16, torch.float16 or torch.float32.")
         self._group = process_group
         self._average = average_grads
+        if type(pieces) is not int or pieces < 1:
+            raise ValueError("pieces must be a positive integer.")
+        self._pieces = pieces
+        self.timing = False
+        self.last_events: list | None = None
         self._kernels = _kernels
         self._copy_dtype = model_dtype
         super().__init__(params, {"lr": lr, "betas": betas, "eps": eps, "weight_decay": weight_decay,
@@ -147,20 +165,21 @@ class ZeroAdamW(_FirstOrderAdam):
         self.device = device
         self.params_list = params
         self.index = {id(p): i for i, p in enumerate(params)}
-        base = FlatLayout.build([p.numel() for p in params])
-        total = round_up(base.total, ALIGN * self.world)
-        self.layout = FlatLayout(base.numels, base.offsets, total)
-        self.shard_start, self.shard_stop = shard_bounds(total, self.world, self.rank)
-        shard = self.shard_stop - self.shard_start
-        self.pieces = shard_pieces(base.offsets, base.numels, self.shard_start, self.shard_stop)
+        numels = [p.numel() for p in params]
+        offsets, total, c = interleaved_layout(numels, self.world, self._pieces)
+        self.layout = FlatLayout(numels, offsets, total)
+        self.piece_len = c
+        self.ranges = owned_ranges(self.world, self.rank, self._pieces, c)
+        shard = self._pieces * c
+        self.pieces = shard_pieces(offsets, numels, self.ranges)
         with torch.no_grad():
             self.copy = torch.zeros(total, dtype=self._copy_dtype, device=device)
             self.flat_grads = torch.zeros(total, dtype=self._copy_dtype, device=device)
             self.grad_shard = torch.zeros(shard, dtype=self._copy_dtype, device=device)
             self.master = torch.zeros(shard, dtype=torch.float32, device=device)
-            for i, off, n in self.pieces:
+            for i, off, n, j in self.pieces:
                 src = params[i].detach().reshape(-1)
-                lo = self.shard_start + off - self.layout.offsets[i]
+                lo = self._global(off) - self.layout.offsets[i]
                 self.master[off:off + n].copy_(src[lo:lo + n])
             for p, off in zip(params, self.layout.offsets):
                 view = self.copy[off:off + p.numel()].view(p.shape)
@@ -174,9 +193,27 @@ class ZeroAdamW(_FirstOrderAdam):
         self.corrections = CorrectionTable(device)
         self.max_step = 0
         self._reduced = False
-        self._segments_key = None
+        self._tables = None
+        self._side = torch.cuda.Stream(device) if device.type == "cuda" else None
         for p in params:
             _OWNERS[id(p)] = self
+
+    def _global(self, local: int) -> int:
+        """Global flat offset of an element of the rank's shard."""
+        j, r = divmod(local, self.piece_len)
+        return j * self.world * self.piece_len + self.rank * self.piece_len + r
+
+    def _piece_slices(self, j: int):
+        n, c = self.world, self.piece_len
+        full = slice(j * n * c, (j + 1) * n * c)
+        mine = slice(j * n * c + self.rank * c, j * n * c + (self.rank + 1) * c)
+        return full, mine
+
+    def _event(self):
+        if self.timing and self.device.type == "cuda":
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.last_events.append(e)
 
     def _ensure_engine(self):
         return self
@@ -214,8 +251,16 @@ class ZeroAdamW(_FirstOrderAdam):
         if self._reduced:
             return
         self._adopt_foreign_grads()
+        if self.timing:
+            self.last_events = []
+        self._event()
         op = dist.ReduceOp.AVG if self._average else dist.ReduceOp.SUM
-        dist.reduce_scatter_tensor(self.grad_shard, self.flat_grads, op=op, group=self._group)
+        c = self.piece_len
+        for j in range(self._pieces):
+            full, _ = self._piece_slices(j)
+            dist.reduce_scatter_tensor(self.grad_shard[j * c:(j + 1) * c], self.flat_grads[full], op=op,
+                                       group=self._group)
+        self._event()
         self._reduced = True
 
     def _global_stats(self, scale, norm_type: float) -> torch.Tensor:
@@ -301,36 +346,78 @@ class ZeroAdamW(_FirstOrderAdam):
         if len(used) > N.NT_MAX_GROUPS:
             raise RuntimeError(f"ZeroAdamW supports at most {N.NT_MAX_GROUPS} parameter groups.")
         local = {gi: k for k, gi in enumerate(used)}
+        structs = [self._group_struct(options[gi]) for gi in used]
+        self.corrections.ensure(self.max_step + 1)
+        tables = self._piece_tables(local)
+        self._event()
+        cuda = self.device.type == "cuda"
+        main = torch.cuda.current_stream(self.device) if cuda else None
+        if cuda:
+            self._side.wait_stream(main)
+        for j in range(self._pieces):
+            table = tables[j]
+            if table is not None:
+                segs, nseg, nchunks = table
+                self._kernels.update(
+                    master=self.master, exp_avg=self.exp_avg, exp_avg_sq=self.exp_avg_sq, copy=self._copy_base(j),
+                    grad_dtype=self.grad_shard.dtype, segments=segs, num_segments=nseg, num_chunks=nchunks,
+                    steps=self.steps, corrections=self.corrections.tensor, capacity=self.corrections.capacity,
+                    scale=None if amp is None else amp.scale, stats=None if amp is None else amp.stats,
+                    skip=bool(amp is not None and amp.skip), max_norm=None if amp is None else amp.max_norm,
+                    groups=structs)
+            full, mine = self._piece_slices(j)
+            if cuda:
+                # The piece's all-gather overlaps the next piece's update.
+                self._side.wait_stream(main)
+                with torch.cuda.stream(self._side):
+                    dist.all_gather_into_tensor(self.copy[full], self.copy[mine], group=self._group)
+            else:
+                dist.all_gather_into_tensor(self.copy[full], self.copy[mine], group=self._group)
+        self._event()
+        if cuda:
+            main.wait_stream(self._side)
+        if not self.pieces:
+            # A rank whose shard holds no parameter still advances the shared step counters.
+            self._advance_steps_without_update(amp)
+        self._event()
+        self._reduced = False
+        self.max_step += 1
+        return loss
+
+    def _copy_base(self, j: int) -> torch.Tensor:
+        """The model copy as the kernel addresses it for piece j: the kernel writes element
+        `local` (shard offset, in [j*c, (j+1)*c)) at base + local, and that element's global
+        position is local + j*(N-1)*c + r*c."""
+        return self.copy[j * (self.world - 1) * self.piece_len + self.rank * self.piece_len:]
+
+    def _piece_tables(self, local_group):
+        """One segment table per piece; the copy pointer offset is folded into each segment."""
+        key = (tuple(local_group.items()),)
+        if self._tables is not None and self._tables[0] == key:
+            return self._tables[1]
         group_of = {}
         for gi, group in enumerate(self.param_groups):
             for p in group["params"]:
                 group_of[self.index[id(p)]] = gi
-        structs = [self._group_struct(options[gi]) for gi in used]
-        self.corrections.ensure(self.max_step + 1)
-        rows = [(self.grad_shard.data_ptr() + off * self.grad_shard.element_size(), off, n,
-                 local[group_of[i]], i) for i, off, n in self.pieces]
-        if rows:
-            key = tuple(rows)
-            if key != self._segments_key:
-                table, nchunks = segment_table(rows, CHUNK)
-                self._segments = upload(table, self.device)
-                self._num_chunks = nchunks
-                self._segments_key = key
-            copy_shard = self.copy[self.shard_start:self.shard_stop]
-            self._kernels.update(
-                master=self.master, exp_avg=self.exp_avg, exp_avg_sq=self.exp_avg_sq, copy=copy_shard,
-                grad_dtype=self.grad_shard.dtype, segments=self._segments, num_segments=len(rows),
-                num_chunks=self._num_chunks, steps=self.steps, corrections=self.corrections.tensor,
-                capacity=self.corrections.capacity, scale=None if amp is None else amp.scale,
-                stats=None if amp is None else amp.stats, skip=bool(amp is not None and amp.skip),
-                max_norm=None if amp is None else amp.max_norm, groups=structs)
-        else:
-            # A rank whose shard holds no parameter still advances the shared step counters.
-            self._advance_steps_without_update(amp)
-        dist.all_gather_into_tensor(self.copy, self.copy[self.shard_start:self.shard_stop], group=self._group)
-        self._reduced = False
-        self.max_step += 1
-        return loss
+        last_piece = {}
+        for i, off, n, j in self.pieces:
+            last_piece[i] = max(last_piece.get(i, -1), j)
+        esize = self.grad_shard.element_size()
+        tables = []
+        for j in range(self._pieces):
+            rows = []
+            for i, off, n, jj in self.pieces:
+                if jj != j:
+                    continue
+                slot = i if last_piece[i] == j else -i - 1
+                rows.append((self.grad_shard.data_ptr() + off * esize, off, n, local_group[group_of[i]], slot))
+            if not rows:
+                tables.append(None)
+                continue
+            table, nchunks = segment_table(rows, CHUNK)
+            tables.append((upload(table, self.device), len(rows), nchunks))
+        self._tables = (key, tables)
+        return tables
 
     def _advance_steps_without_update(self, amp):
         if amp is not None and amp.skip:
@@ -353,9 +440,11 @@ class ZeroAdamW(_FirstOrderAdam):
 
     # ---- state ----------------------------------------------------------------------------------
     def _gather_shards(self, shard: torch.Tensor) -> torch.Tensor:
-        full = torch.empty(self.layout.total, dtype=shard.dtype, device=shard.device)
-        dist.all_gather_into_tensor(full, shard, group=self._group)
-        return full
+        """Every rank's shard, reassembled in the global (interleaved) layout."""
+        gathered = torch.empty(self.layout.total, dtype=shard.dtype, device=shard.device)
+        dist.all_gather_into_tensor(gathered, shard, group=self._group)
+        # gathered is [rank][piece][c]; the layout is [piece][rank][c].
+        return gathered.view(self.world, self._pieces, self.piece_len).transpose(0, 1).reshape(-1)
 
     def _state_by_id(self):
         exported = self._full_state()
@@ -410,15 +499,18 @@ class ZeroAdamW(_FirstOrderAdam):
                     src = values[name]
                     src = torch.from_numpy(src) if isinstance(src, np.ndarray) else src
                     src = src.detach().reshape(-1).to(device=self.device, dtype=torch.float32)
-                    for j, off, n in self.pieces:
-                        if j == i:
-                            lo = self.shard_start + off - self.layout.offsets[i]
+                    for k, off, n, j in self.pieces:
+                        if k == i:
+                            lo = self._global(off) - self.layout.offsets[i]
                             arena[off:off + n].copy_(src[lo:lo + n])
             self.steps.copy_(torch.tensor(steps, dtype=torch.int32))
             # The model copy follows the (possibly restored) masters.
-            for i, off, n in self.pieces:
-                self.copy[self.shard_start + off:self.shard_start + off + n].copy_(self.master[off:off + n])
-        dist.all_gather_into_tensor(self.copy, self.copy[self.shard_start:self.shard_stop].clone(), group=self._group)
+            for k, off, n, j in self.pieces:
+                g = self._global(off)
+                self.copy[g:g + n].copy_(self.master[off:off + n])
+        for j in range(self._pieces):
+            full, mine = self._piece_slices(j)
+            dist.all_gather_into_tensor(self.copy[full], self.copy[mine].clone(), group=self._group)
         self.max_step = max(steps) if steps else 0
 
     @property

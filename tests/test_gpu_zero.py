@@ -51,8 +51,7 @@ def _worker(rank, world, port, out_path):
                 p.grad.copy_(torch.from_numpy(g).to(torch.bfloat16))
             local.append(opt.flat_grads.float().cpu().numpy())
             opt._reduce()
-            full = torch.empty(opt.layout.total, dtype=torch.bfloat16, device="cuda")
-            dist.all_gather_into_tensor(full, opt.grad_shard)
+            full = opt._gather_shards(opt.grad_shard)   # global (interleaved-piece) order
             reduced.append(full.float().cpu().numpy())
             scaler.scale(torch.ones((), device="cuda"))
             scaler.unscale_(opt)
@@ -106,10 +105,12 @@ def test_zero1_nccl_matches_oracle(tmp_path):
     oracle = oadamw.OracleAdamW(params, [(decay, {**base, "weight_decay": 0.1}),
                                          (no_decay, {**base, "weight_decay": 0.0})])
     oscaler = oamp.OracleGradScaler(1024.0, 2.0, 0.5, 2)
+    shapes = [s for _, s in shape.shapes()]
     for step in range(4):
         flat = out["reduced"][step]
-        grads = [flat[o:o + n].reshape(s).astype(np.float32).copy()
-                 for o, n, (_, s) in zip(offsets, numels, shape.shapes())]
+        grads = [None] * len(shapes)
+        for k, orig in enumerate(order):   # flat-layout offsets follow the registration order
+            grads[orig] = flat[offsets[k]:offsets[k] + numels[orig]].reshape(shapes[orig]).astype(np.float32).copy()
         r = oamp.amp_step(oracle, oscaler, grads, max_norm=1.0)
         assert bool(out["stepped"][step]) == r["stepped"]
         if r["norm"] is not None:

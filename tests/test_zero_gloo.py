@@ -19,27 +19,28 @@ import torch.multiprocessing as mp
 
 from namitorch_b200 import _native as N
 from namitorch_b200.flat import SEGMENT_DTYPE
-from namitorch_b200.zero import shard_bounds, shard_pieces
+from namitorch_b200.zero import interleaved_layout, owned_ranges, shard_pieces
 
 SIZES = [(37, 5), (100,), (1000,), (7,), (64, 64), (3,)]
 
 
 def test_shard_partition_covers_every_element_once():
-    from namitorch_b200.flat import FlatLayout
     numels = [int(np.prod(s)) for s in SIZES]
-    base = FlatLayout.build(numels)
     for world in (1, 2, 3, 4, 8):
-        total = -(-base.total // (64 * world)) * 64 * world
-        covered = np.zeros(total, np.int32)
-        for rank in range(world):
-            start, stop = shard_bounds(total, world, rank)
-            assert stop - start == total // world and start % 64 == 0
-            for i, off, n in shard_pieces(base.offsets, numels, start, stop):
-                lo = start + off
-                assert base.offsets[i] <= lo and lo + n <= base.offsets[i] + numels[i]
-                covered[lo:lo + n] += 1
-        for off, n in zip(base.offsets, numels):
-            assert np.all(covered[off:off + n] == 1)
+        for pieces in (1, 3, 8):
+            offsets, total, c = interleaved_layout(numels, world, pieces)
+            assert total == pieces * world * c and c % 64 == 0
+            covered = np.zeros(total, np.int32)
+            for rank in range(world):
+                ranges = owned_ranges(world, rank, pieces, c)
+                assert [r[2] for r in ranges] == [j * c for j in range(pieces)]
+                for i, off, n, j in shard_pieces(offsets, numels, ranges):
+                    start, stop, local = ranges[j]
+                    lo = start + off - local
+                    assert offsets[i] <= lo and lo + n <= offsets[i] + numels[i] and lo + n <= stop
+                    covered[lo:lo + n] += 1
+            for off, n in zip(offsets, numels):
+                assert np.all(covered[off:off + n] == 1)
 
 
 class NumpyShardKernels:
@@ -115,7 +116,7 @@ class NumpyShardKernels:
             g = gshard[off:off + n]
             if coef is not None:
                 g = (g.astype(np.float64) * coef).astype(np.float32)
-            t = min(int(st[slot]) + 1, capacity - 1)
+            t = min(int(st[slot if slot >= 0 else -slot - 1]) + 1, capacity - 1)
             c1, c2 = corr[gr.correction_row, t]
             pp, mm, vv = p[off:off + n], m[off:off + n], v[off:off + n]
             mm[...] = f32(gr.beta1) * mm + f32(gr.one_minus_beta1) * g
@@ -124,8 +125,9 @@ class NumpyShardKernels:
             if gr.update_parameter:
                 base = pp * f32(gr.decay_factor) if gr.decay_mode == N.NT_DECAY_DECOUPLED else pp
                 pp[...] = base - f32(gr.lr) * u
-            st[slot] += 1
-        copy.copy_(master.to(copy.dtype))
+            if slot >= 0:   # a negative slot is advanced by the parameter's last piece
+                st[slot] += 1
+            copy[off:off + n].copy_(master[off:off + n].to(copy.dtype))
 
 
 def _free_port() -> int:
@@ -163,6 +165,28 @@ def _worker(rank, world, port, result_path):
         sd = opt.state_dict()
         copies = [p.detach().numpy().copy() for p in params]
         order = [0, 2, 4, 1, 3, 5]   # registration order: group by group
+        # Round trip: a fresh optimizer loaded from the gathered state takes the same 4th step.
+        params2 = [torch.nn.Parameter(torch.from_numpy(a.copy())) for a in arrays]
+        kernels2 = NumpyShardKernels()
+        groups2 = [{"params": [params2[i] for i in (0, 2, 4)], "weight_decay": 0.1},
+                   {"params": [params2[i] for i in (1, 3, 5)], "weight_decay": 0.0}]
+        opt2 = ZeroAdamW(groups2, lr=1e-2, model_dtype=torch.float32, average_grads=False, _kernels=kernels2)
+        kernels2.opt = opt2
+        opt2.load_state_dict(sd)
+        for k in range(len(params)):
+            np.testing.assert_array_equal(params2[k].detach().numpy(), copies[k])
+        for o, ps in ((opt, params), (opt2, params2)):
+            o.zero_grad()
+            for p, g in zip(ps, _rank_grads(rank, 3)):
+                p.grad.copy_(torch.from_numpy(g))
+            o.step()
+        sd_a, sd_b = opt.state_dict(), opt2.state_dict()
+        for k in sd_a["state"]:
+            assert sd_a["state"][k]["step"] == sd_b["state"][k]["step"] == 4
+            for name in ("exp_avg", "exp_avg_sq", "master_param"):
+                np.testing.assert_array_equal(sd_a["state"][k][name].numpy(), sd_b["state"][k][name].numpy())
+        for k in range(len(params)):
+            np.testing.assert_array_equal(params2[k].detach().numpy(), params[k].detach().numpy())
         if rank == 0:
             np.savez(result_path, norms=np.array(norms),
                      **{f"master{order[k]}": sd["state"][k]["master_param"].numpy() for k in sd["state"]},
