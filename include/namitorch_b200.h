@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define NT_ABI_VERSION 1
+#define NT_ABI_VERSION 2
 #define NT_MAX_GROUPS 32      /* coefficient groups per nt_adamw_mt call */
 #define NT_MAX_FOUND_INF 16   /* optimizers combined by one nt_scaler_update call */
 
@@ -255,6 +255,61 @@ int nt_grad_clip_value(const nt_span* spans, int32_t num_spans, int32_t chunk_el
 int nt_scaler_update(float* scale, int32_t* growth_tracker, const double* const* found_inf,
                      int32_t count, double growth_factor, double backoff_factor,
                      int32_t growth_interval, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* ZeRO-1 over peer memory (NVLink / NVSwitch)                                           */
+/* ------------------------------------------------------------------------------------ */
+/* The reference has no distributed code. These entry points run the two ZeRO-1 exchanges
+   inside the kernels that consume or produce the exchanged data, as loads and stores to
+   the other GPUs' memory: the gradient reduce-scatter inside the statistics pass, and the
+   model-copy all-gather inside the AdamW update. One process drives one GPU. Ordering
+   between the ranks (peers' gradients written before they are read, every push landed
+   before the copy is read) is the caller's: a stream-ordered barrier collective before
+   nt_zero_reduce_scatter_stats and after nt_adamw_mt_push. */
+#define NT_MAX_RANKS 8
+
+/* CUDA IPC export of a device buffer that may start inside a larger allocation: the
+   allocation's IPC handle and the byte offset of `ptr` inside it. */
+int nt_ipc_export(const void* ptr, unsigned char handle[64], uint64_t* offset);
+
+/* Maps an exported buffer of another process into this one, on the current device, with
+   peer access enabled lazily; *ptr = mapping + offset. */
+int nt_ipc_open(const unsigned char handle[64], uint64_t offset, void** ptr);
+
+/* Unmaps a pointer returned by nt_ipc_open. */
+int nt_ipc_close(void* ptr);
+
+/* *ok = 1 when the current device can load from and store to device `peer` directly. */
+int nt_can_access_peer(int32_t peer, int32_t* ok);
+
+typedef struct nt_zero_reduce_args {
+  const void* sources[NT_MAX_RANKS]; /* rank-ordered: rank q's gradients for this rank's shard
+                                        (the local buffer at this rank's index, peer mappings
+                                        elsewhere), all 16-byte aligned */
+  int32_t num_ranks;                 /* 1..NT_MAX_RANKS */
+  int32_t dtype;                     /* NT_F32 / NT_F16 / NT_BF16 */
+  int64_t count;                     /* shard elements */
+  int32_t average;                   /* 1: the sum is divided by num_ranks */
+  void* dest;                        /* reduced shard (same dtype, 16-byte aligned); with count 0
+                                        dest and sources may be NULL and only stats is written */
+  const float* scale;                /* device loss scale applied to the statistics, or NULL */
+  nt_stats* stats;                   /* device: sumsq, nonfinite, nan, maxabs of dest/scale */
+  void* workspace;                   /* nt_grad_stats_workspace_size() bytes, zero-filled once */
+  size_t workspace_bytes;
+} nt_zero_reduce_args;
+
+/* Reduce-scatter fused with the first statistics pass: dest[i] = dtype(sum over q in rank
+   order of f32(sources[q][i]), divided by num_ranks when averaging), and, in the same pass,
+   the pass-0 fields of nt_grad_stats over dest/scale. The norm and found_inf need the
+   other ranks' fields: sum-reduce (sumsq, nonfinite, nan), max-reduce maxabs, then call
+   nt_grad_stats_finalize. */
+int nt_zero_reduce_scatter_stats(const nt_zero_reduce_args* args, void* stream);
+
+/* nt_adamw_mt whose model-copy stores also go to `num_peers` (0..NT_MAX_RANKS-1) other
+   copies: element `offset` of a segment is written at model_copy + offset and at
+   peer_copies[k] + offset (same dtype), which fuses the ZeRO-1 all-gather of the model
+   copy into the update. `peer_copies` is a host array of device pointers. */
+int nt_adamw_mt_push(const nt_adamw_mt_args* args, void* const* peer_copies, int32_t num_peers, void* stream);
 
 /* ------------------------------------------------------------------------------------ */
 /* Fused softmax cross-entropy forward + backward                                        */

@@ -21,7 +21,8 @@ NT_REDUCTION_NONE, NT_REDUCTION_MEAN, NT_REDUCTION_SUM = 0, 1, 2
 NT_DECAY_NONE, NT_DECAY_DECOUPLED, NT_DECAY_COUPLED = 0, 1, 2
 NT_MAX_GROUPS = 32
 NT_MAX_FOUND_INF = 16
-ABI_VERSION = 1
+NT_MAX_RANKS = 8
+ABI_VERSION = 2
 
 
 class Segment(C.Structure):
@@ -84,6 +85,12 @@ class XentArgs(C.Structure):
                 ("workspace_bytes", C.c_size_t)]
 
 
+class ZeroReduceArgs(C.Structure):
+    _fields_ = [("sources", C.c_void_p * NT_MAX_RANKS), ("num_ranks", C.c_int32), ("dtype", C.c_int32),
+                ("count", C.c_int64), ("average", C.c_int32), ("dest", C.c_void_p), ("scale", C.c_void_p),
+                ("stats", C.c_void_p), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
+
+
 # name -> (restype, argtypes). Every symbol of include/namitorch_b200.h.
 SIGNATURES: dict[str, tuple] = {
     "nt_abi_version": (C.c_int, []),
@@ -114,6 +121,12 @@ SIGNATURES: dict[str, tuple] = {
                                      C.c_void_p]),
     "nt_scaler_update": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p), C.c_int32, C.c_double,
                                    C.c_double, C.c_int32, C.c_void_p]),
+    "nt_ipc_export": (C.c_int, [C.c_void_p, C.POINTER(C.c_ubyte), C.POINTER(C.c_uint64)]),
+    "nt_ipc_open": (C.c_int, [C.POINTER(C.c_ubyte), C.c_uint64, C.POINTER(C.c_void_p)]),
+    "nt_ipc_close": (C.c_int, [C.c_void_p]),
+    "nt_can_access_peer": (C.c_int, [C.c_int32, C.POINTER(C.c_int32)]),
+    "nt_zero_reduce_scatter_stats": (C.c_int, [C.POINTER(ZeroReduceArgs), C.c_void_p]),
+    "nt_adamw_mt_push": (C.c_int, [C.POINTER(AdamWMtArgs), C.POINTER(C.c_void_p), C.c_int32, C.c_void_p]),
     "nt_xent_workspace_size": (C.c_size_t, []),
     "nt_softmax_xent": (C.c_int, [C.POINTER(XentArgs), C.c_void_p]),
     "nt_xent_backward_scale": (C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_int64, C.c_void_p, C.c_int32,
@@ -169,7 +182,8 @@ def check(status: int, what: str = "") -> None:
 
 # Kernel launches issued per successful call of each launching entry point (for the
 # benchmark's launch count; the statistics entry point launches one kernel per call).
-LAUNCHES_PER_CALL = {"nt_adamw_f32": 1, "nt_adamw_mt": 1, "nt_grad_stats": 1, "nt_grad_stats_finalize": 1,
+LAUNCHES_PER_CALL = {"nt_adamw_f32": 1, "nt_adamw_mt": 1, "nt_adamw_mt_push": 1, "nt_zero_reduce_scatter_stats": 1,
+                     "nt_grad_stats": 1, "nt_grad_stats_finalize": 1,
                      "nt_grad_stats_noalloc": 2,
                      "nt_grad_transform": 1, "nt_grad_clip_value": 1, "nt_scaler_update": 1,
                      "nt_softmax_xent": 2, "nt_xent_backward_scale": 1, "nt_cast": 1}
@@ -196,3 +210,29 @@ def dtype_code(dtype) -> int:
     if dtype not in codes:
         raise TypeError(f"namitorch_b200 kernels support float32, float16 and bfloat16, got {dtype}.")
     return codes[dtype]
+
+
+def ipc_export(ptr: int) -> tuple[bytes, int]:
+    """(CUDA IPC handle of the allocation holding ``ptr``, byte offset of ``ptr`` in it)."""
+    handle = (C.c_ubyte * 64)()
+    offset = C.c_uint64()
+    call("nt_ipc_export", C.c_void_p(ptr), handle, C.byref(offset))
+    return bytes(handle), int(offset.value)
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """Maps another process's exported buffer on the current device; returns its address."""
+    buf = (C.c_ubyte * 64).from_buffer_copy(handle)
+    out = C.c_void_p()
+    call("nt_ipc_open", buf, C.c_uint64(offset), C.byref(out))
+    return int(out.value)
+
+
+def ipc_close(ptr: int) -> None:
+    call("nt_ipc_close", C.c_void_p(ptr))
+
+
+def can_access_peer(peer: int) -> bool:
+    ok = C.c_int32()
+    call("nt_can_access_peer", int(peer), C.byref(ok))
+    return bool(ok.value)

@@ -120,6 +120,8 @@ struct MtParams {
   unsigned* counter;
   int32_t* error;
   int ngroups;
+  int npeers;                        // other model copies the update also writes (ZeRO-1)
+  void* peers[NT_MAX_RANKS - 1];
   nt_adamw_group groups[NT_MAX_GROUPS];
 };
 
@@ -128,7 +130,31 @@ struct AdamwWorkspace {
   unsigned pad[63];
 };
 
-template <int GDT, int CDT>
+// Stores 8 updated parameters into the model copy and, with PUSH, into every peer's copy
+// at the same offset (the ZeRO-1 all-gather, as stores over NVLink).
+template <int CDT, bool PUSH>
+__device__ __forceinline__ void store_copy8(const MtParams& P, int64_t ai, const float v[8]) {
+  using T = typename Elem<CDT>::T;
+  uint4 raw;
+  T* h = reinterpret_cast<T*>(&raw);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) h[k] = Elem<CDT>::from_f32(v[k]);
+  __stcs(reinterpret_cast<uint4*>(static_cast<T*>(P.copy) + ai), raw);
+  if constexpr (PUSH) {
+#pragma unroll 1
+    for (int q = 0; q < P.npeers; ++q) __stcs(reinterpret_cast<uint4*>(static_cast<T*>(P.peers[q]) + ai), raw);
+  }
+}
+
+template <int CDT, bool PUSH>
+__device__ __forceinline__ void store_copy1(const MtParams& P, int64_t ai, float v) {
+  store1<CDT>(P.copy, ai, v);
+  if constexpr (PUSH) {
+    for (int q = 0; q < P.npeers; ++q) store1<CDT>(P.peers[q], ai, v);
+  }
+}
+
+template <int GDT, int CDT, bool PUSH>
 __device__ __forceinline__ void mt_vec8(const MtParams& P, int64_t ai, const void* g, int64_t gi,
                                         const Coef& c, const Unscale& un, bool clip, double coef) {
   float pv[8], mv[8], vv[8], gv[8];
@@ -146,11 +172,11 @@ __device__ __forceinline__ void mt_vec8(const MtParams& P, int64_t ai, const voi
   store8_f32(P.v + ai, vv);
   if (c.update) {
     store8_f32(P.p + ai, pv);
-    if constexpr (CDT != kNoCopy) store8<CDT>(P.copy, ai, pv);
+    if constexpr (CDT != kNoCopy) store_copy8<CDT, PUSH>(P, ai, pv);
   }
 }
 
-template <int GDT, int CDT>
+template <int GDT, int CDT, bool PUSH>
 __device__ __forceinline__ void mt_elem(const MtParams& P, int64_t ai, const void* g, int64_t gi,
                                         const Coef& c, const Unscale& un, bool clip, double coef) {
   float p = P.p[ai], m = P.m[ai], v = P.v[ai];
@@ -161,11 +187,11 @@ __device__ __forceinline__ void mt_elem(const MtParams& P, int64_t ai, const voi
   P.v[ai] = v;
   if (c.update) {
     P.p[ai] = p;
-    if constexpr (CDT != kNoCopy) store1<CDT>(P.copy, ai, p);
+    if constexpr (CDT != kNoCopy) store_copy1<CDT, PUSH>(P, ai, p);
   }
 }
 
-template <int GDT, int CDT>
+template <int GDT, int CDT, bool PUSH>
 __global__ void __launch_bounds__(256) adamw_mt_kernel(const __grid_constant__ MtParams P) {
   __shared__ bool last;
   if (P.stats != nullptr && P.skip_nonfinite && P.stats->found_inf != 0.0) return;  // GradScaler skip
@@ -222,11 +248,11 @@ __global__ void __launch_bounds__(256) adamw_mt_kernel(const __grid_constant__ M
     if (vec) {
       const int64_t body_end = begin + ((end - begin) & ~(int64_t)7);
       for (int64_t i = begin + (int64_t)threadIdx.x * 8; i < body_end; i += (int64_t)blockDim.x * 8)
-        mt_vec8<GDT, CDT>(P, abase + i, seg.grad, i, c, un, clip, coef);
+        mt_vec8<GDT, CDT, PUSH>(P, abase + i, seg.grad, i, c, un, clip, coef);
       e = body_end;
     }
     for (int64_t i = e + threadIdx.x; i < end; i += blockDim.x)
-      mt_elem<GDT, CDT>(P, abase + i, seg.grad, i, c, un, clip, coef);
+      mt_elem<GDT, CDT, PUSH>(P, abase + i, seg.grad, i, c, un, clip, coef);
   }
 
   // The last block advances the step counter of every updated segment.
@@ -240,27 +266,94 @@ __global__ void __launch_bounds__(256) adamw_mt_kernel(const __grid_constant__ M
   }
 }
 
-template <int GDT, int CDT>
+template <int GDT, int CDT, bool PUSH>
 static int launch_mt(const MtParams& P, cudaStream_t stream) {
   static int per_sm = 0;
   if (per_sm == 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adamw_mt_kernel<GDT, CDT>, 256, 0) != cudaSuccess || per_sm <= 0)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adamw_mt_kernel<GDT, CDT, PUSH>, 256, 0) != cudaSuccess ||
+        per_sm <= 0)
       per_sm = 2;
   }
   int64_t grid = (int64_t)current_sm_count() * per_sm;
   if (grid > P.nchunks) grid = P.nchunks;
   if (grid < 1) grid = 1;
-  adamw_mt_kernel<GDT, CDT><<<(unsigned)grid, 256, 0, stream>>>(P);
+  adamw_mt_kernel<GDT, CDT, PUSH><<<(unsigned)grid, 256, 0, stream>>>(P);
   return launch_status("nt_adamw_mt launch");
 }
 
 template <int GDT>
 static int dispatch_copy(const MtParams& P, int copy_dtype, cudaStream_t stream) {
-  if (P.copy == nullptr) return launch_mt<GDT, kNoCopy>(P, stream);
-  if (copy_dtype == NT_BF16) return launch_mt<GDT, NT_BF16>(P, stream);
-  if (copy_dtype == NT_F16) return launch_mt<GDT, NT_F16>(P, stream);
+  const bool push = P.npeers > 0;
+  if (P.copy == nullptr) return launch_mt<GDT, kNoCopy, false>(P, stream);
+  if (copy_dtype == NT_BF16)
+    return push ? launch_mt<GDT, NT_BF16, true>(P, stream) : launch_mt<GDT, NT_BF16, false>(P, stream);
+  if (copy_dtype == NT_F16)
+    return push ? launch_mt<GDT, NT_F16, true>(P, stream) : launch_mt<GDT, NT_F16, false>(P, stream);
   set_error("nt_adamw_mt: model copy dtype must be NT_F16 or NT_BF16 (got %d)", copy_dtype);
   return NT_EUNSUPPORTED;
+}
+
+// Validates the arguments and fills the kernel parameters; NT_OK with P.nchunks == 0 means
+// there is nothing to launch.
+static int build_mt_params(const nt_adamw_mt_args* args, MtParams& P) {
+  if (!args) { set_error("nt_adamw_mt: args is NULL"); return NT_EINVAL; }
+  const nt_adamw_mt_args& a = *args;
+  if (a.num_segments < 0 || a.num_chunks < 0) { set_error("nt_adamw_mt: negative sizes"); return NT_EINVAL; }
+  P.nchunks = 0;
+  P.npeers = 0;
+  if (a.num_segments == 0 || a.num_chunks == 0) return NT_OK;
+  if (!a.param || !a.exp_avg || !a.exp_avg_sq || !a.segments || !a.steps || !a.corrections || !a.workspace) {
+    set_error("nt_adamw_mt: NULL param/exp_avg/exp_avg_sq/segments/steps/corrections/workspace");
+    return NT_EINVAL;
+  }
+  if (a.chunk_elems <= 0 || (a.chunk_elems & 7) != 0) {
+    set_error("nt_adamw_mt: chunk_elems must be a positive multiple of 8 (got %d)", a.chunk_elems);
+    return NT_EINVAL;
+  }
+  if (a.num_groups < 1 || a.num_groups > NT_MAX_GROUPS || !a.groups) {
+    set_error("nt_adamw_mt: num_groups must be in [1, %d] (got %d)", NT_MAX_GROUPS, a.num_groups);
+    return NT_EINVAL;
+  }
+  if (a.correction_capacity < 2) { set_error("nt_adamw_mt: correction_capacity < 2"); return NT_EINVAL; }
+  if ((a.skip_nonfinite || a.clip) && !a.stats) {
+    set_error("nt_adamw_mt: skip_nonfinite / clip need stats");
+    return NT_EINVAL;
+  }
+  if (!aligned16(a.param) || !aligned16(a.exp_avg) || !aligned16(a.exp_avg_sq) ||
+      (a.model_copy && !aligned16(a.model_copy))) {
+    set_error("nt_adamw_mt: arenas must be 16-byte aligned");
+    return NT_EINVAL;
+  }
+  for (int i = 0; i < a.num_groups; ++i) {
+    const nt_adamw_group& g = a.groups[i];
+    if (!(g.eps > 0.0f) || !isfinite(g.lr) || !isfinite(g.beta1) || !isfinite(g.beta2) ||
+        !isfinite(g.weight_decay) || !isfinite(g.decay_factor) || g.decay_mode < 0 || g.decay_mode > 2 ||
+        g.correction_row < 0) {
+      set_error("nt_adamw_mt: group %d has invalid coefficients", i);
+      return NT_EINVAL;
+    }
+  }
+  P.p = a.param; P.m = a.exp_avg; P.v = a.exp_avg_sq; P.copy = a.model_copy;
+  P.segs = a.segments; P.nseg = a.num_segments; P.chunk_elems = a.chunk_elems; P.nchunks = a.num_chunks;
+  P.steps = a.steps; P.corr = reinterpret_cast<const float2*>(a.corrections); P.cap = a.correction_capacity;
+  P.scale = a.scale; P.stats = a.stats; P.skip_nonfinite = a.skip_nonfinite; P.clip = a.clip;
+  P.max_norm = a.max_norm;
+  P.counter = &static_cast<AdamwWorkspace*>(a.workspace)->counter;
+  P.error = a.error;
+  P.ngroups = a.num_groups;
+  for (int i = 0; i < a.num_groups; ++i) P.groups[i] = a.groups[i];
+  return NT_OK;
+}
+
+static int dispatch_mt(const MtParams& P, const nt_adamw_mt_args& a, cudaStream_t s) {
+  switch (a.grad_dtype) {
+    case NT_F32: return dispatch_copy<NT_F32>(P, a.model_dtype, s);
+    case NT_F16: return dispatch_copy<NT_F16>(P, a.model_dtype, s);
+    case NT_BF16: return dispatch_copy<NT_BF16>(P, a.model_dtype, s);
+    default:
+      set_error("nt_adamw_mt: unsupported gradient dtype %d", a.grad_dtype);
+      return NT_EUNSUPPORTED;
+  }
 }
 
 }  // namespace nt
@@ -306,60 +399,34 @@ int nt_adamw_f32(float* param, const float* grad, float* exp_avg, float* exp_avg
 size_t nt_adamw_workspace_size(void) { return sizeof(AdamwWorkspace); }
 
 int nt_adamw_mt(const nt_adamw_mt_args* args, void* stream) {
-  if (!args) { set_error("nt_adamw_mt: args is NULL"); return NT_EINVAL; }
-  const nt_adamw_mt_args& a = *args;
-  if (a.num_segments < 0 || a.num_chunks < 0) { set_error("nt_adamw_mt: negative sizes"); return NT_EINVAL; }
-  if (a.num_segments == 0 || a.num_chunks == 0) return NT_OK;
-  if (!a.param || !a.exp_avg || !a.exp_avg_sq || !a.segments || !a.steps || !a.corrections || !a.workspace) {
-    set_error("nt_adamw_mt: NULL param/exp_avg/exp_avg_sq/segments/steps/corrections/workspace");
+  MtParams P;
+  const int rc = build_mt_params(args, P);
+  if (rc != NT_OK || P.nchunks == 0) return rc;
+  return dispatch_mt(P, *args, as_stream(stream));
+}
+
+int nt_adamw_mt_push(const nt_adamw_mt_args* args, void* const* peer_copies, int32_t num_peers, void* stream) {
+  MtParams P;
+  const int rc = build_mt_params(args, P);
+  if (rc != NT_OK || P.nchunks == 0) return rc;
+  if (num_peers < 0 || num_peers > NT_MAX_RANKS - 1 || (num_peers > 0 && !peer_copies)) {
+    set_error("nt_adamw_mt_push: num_peers must be in [0, %d] with a peer array (got %d)", NT_MAX_RANKS - 1,
+              num_peers);
     return NT_EINVAL;
   }
-  if (a.chunk_elems <= 0 || (a.chunk_elems & 7) != 0) {
-    set_error("nt_adamw_mt: chunk_elems must be a positive multiple of 8 (got %d)", a.chunk_elems);
+  if (num_peers > 0 && !args->model_copy) {
+    set_error("nt_adamw_mt_push: peer copies need a model copy");
     return NT_EINVAL;
   }
-  if (a.num_groups < 1 || a.num_groups > NT_MAX_GROUPS || !a.groups) {
-    set_error("nt_adamw_mt: num_groups must be in [1, %d] (got %d)", NT_MAX_GROUPS, a.num_groups);
-    return NT_EINVAL;
-  }
-  if (a.correction_capacity < 2) { set_error("nt_adamw_mt: correction_capacity < 2"); return NT_EINVAL; }
-  if ((a.skip_nonfinite || a.clip) && !a.stats) {
-    set_error("nt_adamw_mt: skip_nonfinite / clip need stats");
-    return NT_EINVAL;
-  }
-  if (!aligned16(a.param) || !aligned16(a.exp_avg) || !aligned16(a.exp_avg_sq) ||
-      (a.model_copy && !aligned16(a.model_copy))) {
-    set_error("nt_adamw_mt: arenas must be 16-byte aligned");
-    return NT_EINVAL;
-  }
-  for (int i = 0; i < a.num_groups; ++i) {
-    const nt_adamw_group& g = a.groups[i];
-    if (!(g.eps > 0.0f) || !isfinite(g.lr) || !isfinite(g.beta1) || !isfinite(g.beta2) ||
-        !isfinite(g.weight_decay) || !isfinite(g.decay_factor) || g.decay_mode < 0 || g.decay_mode > 2 ||
-        g.correction_row < 0) {
-      set_error("nt_adamw_mt: group %d has invalid coefficients", i);
+  for (int q = 0; q < num_peers; ++q) {
+    if (!peer_copies[q] || !aligned16(peer_copies[q])) {
+      set_error("nt_adamw_mt_push: peer copy %d is NULL or not 16-byte aligned", q);
       return NT_EINVAL;
     }
+    P.peers[q] = peer_copies[q];
   }
-  MtParams P;
-  P.p = a.param; P.m = a.exp_avg; P.v = a.exp_avg_sq; P.copy = a.model_copy;
-  P.segs = a.segments; P.nseg = a.num_segments; P.chunk_elems = a.chunk_elems; P.nchunks = a.num_chunks;
-  P.steps = a.steps; P.corr = reinterpret_cast<const float2*>(a.corrections); P.cap = a.correction_capacity;
-  P.scale = a.scale; P.stats = a.stats; P.skip_nonfinite = a.skip_nonfinite; P.clip = a.clip;
-  P.max_norm = a.max_norm;
-  P.counter = &static_cast<AdamwWorkspace*>(a.workspace)->counter;
-  P.error = a.error;
-  P.ngroups = a.num_groups;
-  for (int i = 0; i < a.num_groups; ++i) P.groups[i] = a.groups[i];
-  cudaStream_t s = as_stream(stream);
-  switch (a.grad_dtype) {
-    case NT_F32: return dispatch_copy<NT_F32>(P, a.model_dtype, s);
-    case NT_F16: return dispatch_copy<NT_F16>(P, a.model_dtype, s);
-    case NT_BF16: return dispatch_copy<NT_BF16>(P, a.model_dtype, s);
-    default:
-      set_error("nt_adamw_mt: unsupported gradient dtype %d", a.grad_dtype);
-      return NT_EUNSUPPORTED;
-  }
+  P.npeers = num_peers;
+  return dispatch_mt(P, *args, as_stream(stream));
 }
 
 }  // extern "C"

@@ -1,0 +1,277 @@
+// ZeRO-1 over peer memory: CUDA IPC of the flat buffers and the reduce-scatter fused with
+// the first statistics pass.
+//
+// Each rank owns one contiguous shard of the flat gradient buffer. The reduce-scatter is a
+// pull: the owner reads the same shard range from every rank's buffer (its own from HBM,
+// the others' over NVLink through IPC mappings), sums the contributions in f32 in rank
+// order, rounds once to the gradient dtype and writes its reduced shard. The statistics of
+// that shard (sum of squares, non-finite and NaN counts, max |g|, all of g / scale) are
+// accumulated from the values just written, so found_inf and the norm cost no extra pass.
+// The sum order is fixed, so the result does not depend on the transport's chunking.
+#include <cuda.h>
+
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "nt_stats.cuh"
+
+namespace nt {
+
+struct ZeroReduceParams {
+  const void* src[NT_MAX_RANKS];
+  int nranks;
+  int64_t count;
+  int average;
+  float inv_n;      // 1/num_ranks when that is exact (power of two), else 0: divide instead
+  float n_f;
+  void* dst;
+  const float* scale;
+  nt_stats* stats;
+  StatsWorkspace* ws;
+};
+
+constexpr int kZeroThreads = kStatsThreads;
+
+template <int DT>
+__device__ __forceinline__ uint4 pack_vec(const float* x) {
+  uint4 raw;
+  if constexpr (DT == NT_F32) {
+    raw.x = __float_as_uint(x[0]); raw.y = __float_as_uint(x[1]);
+    raw.z = __float_as_uint(x[2]); raw.w = __float_as_uint(x[3]);
+  } else {
+    using T = typename Elem<DT>::T;
+    T* h = reinterpret_cast<T*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) h[k] = Elem<DT>::from_f32(x[k]);
+  }
+  return raw;
+}
+
+__device__ __forceinline__ float average(float sum, const ZeroReduceParams& P) {
+  if (P.average) sum = P.inv_n != 0.0f ? __fmul_rn(sum, P.inv_n) : __fdiv_rn(sum, P.n_f);
+  return sum;
+}
+
+// NR > 0: the rank count is a compile-time constant (2, 4, 8); NR == 0: any count up to
+// NT_MAX_RANKS, one vector per source in flight. The statistics see exactly the values
+// stored in the shard (rounded to the gradient dtype, then unscaled).
+template <int DT, int NR, int MODE>
+__device__ __forceinline__ void zero_reduce_body(const ZeroReduceParams& P, const Unscale& un, StatsAcc& a) {
+  constexpr int ES = DT == NT_F32 ? 4 : 2;
+  constexpr int EPV = 16 / ES;
+  constexpr int R = NR > 0 ? NR : NT_MAX_RANKS;
+  constexpr int U = NR > 0 && NR < 8 ? 8 / NR : 1;  // vectors in flight per source
+  const int nr = NR > 0 ? NR : P.nranks;
+  const int64_t nv = P.count / EPV;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * U;
+  uint4* dst = static_cast<uint4*>(P.dst);
+
+  for (int64_t v0 = (int64_t)blockIdx.x * blockDim.x * U + threadIdx.x; v0 < nv; v0 += stride) {
+    uint4 raw[U][R];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + (int64_t)u * blockDim.x;
+#pragma unroll
+      for (int q = 0; q < R; ++q)
+        if (v < nv && q < nr) raw[u][q] = __ldcs(static_cast<const uint4*>(P.src[q]) + v);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + (int64_t)u * blockDim.x;
+      if (v >= nv) continue;
+      float sum[EPV], x[EPV];
+      unpack16<DT>(raw[u][0], sum);
+#pragma unroll
+      for (int q = 1; q < R; ++q) {
+        if (q < nr) {
+          unpack16<DT>(raw[u][q], x);
+#pragma unroll
+          for (int k = 0; k < EPV; ++k) sum[k] = __fadd_rn(sum[k], x[k]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) sum[k] = average(sum[k], P);
+      const uint4 out = pack_vec<DT>(sum);
+      __stcs(dst + v, out);
+      unpack16<DT>(out, x);
+#pragma unroll
+      for (int k = 0; k < EPV; ++k) x[k] = unscale_by<MODE>(x[k], un.scale, un.inv);
+      stats_pass0<EPV>(x, a);
+    }
+  }
+  // Elements past the last full vector (count not a multiple of the vector width).
+  for (int64_t i = nv * EPV + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < P.count;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float sum = load1<DT>(P.src[0], i);
+    for (int q = 1; q < nr; ++q) sum = __fadd_rn(sum, load1<DT>(P.src[q], i));
+    store1<DT>(P.dst, i, average(sum, P));
+    stats_one(unscale_by<MODE>(load1<DT>(P.dst, i), un.scale, un.inv), a);
+  }
+}
+
+template <int DT, int NR>
+__global__ void __launch_bounds__(kZeroThreads, 2) zero_reduce_stats_kernel(const __grid_constant__ ZeroReduceParams P) {
+  Unscale un;
+  un.init(P.scale);
+  StatsAcc a{0.0, 0.0, 0.0, 0.0f, 0u, 0u};
+  if (!un.active) zero_reduce_body<DT, NR, kScaleNone>(P, un, a);
+  else if (un.pow2) zero_reduce_body<DT, NR, kScaleMul>(P, un, a);
+  else zero_reduce_body<DT, NR, kScaleDiv>(P, un, a);
+  stats_reduce_pass0(a, P.ws, P.stats);
+}
+
+template <int DT, int NR>
+static int launch_zero_reduce(const ZeroReduceParams& P, cudaStream_t s) {
+  int grid = current_sm_count() * 2;   // two 256-thread blocks per SM, 8 vectors in flight per thread
+  if (grid > kStatsMaxBlocks) grid = kStatsMaxBlocks;
+  const int64_t epv = DT == NT_F32 ? 4 : 8;
+  const int64_t want = (P.count / epv + kZeroThreads - 1) / kZeroThreads;
+  if (want < grid) grid = want > 0 ? (int)want : 1;
+  zero_reduce_stats_kernel<DT, NR><<<grid, kZeroThreads, 0, s>>>(P);
+  return launch_status("nt_zero_reduce_scatter_stats launch");
+}
+
+template <int DT>
+static int dispatch_ranks(const ZeroReduceParams& P, cudaStream_t s) {
+  switch (P.nranks) {
+    case 2: return launch_zero_reduce<DT, 2>(P, s);
+    case 4: return launch_zero_reduce<DT, 4>(P, s);
+    case 8: return launch_zero_reduce<DT, 8>(P, s);
+    default: return launch_zero_reduce<DT, 0>(P, s);
+  }
+}
+
+typedef CUresult (*GetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static GetAddressRangeFn address_range_fn() {
+  static GetAddressRangeFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<GetAddressRangeFn>(p);
+  }
+  return fn;
+}
+
+// Pointer handed out by nt_ipc_open -> the mapping's base, which cudaIpcCloseMemHandle wants.
+static std::mutex g_ipc_lock;
+static std::unordered_map<void*, void*> g_ipc_bases;
+
+}  // namespace nt
+
+using namespace nt;
+
+extern "C" {
+
+int nt_ipc_export(const void* ptr, unsigned char handle[64], uint64_t* offset) {
+  if (!ptr || !handle || !offset) { set_error("nt_ipc_export: NULL argument"); return NT_EINVAL; }
+  GetAddressRangeFn range = address_range_fn();
+  if (!range) { set_error("nt_ipc_export: cuMemGetAddressRange is unavailable"); return NT_ECUDA; }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) {
+    set_error("nt_ipc_export: %p is not device memory of this process", ptr);
+    return NT_EINVAL;
+  }
+  cudaIpcMemHandle_t h;
+  cudaError_t err = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (err != cudaSuccess) return cuda_fail(err, "nt_ipc_export (cudaIpcGetMemHandle)");
+  static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
+  memcpy(handle, &h, 64);
+  *offset = reinterpret_cast<uint64_t>(ptr) - static_cast<uint64_t>(base);
+  return NT_OK;
+}
+
+int nt_ipc_open(const unsigned char handle[64], uint64_t offset, void** ptr) {
+  if (!handle || !ptr) { set_error("nt_ipc_open: NULL argument"); return NT_EINVAL; }
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, 64);
+  void* base = nullptr;
+  cudaError_t err = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) return cuda_fail(err, "nt_ipc_open (cudaIpcOpenMemHandle)");
+  *ptr = static_cast<char*>(base) + offset;
+  std::lock_guard<std::mutex> lock(g_ipc_lock);
+  g_ipc_bases[*ptr] = base;
+  return NT_OK;
+}
+
+int nt_ipc_close(void* ptr) {
+  if (!ptr) return NT_OK;
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_ipc_lock);
+    auto it = g_ipc_bases.find(ptr);
+    if (it == g_ipc_bases.end()) {
+      set_error("nt_ipc_close: %p was not returned by nt_ipc_open", ptr);
+      return NT_EINVAL;
+    }
+    base = it->second;
+    g_ipc_bases.erase(it);
+  }
+  cudaError_t err = cudaIpcCloseMemHandle(base);
+  if (err != cudaSuccess) return cuda_fail(err, "nt_ipc_close (cudaIpcCloseMemHandle)");
+  return NT_OK;
+}
+
+int nt_can_access_peer(int32_t peer, int32_t* ok) {
+  if (!ok) { set_error("nt_can_access_peer: NULL argument"); return NT_EINVAL; }
+  int dev = 0, can = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(err, "nt_can_access_peer (cudaGetDevice)");
+  if (peer == dev) { *ok = 1; return NT_OK; }
+  err = cudaDeviceCanAccessPeer(&can, dev, peer);
+  if (err != cudaSuccess) return cuda_fail(err, "nt_can_access_peer");
+  *ok = can ? 1 : 0;
+  return NT_OK;
+}
+
+int nt_zero_reduce_scatter_stats(const nt_zero_reduce_args* args, void* stream) {
+  if (!args) { set_error("nt_zero_reduce_scatter_stats: args is NULL"); return NT_EINVAL; }
+  const nt_zero_reduce_args& a = *args;
+  if (a.num_ranks < 1 || a.num_ranks > NT_MAX_RANKS) {
+    set_error("nt_zero_reduce_scatter_stats: num_ranks must be in [1, %d] (got %d)", NT_MAX_RANKS, a.num_ranks);
+    return NT_EINVAL;
+  }
+  if (a.count < 0) { set_error("nt_zero_reduce_scatter_stats: negative count"); return NT_EINVAL; }
+  if (!a.stats || !a.workspace || (a.count > 0 && !a.dest)) {
+    set_error("nt_zero_reduce_scatter_stats: NULL dest/stats/workspace");
+    return NT_EINVAL;
+  }
+  if (a.workspace_bytes < sizeof(StatsWorkspace)) {
+    set_error("nt_zero_reduce_scatter_stats: workspace needs %zu bytes (got %zu)", sizeof(StatsWorkspace),
+              a.workspace_bytes);
+    return NT_EINVAL;
+  }
+  if (!aligned16(a.dest)) { set_error("nt_zero_reduce_scatter_stats: dest must be 16-byte aligned"); return NT_EINVAL; }
+  for (int q = 0; q < a.num_ranks && a.count > 0; ++q) {   // an empty shard reads nothing
+    if (!a.sources[q] || !aligned16(a.sources[q])) {
+      set_error("nt_zero_reduce_scatter_stats: source %d is NULL or not 16-byte aligned", q);
+      return NT_EINVAL;
+    }
+  }
+  ZeroReduceParams P;
+  for (int q = 0; q < NT_MAX_RANKS; ++q) P.src[q] = q < a.num_ranks ? a.sources[q] : a.sources[0];
+  P.nranks = a.num_ranks;
+  P.count = a.count;
+  P.average = a.average != 0;
+  P.n_f = (float)a.num_ranks;
+  P.inv_n = (a.num_ranks & (a.num_ranks - 1)) == 0 ? 1.0f / (float)a.num_ranks : 0.0f;
+  P.dst = a.dest;
+  P.scale = a.scale;
+  P.stats = a.stats;
+  P.ws = static_cast<StatsWorkspace*>(a.workspace);
+  cudaStream_t s = as_stream(stream);
+  switch (a.dtype) {
+    case NT_F32: return dispatch_ranks<NT_F32>(P, s);
+    case NT_F16: return dispatch_ranks<NT_F16>(P, s);
+    case NT_BF16: return dispatch_ranks<NT_BF16>(P, s);
+    default:
+      set_error("nt_zero_reduce_scatter_stats: unsupported dtype %d", a.dtype);
+      return NT_EUNSUPPORTED;
+  }
+}
+
+}  // extern "C"

@@ -116,6 +116,13 @@ def _sole_owner(params: list[torch.Tensor]):
     return owner
 
 
+def _sharded_owner(params: list[torch.Tensor]):
+    """The ZeRO-1 optimizer that owns exactly these parameters, if any. Its gradients only
+    mean something after its reduce-scatter, so the norm and the clips go through it."""
+    owner = _sole_owner(params)
+    return owner if owner is not None and getattr(owner, "_sharded", False) else None
+
+
 def _pending_owners(params: list[torch.Tensor]):
     owners = {}
     for p in params:
@@ -129,6 +136,9 @@ def get_grad_norm(parameters, norm_type: float = 2) -> torch.Tensor:
     """namitorch/optim/clip_grad.py:86-88."""
     order = _norm_type(norm_type)
     params, gradients = _parameters_and_gradients(parameters)
+    sharded = _sharded_owner(params)
+    if sharded is not None:
+        return sharded._grad_norm(order)[N.STATS_FIELDS.index("norm")]
     _require_cuda(gradients)
     for owner in _pending_owners(params):
         owner._materialize_pending()
@@ -151,8 +161,11 @@ def clip_grad_norm_(parameters, max_norm: float, norm_type: float = 2, error_if_
             if not math.isfinite(value):
                 raise RuntimeError(f"Cannot clip gradients with nonfinite total norm {value}.")
 
-    owner = _sole_owner(params) if _LAZY else None
+    sharded = _sharded_owner(params)
+    owner = sharded if sharded is not None else (_sole_owner(params) if _LAZY else None)
     stats = owner._lazy_clip(maximum, order, check) if owner is not None else None
+    if stats is not None and sharded is not None and not _LAZY:
+        sharded._materialize_pending()   # eager: rewrite the reduced shard now
     if stats is None:
         _require_cuda(gradients)
         for o in _pending_owners(params):
@@ -167,6 +180,10 @@ def clip_grad_value_(parameters, clip_value: float) -> None:
     """namitorch/optim/clip_grad.py:115-121."""
     bound = _nonnegative(clip_value, "clip_value")
     params, gradients = _parameters_and_gradients(parameters)
+    sharded = _sharded_owner(params)
+    if sharded is not None:
+        sharded._clip_value_(bound)
+        return
     _require_cuda(gradients)
     for owner in _pending_owners(params):
         owner._materialize_pending()

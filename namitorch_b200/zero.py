@@ -11,14 +11,24 @@ ranks, so both collectives run per piece on contiguous slices, in place:
   gradient buffer (the parameters' ``.grad`` views), both in ``model_dtype``;
 * rank r holds only its K*c elements of the fp32 master weights, exp_avg and exp_avg_sq.
 
-One step:
-1. reduce-scatter of every piece of the gradient buffer (NCCL, average over ranks);
-2. one statistics kernel over the rank's gradient shard, one all-reduce (SUM) of the
-   24-byte record {sum g^2, #non-finite, #NaN} (plus a MAX of max|g| for a non-2 norm) and a
-   one-thread finalize kernel: every rank then holds the same found_inf and global norm;
-3. per piece: the fused AdamW kernel over the piece's parameter segments (unscale, skip,
-   clip, update, bf16 cast-out into the rank's slice of the model copy), after which the
-   piece's all-gather runs on a side stream while the next piece is updated.
+One step has two exchanges around the update, over one of two transports:
+
+* ``transport="p2p"`` (default when every pair of GPUs can address each other's memory):
+  the exchanges run inside the kernels, over NVLink, through CUDA IPC mappings of every
+  rank's gradient buffer and model copy (K = 1: one contiguous shard per rank).
+  1. a 4-byte stream-ordered barrier (NCCL all-reduce): every rank's gradients are final;
+  2. ``nt_zero_reduce_scatter_stats``: the rank pulls its shard range from every rank's
+     gradient buffer, sums in f32 in rank order, writes the reduced shard and, in the same
+     pass, the shard's statistics;
+  3. one all-reduce (SUM) of the 24-byte record {sum g^2, #non-finite, #NaN} (plus a MAX of
+     max|g| for a non-2 norm) and a one-thread finalize kernel: every rank then holds the
+     same found_inf and global norm;
+  4. ``nt_adamw_mt_push``: the fused AdamW kernel (unscale, skip, clip, update) stores each
+     bf16 result into its own model copy and into every peer's, which is the all-gather;
+  5. a second 4-byte barrier: every push has landed and every pull is done.
+* ``transport="nccl"``: NCCL reduce-scatter of every piece (average over ranks), the
+  statistics kernel plus the same all-reduce, then per piece the fused AdamW kernel
+  followed by that piece's all-gather on a side stream, overlapping the next piece's update.
 
 A parameter cut by a piece or rank boundary is several segments; only its last segment on a
 rank advances its step counter (a negative step slot marks the others).
@@ -104,8 +114,23 @@ class CudaShardKernels:
                None if scale is None else scale.data_ptr(), None if stats is None else stats.data_ptr(),
                int(max_norm is not None), float(max_norm or 0.0), N.stream_handle())
 
+    def clip_value(self, buf, bound):
+        spans, nchunks = self._span(buf)
+        N.call("nt_grad_clip_value", spans.data_ptr(), 1, CHUNK, nchunks, N.dtype_code(buf.dtype), float(bound),
+               N.stream_handle())
+
+    def reduce_stats(self, sources, dest, stats, *, scale, average):
+        """Fused reduce-scatter + pass-0 statistics over peer memory."""
+        args = N.ZeroReduceArgs(num_ranks=len(sources), dtype=N.dtype_code(dest.dtype), count=dest.numel(),
+                                average=int(bool(average)), dest=dest.data_ptr(),
+                                scale=None if scale is None else scale.data_ptr(), stats=stats.data_ptr(),
+                                workspace=self.workspace.data_ptr(), workspace_bytes=self.workspace.numel())
+        for q, ptr in enumerate(sources[:N.NT_MAX_RANKS]):   # more ranks: the library rejects num_ranks
+            args.sources[q] = ptr
+        N.call("nt_zero_reduce_scatter_stats", N.C.byref(args), N.stream_handle())
+
     def update(self, *, master, exp_avg, exp_avg_sq, copy, grad_dtype, segments, num_segments, num_chunks, steps,
-               corrections, capacity, scale, stats, skip, max_norm, groups):
+               corrections, capacity, scale, stats, skip, max_norm, groups, peers=None):
         group_array = (N.AdamWGroup * len(groups))(*groups)
         args = N.AdamWMtArgs(
             param=master.data_ptr(), exp_avg=exp_avg.data_ptr(), exp_avg_sq=exp_avg_sq.data_ptr(),
@@ -116,7 +141,11 @@ class CudaShardKernels:
             skip_nonfinite=int(skip), clip=int(max_norm is not None), max_norm=float(max_norm or 0.0),
             workspace=self.adamw_workspace.data_ptr(), error=self.error.data_ptr(), groups=group_array,
             num_groups=len(groups))
-        N.call("nt_adamw_mt", N.C.byref(args), N.stream_handle())
+        if peers:
+            array = (N.C.c_void_p * len(peers))(*peers)
+            N.call("nt_adamw_mt_push", N.C.byref(args), array, len(peers), N.stream_handle())
+        else:
+            N.call("nt_adamw_mt", N.C.byref(args), N.stream_handle())
 
 
 class ZeroAdamW(_FirstOrderAdam):
@@ -128,17 +157,24 @@ class ZeroAdamW(_FirstOrderAdam):
     ``zero_grad`` zeroes that buffer in place."""
 
     _decoupled_weight_decay = True
+    _sharded = True   # gradients are meaningful only after the reduce-scatter: norms and clips go through us
 
     def __init__(self, params, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 1e-2,
                  *, maximize: bool = False, model_dtype=torch.bfloat16, process_group=None, average_grads: bool = True,
-                 pieces: int = DEFAULT_PIECES, _kernels=None):
+                 pieces: int = DEFAULT_PIECES, transport: str = "auto", _kernels=None):
         if model_dtype not in (torch.bfloat16, torch.float16, torch.float32):
             raise TypeError("model_dtype must be torch.bfloat16, torch.float16 or torch.float32.")
         self._group = process_group
         self._average = average_grads
         if type(pieces) is not int or pieces < 1:
             raise ValueError("pieces must be a positive integer.")
+        if transport not in ("auto", "p2p", "nccl"):
+            raise ValueError("transport must be 'auto', 'p2p' or 'nccl'.")
         self._pieces = pieces
+        self._transport_request = transport
+        self.transport = "nccl"
+        self._peer_maps: list[int] = []
+        self._local_stats = None
         self.timing = False
         self.last_events: list | None = None
         self._kernels = _kernels
@@ -163,6 +199,9 @@ class ZeroAdamW(_FirstOrderAdam):
         self.world = dist.get_world_size(self._group)
         self.rank = dist.get_rank(self._group)
         self.device = device
+        self.transport = self._choose_transport(device)
+        if self.transport == "p2p":
+            self._pieces = 1
         self.params_list = params
         self.index = {id(p): i for i, p in enumerate(params)}
         numels = [p.numel() for p in params]
@@ -195,8 +234,78 @@ class ZeroAdamW(_FirstOrderAdam):
         self._reduced = False
         self._tables = None
         self._side = torch.cuda.Stream(device) if device.type == "cuda" else None
+        if self.transport == "p2p":
+            self._sync = torch.zeros(1, dtype=torch.int32, device=device)
+            self._map_peers()
         for p in params:
             _OWNERS[id(p)] = self
+
+    # ---- peer memory ------------------------------------------------------------------------
+    def _choose_transport(self, device) -> str:
+        """'p2p' when every rank's GPU can load from and store to every other rank's GPU
+        (decided collectively, so all ranks agree), else 'nccl'."""
+        want = self._transport_request
+        if want == "nccl" or self.world == 1:
+            return "nccl"
+        usable = (device.type == "cuda" and isinstance(self._kernels, CudaShardKernels)
+                  and dist.get_backend(self._group) == "nccl")
+        devices = [None] * self.world
+        dist.all_gather_object(devices, device.index if device.type == "cuda" else -1, group=self._group)
+        if usable:
+            try:
+                usable = all(N.can_access_peer(d) for d in devices if d is not None and d >= 0)
+                # The allocator's memory must be exportable (not so with expandable segments).
+                probe = torch.empty(1 << 20, dtype=torch.uint8, device=device)
+                N.ipc_export(probe.data_ptr())
+                del probe
+            except (RuntimeError, ValueError):
+                usable = False
+        votes = [None] * self.world
+        dist.all_gather_object(votes, bool(usable), group=self._group)
+        if all(votes):
+            return "p2p"
+        if want == "p2p":
+            raise RuntimeError("ZeroAdamW(transport='p2p') needs CUDA tensors, the NCCL backend and peer access "
+                               "between every pair of GPUs in the group.")
+        return "nccl"
+
+    def _map_peers(self):
+        """Maps every other rank's gradient buffer and model copy into this process."""
+        mine = (N.ipc_export(self.flat_grads.data_ptr()), N.ipc_export(self.copy.data_ptr()))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, mine, group=self._group)
+        grads, copies = [], []
+        for q, ((gh, goff), (ch, coff)) in enumerate(handles):
+            if q == self.rank:
+                grads.append(self.flat_grads.data_ptr())
+                copies.append(self.copy.data_ptr())
+                continue
+            g = N.ipc_open(gh, goff)
+            self._peer_maps.append(g)
+            c = N.ipc_open(ch, coff)
+            self._peer_maps.append(c)
+            grads.append(g)
+            copies.append(c)
+        esize = self.flat_grads.element_size()
+        shard_bytes = self.rank * self.piece_len * esize
+        # Rank q's gradients for this rank's shard, in rank order.
+        self._sources = [g + shard_bytes for g in grads]
+        # Where this rank's shard lands in every other rank's copy, addressed like the local
+        # copy base (the kernel adds the shard-local offset).
+        self._push = [c + shard_bytes for q, c in enumerate(copies) if q != self.rank]
+        dist.barrier(group=self._group)
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers (collective with the other ranks' close())."""
+        if self._peer_maps:
+            torch.cuda.synchronize(self.device)
+            for ptr in self._peer_maps:
+                N.ipc_close(ptr)
+            self._peer_maps = []
+
+    def _barrier(self):
+        """Stream-ordered: later work on this stream starts after every rank reached it."""
+        dist.all_reduce(self._sync, op=dist.ReduceOp.MAX, group=self._group)
 
     def _global(self, local: int) -> int:
         """Global flat offset of an element of the rank's shard."""
@@ -247,13 +356,24 @@ class ZeroAdamW(_FirstOrderAdam):
                     view.copy_(p.grad.reshape(-1))
                     p.grad = view.view(p.shape)
 
-    def _reduce(self):
+    def _reduce(self, scale=None):
+        """Reduce-scatters the gradients (once per step). Over p2p the shard's pass-0
+        statistics of g / scale come out of the same kernel and are kept for
+        _global_stats."""
         if self._reduced:
             return
         self._adopt_foreign_grads()
         if self.timing:
             self.last_events = []
         self._event()
+        if self.transport == "p2p":
+            self._barrier()
+            stats = stats_tensor(self.device)
+            self._kernels.reduce_stats(self._sources, self.grad_shard, stats, scale=scale, average=self._average)
+            self._local_stats = (scale, stats)
+            self._event()
+            self._reduced = True
+            return
         op = dist.ReduceOp.AVG if self._average else dist.ReduceOp.SUM
         c = self.piece_len
         for j in range(self._pieces):
@@ -265,9 +385,13 @@ class ZeroAdamW(_FirstOrderAdam):
 
     def _global_stats(self, scale, norm_type: float) -> torch.Tensor:
         """found_inf and the global norm, identical on every rank."""
-        stats = stats_tensor(self.device)
         k = self._kernels
-        k.stats(self.grad_shard, stats, scale=scale, norm_type=norm_type, pass_=0, finalize=False)
+        cached, self._local_stats = self._local_stats, None
+        if cached is not None and cached[0] is scale:
+            stats = cached[1]          # pass 0 ran inside the p2p reduce-scatter
+        else:
+            stats = stats_tensor(self.device)
+            k.stats(self.grad_shard, stats, scale=scale, norm_type=norm_type, pass_=0, finalize=False)
         dist.all_reduce(stats[_SUM_FIELDS], op=dist.ReduceOp.SUM, group=self._group)
         if norm_type != 2.0:
             dist.all_reduce(stats[_MAXABS:_MAXABS + 1], op=dist.ReduceOp.MAX, group=self._group)
@@ -286,11 +410,12 @@ class ZeroAdamW(_FirstOrderAdam):
         return [self.grad_shard]
 
     def _amp_unscale_(self, scale: torch.Tensor, lazy: bool) -> torch.Tensor:
-        self._reduce()
+        self._reduce(scale if lazy else None)
         if lazy:
             stats = self._global_stats(scale, 2.0)
             self._amp = _AmpPending(self._grad_key(self._entries()), stats, scale)
         else:
+            self._local_stats = None
             self._kernels.transform(self.grad_shard, scale=scale, stats=None, max_norm=None)
             stats = self._global_stats(None, 2.0)
             self._amp = _AmpPending(self._grad_key(self._entries()), stats, None)
@@ -320,10 +445,28 @@ class ZeroAdamW(_FirstOrderAdam):
         self._amp = amp
         return stats
 
+    def _grad_norm(self, norm_type: float) -> torch.Tensor:
+        """Global statistics of the reduced gradients as the next step would see them
+        (get_grad_norm on this optimizer's parameters)."""
+        self._reduce()
+        amp = self._amp
+        if amp is not None and amp.max_norm is not None:
+            self._materialize_pending()
+            amp = self._amp
+        return self._global_stats(None if amp is None else amp.scale, norm_type)
+
+    def _clip_value_(self, bound: float) -> None:
+        """clip_grad_value_ on this optimizer's parameters: clamps the reduced shard."""
+        self._reduce()
+        self._materialize_pending()
+        self._local_stats = None
+        self._kernels.clip_value(self.grad_shard, bound)
+
     def _materialize_pending(self):
         amp = self._amp
         if amp is None or (amp.scale is None and amp.max_norm is None):
             return
+        self._local_stats = None
         self._kernels.transform(self.grad_shard, scale=amp.scale, stats=amp.stats, max_norm=amp.max_norm)
         amp.scale = None
         amp.max_norm = None
@@ -352,6 +495,27 @@ class ZeroAdamW(_FirstOrderAdam):
         self._event()
         cuda = self.device.type == "cuda"
         main = torch.cuda.current_stream(self.device) if cuda else None
+        self._local_stats = None
+        if self.transport == "p2p":
+            table = tables[0]
+            if table is not None:
+                segs, nseg, nchunks = table
+                self._kernels.update(
+                    master=self.master, exp_avg=self.exp_avg, exp_avg_sq=self.exp_avg_sq, copy=self._copy_base(0),
+                    grad_dtype=self.grad_shard.dtype, segments=segs, num_segments=nseg, num_chunks=nchunks,
+                    steps=self.steps, corrections=self.corrections.tensor, capacity=self.corrections.capacity,
+                    scale=None if amp is None else amp.scale, stats=None if amp is None else amp.stats,
+                    skip=bool(amp is not None and amp.skip), max_norm=None if amp is None else amp.max_norm,
+                    groups=structs, peers=self._push)
+            self._event()
+            self._barrier()
+            self._event()
+            if not self.pieces:
+                self._advance_steps_without_update(amp)
+            self._event()
+            self._reduced = False
+            self.max_step += 1
+            return loss
         if cuda:
             self._side.wait_stream(main)
         for j in range(self._pieces):

@@ -43,6 +43,11 @@ def test_errors_are_reported_without_a_gpu():
     with pytest.raises(ValueError, match="ten finite float32 coefficients"):
         coef = (ctypes.c_float * 10)(*([float("nan")] + [1.0] * 9))
         N.check(lib.nt_adamw_f32(None, None, None, None, coef, 0, 1, 8, None))
+    args = N.ZeroReduceArgs(num_ranks=9)
+    assert lib.nt_zero_reduce_scatter_stats(ctypes.byref(args), None) == N.NT_EINVAL
+    assert b"num_ranks" in lib.nt_last_error()
+    assert lib.nt_adamw_mt_push(None, None, 0, None) == N.NT_EINVAL
+    assert lib.nt_ipc_close(ctypes.c_void_p(16)) == N.NT_EINVAL
     with pytest.raises(ValueError, match="label_smoothing"):
         args = N.XentArgs(rows=1, classes=4, dtype=N.NT_BF16, label_smoothing=1.5, reduction=1)
         N.check(lib.nt_softmax_xent(ctypes.byref(args), None))
@@ -57,6 +62,7 @@ STRUCTS = {
     "nt_grad_stats_args": (N.GradStatsArgs, [("pass" if f == "pass_" else f) for f, _ in N.GradStatsArgs._fields_]),
     "nt_xent_info": (N.XentInfo, None),
     "nt_xent_args": (N.XentArgs, [f for f, _ in N.XentArgs._fields_]),
+    "nt_zero_reduce_args": (N.ZeroReduceArgs, [f for f, _ in N.ZeroReduceArgs._fields_]),
 }
 
 

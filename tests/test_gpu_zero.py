@@ -1,4 +1,5 @@
-"""ZeRO-1 on 2+ GPUs over NCCL: one process per GPU, GradScaler + clip_grad_norm_ + AdamW.
+"""ZeRO-1 on 2+ GPUs: one process per GPU, GradScaler + clip_grad_norm_ + AdamW, over both
+transports (NCCL collectives; the fused kernels over peer memory).
 
 The oracle receives the gradients as they come out of the reduce-scatter (gathered from
 every rank), so the comparison isolates the sharded update from the bf16 reduction
@@ -23,22 +24,24 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out_path):
+def _worker(rank, world, port, out_path, transport, lazy):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     try:
         from namitorch_b200 import GradScaler, workloads as W
-        from namitorch_b200.optim import clip_grad_norm_
+        from namitorch_b200.optim import clip_grad_norm_, defer_gradient_transforms
         from namitorch_b200.zero import ZeroAdamW
+        defer_gradient_transforms(lazy)
         from oracle.casts import round_to_bf16
         shape = W.CONFIG_SMALL
         params = [torch.nn.Parameter(torch.from_numpy(a).cuda()) for a in W.init_params(shape, seed=0)]
         decay, no_decay = shape.groups()
         groups = [{"params": [params[i] for i in decay], "weight_decay": 0.1},
                   {"params": [params[i] for i in no_decay], "weight_decay": 0.0}]
-        opt = ZeroAdamW(groups, lr=3e-4, model_dtype=torch.bfloat16)
+        opt = ZeroAdamW(groups, lr=3e-4, model_dtype=torch.bfloat16, transport=transport)
+        assert opt.transport == transport
         scaler = GradScaler(1024.0, growth_interval=2)
         reduced, local, norms, stepped = [], [], [], []
         for step in range(4):
@@ -50,14 +53,18 @@ def _worker(rank, world, port, out_path):
             for p, g in zip(params, grads):
                 p.grad.copy_(torch.from_numpy(g).to(torch.bfloat16))
             local.append(opt.flat_grads.float().cpu().numpy())
-            opt._reduce()
-            full = opt._gather_shards(opt.grad_shard)   # global (interleaved-piece) order
-            reduced.append(full.float().cpu().numpy())
+            if not lazy:
+                # The eager path rewrites the reduced shard in place: read it before.
+                opt._reduce()
+                reduced.append(opt._gather_shards(opt.grad_shard).float().cpu().numpy())
             scaler.scale(torch.ones((), device="cuda"))
             scaler.unscale_(opt)
             norms.append(float(clip_grad_norm_(params, 1.0).item()))
             stepped.append(bool(scaler.step(opt)))
             scaler.update()
+            if lazy:
+                # Deferred transforms leave the reduced shard as the reduce-scatter wrote it.
+                reduced.append(opt._gather_shards(opt.grad_shard).float().cpu().numpy())
         sd = opt.state_dict()
         copies = [p.detach().float().cpu().numpy() for p in params]
         all_local = [None] * world
@@ -71,20 +78,22 @@ def _worker(rank, world, port, out_path):
                      steps=np.array([st["step"] for _, st in sorted(sd["state"].items())]),
                      **{f"copy{k}": c for k, c in enumerate(copies)}, scale=np.array(scaler.get_scale()))
         dist.barrier()
+        opt.close()
     finally:
         dist.destroy_process_group()
 
 
-def test_zero1_nccl_matches_oracle(tmp_path):
+@pytest.mark.parametrize("transport,lazy", [("nccl", True), ("p2p", True), ("p2p", False)])
+def test_zero1_matches_oracle(tmp_path, transport, lazy):
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     import torch.multiprocessing as mp
     from namitorch_b200 import workloads as W
     from oracle import adamw as oadamw
     from oracle import amp as oamp
-    from oracle.casts import f32_to_bf16_bits
+    from oracle.casts import f32_to_bf16_bits, round_to_bf16
     out_path = tmp_path / "zero.npz"
-    mp.spawn(_worker, args=(WORLD, _free_port(), str(out_path)), nprocs=WORLD, join=True)
+    mp.spawn(_worker, args=(WORLD, _free_port(), str(out_path), transport, lazy), nprocs=WORLD, join=True)
     out = np.load(out_path)
     shape = W.CONFIG_SMALL
     offsets = out["offsets"]
@@ -97,6 +106,14 @@ def test_zero1_nccl_matches_oracle(tmp_path):
         finite = np.isfinite(mean)
         assert np.array_equal(finite, np.isfinite(out["reduced"]))
         assert np.all(np.abs(out["reduced"][finite] - mean[finite]) <= bound[finite])
+    if transport == "p2p":
+        # The pull reduce-scatter sums in f32 in rank order and rounds once: bit-exact.
+        total = local[0].astype(np.float32)
+        for q in range(1, WORLD):
+            total = total + local[q].astype(np.float32)
+        with np.errstate(invalid="ignore"):
+            expect = round_to_bf16(total * np.float32(1.0 / WORLD))
+        np.testing.assert_array_equal(f32_to_bf16_bits(out["reduced"]), f32_to_bf16_bits(expect))
     params = W.init_params(shape, seed=0)
     decay, no_decay = shape.groups()
     base = {"lr": 3e-4, "betas": (0.9, 0.999), "eps": 1e-8, "maximize": False}
@@ -111,7 +128,9 @@ def test_zero1_nccl_matches_oracle(tmp_path):
         grads = [None] * len(shapes)
         for k, orig in enumerate(order):   # flat-layout offsets follow the registration order
             grads[orig] = flat[offsets[k]:offsets[k] + numels[orig]].reshape(shapes[orig]).astype(np.float32).copy()
-        r = oamp.amp_step(oracle, oscaler, grads, max_norm=1.0)
+        # Eager transforms rewrite the bf16 gradient shard in place, like the reference's
+        # in-place unscale_ / clip on bf16 gradient storage.
+        r = oamp.amp_step(oracle, oscaler, grads, max_norm=1.0, storage=None if lazy else round_to_bf16)
         assert bool(out["stepped"][step]) == r["stepped"]
         if r["norm"] is not None:
             assert abs(out["norms"][step] - r["norm"]) <= 1e-12 * r["norm"]

@@ -95,6 +95,10 @@ class NumpyShardKernels:
                 g = (g.astype(np.float64) * coef).astype(np.float32)
         buf.copy_(torch.from_numpy(g))
 
+    def clip_value(self, buf, bound):
+        g = buf.detach().numpy().astype(np.float64)
+        buf.copy_(torch.from_numpy(np.clip(g, -bound, bound).astype(np.float32)))
+
     def update(self, *, master, exp_avg, exp_avg_sq, copy, grad_dtype, segments, num_segments, num_chunks, steps,
                corrections, capacity, scale, stats, skip, max_norm, groups):
         s = None if stats is None else stats.numpy()
@@ -141,12 +145,16 @@ def _rank_grads(rank, step):
     return [rng.normal(0, 0.3, s).astype(np.float32) for s in SIZES]
 
 
-def _worker(rank, world, port, result_path):
+CLIP_VALUE_STEP = 1   # the step that also applies clip_grad_value_(0.5) after the norm clip
+
+
+def _worker(rank, world, port, result_path, lazy):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        from namitorch_b200.optim import clip_grad_norm_
+        from namitorch_b200.optim import clip_grad_norm_, clip_grad_value_, defer_gradient_transforms, get_grad_norm
         from namitorch_b200.zero import ZeroAdamW
+        defer_gradient_transforms(lazy)
         rng = np.random.default_rng(0)
         arrays = [rng.normal(0, 1, s).astype(np.float32) for s in SIZES]
         params = [torch.nn.Parameter(torch.from_numpy(a.copy())) for a in arrays]
@@ -160,7 +168,11 @@ def _worker(rank, world, port, result_path):
             opt.zero_grad()
             for p, g in zip(params, _rank_grads(rank, step)):
                 p.grad.copy_(torch.from_numpy(g))
+            before = float(get_grad_norm(params).item())   # the global norm of the reduced gradients
             norms.append(float(clip_grad_norm_(params, 5.0).item()))
+            assert abs(before - norms[-1]) <= 1e-12 * norms[-1]
+            if step == CLIP_VALUE_STEP:
+                clip_grad_value_(params, 0.5)
             opt.step()
         sd = opt.state_dict()
         copies = [p.detach().numpy().copy() for p in params]
@@ -197,11 +209,12 @@ def _worker(rank, world, port, result_path):
         dist.destroy_process_group()
 
 
-def test_zero1_two_ranks_match_single_process_oracle(tmp_path):
+@pytest.mark.parametrize("lazy", [True, False], ids=["deferred", "eager"])
+def test_zero1_two_ranks_match_single_process_oracle(tmp_path, lazy):
     from oracle import adamw as oadamw
     from oracle import clip as oclip
     result = tmp_path / "zero.npz"
-    mp.spawn(_worker, args=(2, _free_port(), str(result)), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), str(result), lazy), nprocs=2, join=True)
     out = np.load(result)
     rng = np.random.default_rng(0)
     arrays = [rng.normal(0, 1, s).astype(np.float32) for s in SIZES]
@@ -212,6 +225,8 @@ def test_zero1_two_ranks_match_single_process_oracle(tmp_path):
         grads = [a + b for a, b in zip(_rank_grads(0, step), _rank_grads(1, step))]
         norm = oclip.clip_grad_norm_(grads, 5.0)
         assert abs(out["norms"][step] - float(norm)) <= 1e-12 * float(norm)
+        if step == CLIP_VALUE_STEP:
+            oclip.clip_grad_value_(grads, 0.5)
         oracle.step(grads)
     assert out["steps"].tolist() == [3] * len(SIZES)
     # (the summed norm differs from the reference's two-pass norm in the last bits, so the
