@@ -374,6 +374,19 @@ def run_ours(args):
 
     if not args.no_e2e:
         result["e2e"] = e2e_ours(args, opt, scaler, params, flat_grads, loss, world)
+    # The update alone (the HBM-bound part that shards), for the update-scaling figure
+    # t_update(1 GPU, P) / max over ranks t_update(N, P/N). At N > 1 this runs last: it
+    # advances the optimizer state without exchanges.
+    if world > 1:
+        dist.barrier()
+        t = torch.tensor([opt.benchmark_shard_update(20)], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        only_ms = float(t.item())
+    else:
+        only_ms = update_ms
+    result["update_only"] = {"ms": only_ms, "params_per_s": P / (only_ms / 1e3), "shard_params": shard,
+                             "hbm_gbs": BYTES_UPDATE * shard / (only_ms / 1e3) / 1e9,
+                             "frac_of_measured_hbm": BYTES_UPDATE * shard / (only_ms / 1e3) / 1e9 / peak}
     if world > 1:
         dist.barrier()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -481,32 +481,16 @@ class ZeroAdamW(_FirstOrderAdam):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
-        options = self._validated_options()
         self._reduce()
         amp = self._amp
         self._amp = None
-        used = sorted({gi for gi, _, _ in self._entries()})
-        if len(used) > N.NT_MAX_GROUPS:
-            raise RuntimeError(f"ZeroAdamW supports at most {N.NT_MAX_GROUPS} parameter groups.")
-        local = {gi: k for k, gi in enumerate(used)}
-        structs = [self._group_struct(options[gi]) for gi in used]
-        self.corrections.ensure(self.max_step + 1)
-        tables = self._piece_tables(local)
+        structs, tables = self._update_plan()
         self._event()
         cuda = self.device.type == "cuda"
         main = torch.cuda.current_stream(self.device) if cuda else None
         self._local_stats = None
         if self.transport == "p2p":
-            table = tables[0]
-            if table is not None:
-                segs, nseg, nchunks = table
-                self._kernels.update(
-                    master=self.master, exp_avg=self.exp_avg, exp_avg_sq=self.exp_avg_sq, copy=self._copy_base(0),
-                    grad_dtype=self.grad_shard.dtype, segments=segs, num_segments=nseg, num_chunks=nchunks,
-                    steps=self.steps, corrections=self.corrections.tensor, capacity=self.corrections.capacity,
-                    scale=None if amp is None else amp.scale, stats=None if amp is None else amp.stats,
-                    skip=bool(amp is not None and amp.skip), max_norm=None if amp is None else amp.max_norm,
-                    groups=structs, peers=self._push)
+            self._launch_update(tables[0], structs, amp, 0, self._push)
             self._event()
             self._barrier()
             self._event()
@@ -519,16 +503,7 @@ class ZeroAdamW(_FirstOrderAdam):
         if cuda:
             self._side.wait_stream(main)
         for j in range(self._pieces):
-            table = tables[j]
-            if table is not None:
-                segs, nseg, nchunks = table
-                self._kernels.update(
-                    master=self.master, exp_avg=self.exp_avg, exp_avg_sq=self.exp_avg_sq, copy=self._copy_base(j),
-                    grad_dtype=self.grad_shard.dtype, segments=segs, num_segments=nseg, num_chunks=nchunks,
-                    steps=self.steps, corrections=self.corrections.tensor, capacity=self.corrections.capacity,
-                    scale=None if amp is None else amp.scale, stats=None if amp is None else amp.stats,
-                    skip=bool(amp is not None and amp.skip), max_norm=None if amp is None else amp.max_norm,
-                    groups=structs)
+            self._launch_update(tables[j], structs, amp, j, None)
             full, mine = self._piece_slices(j)
             if cuda:
                 # The piece's all-gather overlaps the next piece's update.
@@ -547,6 +522,47 @@ class ZeroAdamW(_FirstOrderAdam):
         self._reduced = False
         self.max_step += 1
         return loss
+
+    def _update_plan(self):
+        """(group coefficient structs, per-piece segment tables) for the next update."""
+        options = self._validated_options()
+        used = sorted({gi for gi, _, _ in self._entries()})
+        if len(used) > N.NT_MAX_GROUPS:
+            raise RuntimeError(f"ZeroAdamW supports at most {N.NT_MAX_GROUPS} parameter groups.")
+        local = {gi: k for k, gi in enumerate(used)}
+        structs = [self._group_struct(options[gi]) for gi in used]
+        self.corrections.ensure(self.max_step + 1)
+        return structs, self._piece_tables(local)
+
+    def _launch_update(self, table, structs, amp, j: int, peers):
+        """The fused AdamW kernel over piece j of the shard (pushing into `peers` if given)."""
+        if table is None:
+            return
+        segs, nseg, nchunks = table
+        self._kernels.update(
+            master=self.master, exp_avg=self.exp_avg, exp_avg_sq=self.exp_avg_sq, copy=self._copy_base(j),
+            grad_dtype=self.grad_shard.dtype, segments=segs, num_segments=nseg, num_chunks=nchunks,
+            steps=self.steps, corrections=self.corrections.tensor, capacity=self.corrections.capacity,
+            scale=None if amp is None else amp.scale, stats=None if amp is None else amp.stats,
+            skip=bool(amp is not None and amp.skip), max_norm=None if amp is None else amp.max_norm,
+            groups=structs, peers=peers)
+
+    def benchmark_shard_update(self, iters: int) -> float:
+        """Mean device time (ms) of the shard's AdamW update alone -- no reduce-scatter, no
+        statistics, no all-gather or push -- over `iters` launches. It advances the optimizer
+        state like that many un-scaled, un-clipped steps on the current reduced gradients, so
+        call it only when the state no longer matters (a benchmark's last phase)."""
+        structs, tables = self._update_plan()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for j in range(self._pieces):
+            self._launch_update(tables[j], structs, None, j, None)
+        start.record()
+        for _ in range(iters):
+            for j in range(self._pieces):
+                self._launch_update(tables[j], structs, None, j, None)
+        end.record()
+        end.synchronize()
+        return start.elapsed_time(end) / iters
 
     def _copy_base(self, j: int) -> torch.Tensor:
         """The model copy as the kernel addresses it for piece j: the kernel writes element

@@ -15,7 +15,8 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-WORLD = 2
+# Ranks (one GPU each); NT_ZERO_TEST_WORLD raises it on a box with more GPUs.
+WORLD = int(os.environ.get("NT_ZERO_TEST_WORLD", "2"))
 
 
 def _free_port() -> int:

@@ -100,7 +100,8 @@ class NumpyShardKernels:
         buf.copy_(torch.from_numpy(np.clip(g, -bound, bound).astype(np.float32)))
 
     def update(self, *, master, exp_avg, exp_avg_sq, copy, grad_dtype, segments, num_segments, num_chunks, steps,
-               corrections, capacity, scale, stats, skip, max_norm, groups):
+               corrections, capacity, scale, stats, skip, max_norm, groups, peers=None):
+        assert not peers   # the CPU ranks use the collective transport
         s = None if stats is None else stats.numpy()
         if skip and s[6] != 0:
             return
