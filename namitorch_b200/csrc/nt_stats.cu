@@ -23,8 +23,65 @@ __device__ __forceinline__ void stats_pass1(float u, double p, double maxabs, St
   a.ps += p == 2.0 ? scaled * scaled : pow(scaled, p);
 }
 
-// One chunk of one span: 16-byte vectors, kUnroll of them in flight per thread.
-template <int DT, int MODE, int PASS>
+// Pass-0 variants. EXACT follows the reference's per-element float32 unscale and counts
+// every non-finite value. SUMSQ serves p = 2 with no scale or a power-of-two scale <= 1:
+// it sums g^2 of the stored values in f64 (the scale's square, a power of two, is applied
+// once at the end, and g * scale^-1 cannot overflow float32 when scale >= 1), tracks max|g|
+// and skips the per-element finiteness test. A sum of squares of finite float32 values
+// cannot overflow f64 (at most 1.2e77 * 2^31), so a thread's sum is non-finite exactly when
+// one of its values is inf or NaN; that thread then re-reads its own elements with EXACT to
+// count them. The f64 square of g * 2^-k differs from the square of the float32 product only
+// when that product is an f32 subnormal (|g * 2^-k| < 2^-126), by less than 2^-250 each.
+enum { kPassExact = 0, kPassSumsq = 1, kPassPow = 2 };
+
+template <int VARIANT> struct PassShape {   // threads per block and 16-byte vectors in flight per thread
+  static constexpr int kThreads = VARIANT == kPassSumsq ? 128 : kStatsThreads;
+  static constexpr int kUnrollV = VARIANT == kPassSumsq ? 8 : kUnroll;
+};
+
+template <int DT, int MODE, int VARIANT>
+__device__ __forceinline__ void stats_vector(const uint4& raw, float scale, float inv, double maxabs, double p,
+                                             StatsAcc& a) {
+  constexpr int EPV = DT == NT_F32 ? 4 : 8;
+  float x[EPV];
+  unpack16<DT>(raw, x);
+  if constexpr (VARIANT == kPassSumsq) {
+#pragma unroll
+    for (int q = 0; q < EPV; ++q) {
+      a.mx = fmaxf(a.mx, fabsf(x[q]));
+      const double d = (double)x[q];
+      if (q & 1) a.ss1 = fma(d, d, a.ss1);
+      else a.ss0 = fma(d, d, a.ss0);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < EPV; ++q) x[q] = unscale_by<MODE>(x[q], scale, inv);
+    if constexpr (VARIANT == kPassExact) {
+      stats_pass0<EPV>(x, a);
+    } else {
+#pragma unroll
+      for (int q = 0; q < EPV; ++q) stats_pass1(x[q], p, maxabs, a);
+    }
+  }
+}
+
+template <int DT, int MODE, int VARIANT>
+__device__ __forceinline__ void stats_scalar(float g, float scale, float inv, double maxabs, double p, StatsAcc& a) {
+  if constexpr (VARIANT == kPassSumsq) {
+    a.mx = fmaxf(a.mx, fabsf(g));
+    const double d = (double)g;
+    a.ss0 = fma(d, d, a.ss0);
+  } else {
+    const float u = unscale_by<MODE>(g, scale, inv);
+    if constexpr (VARIANT == kPassExact) stats_one(u, a);
+    else stats_pass1(u, p, maxabs, a);
+  }
+}
+
+// One chunk of one span: 16-byte vectors, U of them in flight per thread (guard-free full
+// rounds, then the remainder), then the elements after the last 16-byte boundary. T is the
+// block size of the launch (the kernel's shape, whichever path a thread takes).
+template <int DT, int MODE, int VARIANT, int T, int U>
 __device__ __forceinline__ void stats_chunk(const StatsParams& P, const nt_span& sp, int64_t begin, int64_t end,
                                             float scale, float inv, double maxabs, StatsAcc& a) {
   constexpr int ES = DT == NT_F32 ? 4 : 2;
@@ -33,42 +90,25 @@ __device__ __forceinline__ void stats_chunk(const StatsParams& P, const nt_span&
   int64_t e = begin;
   if (((reinterpret_cast<uintptr_t>(base + begin * ES)) & 15u) == 0) {
     const uint4* vec = reinterpret_cast<const uint4*>(base + begin * ES);
-    const int64_t nv = (end - begin) / EPV;
-    for (int64_t v0 = threadIdx.x; v0 < nv; v0 += (int64_t)blockDim.x * kUnroll) {
-      uint4 raw[kUnroll];
+    const int nv = (int)((end - begin) / EPV);   // a chunk holds at most 2^31 elements
+    int v0 = threadIdx.x;
+    for (; v0 + (U - 1) * T < nv; v0 += U * T) {
+      uint4 raw[U];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int64_t v = v0 + (int64_t)u * blockDim.x;
-        if (v < nv) raw[u] = __ldcs(vec + v);
-      }
+      for (int u = 0; u < U; ++u) raw[u] = __ldcs(vec + v0 + u * T);
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        if (v0 + (int64_t)u * blockDim.x < nv) {
-          float x[EPV];
-          unpack16<DT>(raw[u], x);
-#pragma unroll
-          for (int q = 0; q < EPV; ++q) x[q] = unscale_by<MODE>(x[q], scale, inv);
-          if constexpr (PASS == 0) {
-            stats_pass0<EPV>(x, a);
-          } else {
-#pragma unroll
-            for (int q = 0; q < EPV; ++q) stats_pass1(x[q], P.p, maxabs, a);
-          }
-        }
-      }
+      for (int u = 0; u < U; ++u) stats_vector<DT, MODE, VARIANT>(raw[u], scale, inv, maxabs, P.p, a);
     }
-    e = begin + nv * EPV;
+    for (; v0 < nv; v0 += T) stats_vector<DT, MODE, VARIANT>(__ldcs(vec + v0), scale, inv, maxabs, P.p, a);
+    e = begin + (int64_t)nv * EPV;
   }
-  for (int64_t i = e + threadIdx.x; i < end; i += blockDim.x) {
-    const float u = unscale_by<MODE>(load1<DT>(sp.ptr, i), scale, inv);
-    if constexpr (PASS == 0) stats_one(u, a);
-    else stats_pass1(u, P.p, maxabs, a);
-  }
+  for (int64_t i = e + threadIdx.x; i < end; i += T)
+    stats_scalar<DT, MODE, VARIANT>(load1<DT>(sp.ptr, i), scale, inv, maxabs, P.p, a);
 }
 
 // Each block takes a contiguous range of chunks: one span lookup per block, then the span
 // record is carried in registers and advanced as the chunks cross span boundaries.
-template <int DT, int MODE, int PASS>
+template <int DT, int MODE, int VARIANT, int T, int U>
 __device__ __forceinline__ void stats_all_chunks(const StatsParams& P, float scale, float inv, double maxabs,
                                                  StatsAcc& a) {
   const int64_t per = (P.nchunks + gridDim.x - 1) / gridDim.x;
@@ -87,29 +127,52 @@ __device__ __forceinline__ void stats_all_chunks(const StatsParams& P, float sca
     const int64_t begin = (chunk - sp.chunk_begin) * (int64_t)P.chunk_elems;
     int64_t end = begin + P.chunk_elems;
     if (end > sp.count) end = sp.count;
-    stats_chunk<DT, MODE, PASS>(P, sp, begin, end, scale, inv, maxabs, a);
+    stats_chunk<DT, MODE, VARIANT, T, U>(P, sp, begin, end, scale, inv, maxabs, a);
   }
 }
 
-template <int DT, int PASS>
+// kPassSumsq applies when the launch chose it (p = 2, pass 0) and the device scale allows
+// it; the block shape is the same for both, so the choice is per thread at run time.
+template <int DT, int VARIANT>
 __device__ __forceinline__ void stats_dispatch_scale(const StatsParams& P, const Unscale& un, double maxabs,
                                                      StatsAcc& a) {
-  if (!un.active) stats_all_chunks<DT, kScaleNone, PASS>(P, 1.0f, 1.0f, maxabs, a);
-  else if (un.pow2) stats_all_chunks<DT, kScaleMul, PASS>(P, un.scale, un.inv, maxabs, a);
-  else stats_all_chunks<DT, kScaleDiv, PASS>(P, un.scale, un.inv, maxabs, a);
+  constexpr int T = PassShape<VARIANT>::kThreads;
+  constexpr int U = PassShape<VARIANT>::kUnrollV;
+  if constexpr (VARIANT == kPassSumsq) {
+    if (!un.active || (un.pow2 && un.inv <= 1.0f)) {
+      StatsAcc f{0.0, 0.0, 0.0, 0.0f, 0u, 0u};
+      stats_all_chunks<DT, kScaleNone, kPassSumsq, T, U>(P, 1.0f, 1.0f, maxabs, f);
+      if (isfinite(f.ss0) && isfinite(f.ss1)) {
+        const double s2 = un.active ? (double)un.inv * (double)un.inv : 1.0;   // exact: a power of two
+        a.ss0 = f.ss0 * s2;
+        a.ss1 = f.ss1 * s2;
+        a.mx = un.active ? __fmul_rn(f.mx, un.inv) : f.mx;
+        return;
+      }
+    }
+  }
+  // The exact per-element path (also the re-read of a thread that saw inf / NaN above).
+  constexpr int V = VARIANT == kPassPow ? kPassPow : kPassExact;
+  constexpr int UE = kUnroll;   // the exact path is rare inside the sumsq kernel: keep its registers low
+  if (!un.active) stats_all_chunks<DT, kScaleNone, V, T, UE>(P, 1.0f, 1.0f, maxabs, a);
+  else if (un.pow2) stats_all_chunks<DT, kScaleMul, V, T, UE>(P, un.scale, un.inv, maxabs, a);
+  else stats_all_chunks<DT, kScaleDiv, V, T, UE>(P, un.scale, un.inv, maxabs, a);
 }
 
-template <int DT, int PASS>
-__global__ void __launch_bounds__(kStatsThreads, 4) grad_stats_kernel(const __grid_constant__ StatsParams P) {
-  __shared__ double red_d[kStatsThreads / 32];
-  __shared__ float red_f[kStatsThreads / 32];
-  __shared__ unsigned red_u[kStatsThreads / 32];
+template <int DT, int VARIANT>
+__global__ void __launch_bounds__(PassShape<VARIANT>::kThreads, 2048 / PassShape<VARIANT>::kThreads / 2)
+    grad_stats_kernel(const __grid_constant__ StatsParams P) {
+  constexpr int T = PassShape<VARIANT>::kThreads;
+  constexpr int PASS = VARIANT == kPassPow ? 1 : 0;
+  __shared__ double red_d[T / 32];
+  __shared__ float red_f[T / 32];
+  __shared__ unsigned red_u[T / 32];
   __shared__ bool last;
   Unscale un;
   un.init(P.scale);
   const double maxabs = PASS == 1 ? P.stats->maxabs : 0.0;
   StatsAcc a{0.0, 0.0, 0.0, 0.0f, 0u, 0u};
-  stats_dispatch_scale<DT, PASS>(P, un, maxabs, a);
+  stats_dispatch_scale<DT, VARIANT>(P, un, maxabs, a);
 
   double ss = block_reduce(a.ss0 + a.ss1, red_d, SumOp(), 0.0);
   double ps = block_reduce(a.ps, red_d, SumOp(), 0.0);
@@ -271,18 +334,21 @@ static int launch_grid(K kernel, const Params& P, int64_t nchunks, int threads, 
   return launch_status(what);
 }
 
+template <int DT>
+static int launch_stats_dt(const StatsParams& P, int64_t nchunks, cudaStream_t s, const char* what) {
+  if (P.pass == 1)
+    return launch_grid(grad_stats_kernel<DT, kPassPow>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what);
+  if (P.p == 2.0)
+    return launch_grid(grad_stats_kernel<DT, kPassSumsq>, P, nchunks, PassShape<kPassSumsq>::kThreads, 8,
+                       kStatsMaxBlocks, s, what);
+  return launch_grid(grad_stats_kernel<DT, kPassExact>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what);
+}
+
 static int launch_stats(const StatsParams& P, int32_t dtype, int64_t nchunks, cudaStream_t s, const char* what) {
-  const bool p1 = P.pass == 1;
   switch (dtype) {
-    case NT_F32:
-      return p1 ? launch_grid(grad_stats_kernel<NT_F32, 1>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what)
-                : launch_grid(grad_stats_kernel<NT_F32, 0>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what);
-    case NT_F16:
-      return p1 ? launch_grid(grad_stats_kernel<NT_F16, 1>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what)
-                : launch_grid(grad_stats_kernel<NT_F16, 0>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what);
-    default:
-      return p1 ? launch_grid(grad_stats_kernel<NT_BF16, 1>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what)
-                : launch_grid(grad_stats_kernel<NT_BF16, 0>, P, nchunks, kStatsThreads, 6, kStatsMaxBlocks, s, what);
+    case NT_F32: return launch_stats_dt<NT_F32>(P, nchunks, s, what);
+    case NT_F16: return launch_stats_dt<NT_F16>(P, nchunks, s, what);
+    default: return launch_stats_dt<NT_BF16>(P, nchunks, s, what);
   }
 }
 

@@ -99,10 +99,11 @@ __device__ __forceinline__ void stats_pass0(const float* u, StatsAcc& a) {
 
 // Reduces the per-block partials (fixed order) into the pass-0 fields of `st` once every
 // block has stored its own; returns true in the block that did it.
+template <int THREADS = kStatsThreads>
 __device__ __forceinline__ bool stats_reduce_pass0(const StatsAcc& a, StatsWorkspace* ws, nt_stats* st) {
-  __shared__ double red_d[kStatsThreads / 32];
-  __shared__ float red_f[kStatsThreads / 32];
-  __shared__ unsigned red_u[kStatsThreads / 32];
+  __shared__ double red_d[THREADS / 32];
+  __shared__ float red_f[THREADS / 32];
+  __shared__ unsigned red_u[THREADS / 32];
   __shared__ bool last;
   double ss = block_reduce(a.ss0 + a.ss1, red_d, SumOp(), 0.0);
   float mx = block_reduce(a.mx, red_f, MaxOp(), 0.0f);

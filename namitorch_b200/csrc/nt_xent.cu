@@ -19,7 +19,7 @@
 // read of the logits and one write of dlogits.
 #include <cmath>
 
-#include "nt_common.cuh"
+#include "nt_bulk.cuh"
 
 namespace nt {
 
@@ -49,38 +49,6 @@ struct XentParams {
   int64_t stage_stride;   // bytes per staged row buffer
 };
 
-// ---- PTX helpers (mbarrier + bulk async copy; no cluster multicast) ---------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
 // 2^x on the SFU. Results below 2^-126 flush to zero: a logit that far below the row max
 // contributes nothing to the sum and its gradient is below 2^-126 times the row scale.
 __device__ __forceinline__ float ex2(float x) {
@@ -90,7 +58,6 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per row: far beyond any real copy
 
 template <int DT>
 __device__ __forceinline__ uint4 pack16(const float* v) {
@@ -180,15 +147,6 @@ __device__ __forceinline__ void stage_row(const XentParams& P, int64_t row, unsi
     if (bulk > 0) bulk_g2s(buf, reinterpret_cast<const void*>(a), (uint32_t)bulk, bar);
   }
   for (int k = (int)bulk + threadIdx.x; k < span; k += blockDim.x) buf[k] = *reinterpret_cast<const unsigned char*>(a + k);
-}
-
-// Bounded wait for a staged row; false when the copy did not land within kWaitLimitNs.
-__device__ __forceinline__ bool wait_stage(uint64_t* bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
-  }
-  return true;
 }
 
 // STAGES = 2: double-buffered rows (the next row's copy is in flight while this one is

@@ -148,3 +148,78 @@ def test_scaler_state_dict_roundtrip(cuda_device):
     assert t.state_dict() == d
     with pytest.raises(ValueError):
         t.load_state_dict({**d, "growth_tracker": 99})
+
+
+def _as_dtype(x: np.ndarray, dtype) -> np.ndarray:
+    if dtype is torch.bfloat16:
+        return round_to_bf16(x)
+    if dtype is torch.float16:
+        return x.astype(np.float16).astype(np.float32)
+    return x.astype(np.float32)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("scale", [None, 1024.0, 3.0])
+@pytest.mark.parametrize("poison", [False, True])
+def test_stats_on_misaligned_spans_match_oracle(cuda_device, dtype, scale, poison):
+    """Gradients as views at odd element offsets of one buffer: every chunk starts off a
+    16-byte boundary (the staged kernel masks the first vector and reads the elements after
+    the last boundary with plain loads). With `poison`, a NaN sits in a masked head vector
+    and an inf in a plain-load tail."""
+    rng = np.random.default_rng(5)
+    sizes = [1, 3, 7, 8, 9, 15, 17, 8191, 8192, 8193, 16385, 50001]
+    offsets, off = [], 1
+    for n in sizes:
+        offsets.append(off)
+        off += n + 3
+    flat = _as_dtype(rng.normal(0, 1, off + 8).astype(np.float32) * np.float32(scale or 1.0), dtype)
+    if poison:
+        flat[offsets[9]] = np.nan                    # first element of an unaligned span
+        flat[offsets[10] + sizes[10] - 1] = np.inf   # last element of another
+    buf = torch.from_numpy(flat).cuda().to(dtype)
+    views = [buf[o:o + n] for o, n in zip(offsets, sizes)]
+    arrays = [flat[o:o + n].copy() for o, n in zip(offsets, sizes)]
+    scale_t = None if scale is None else torch.tensor([scale], dtype=torch.float32, device="cuda")
+    stats = grad_stats_for(views, scale=scale_t)
+    s = dict(zip(N.STATS_FIELDS, stats.cpu().numpy()))
+    unscaled = [a if scale is None else a / np.float32(scale) for a in arrays]
+    if poison:
+        assert s["nonfinite"] == 2 and s["nan"] == 1 and s["found_inf"] == 1.0 and math.isnan(s["norm"])
+        return
+    ref = float(oclip.total_norm(unscaled, 2.0))
+    assert abs(s["norm"] - ref) <= 1e-12 * ref
+    assert s["maxabs"] == max(float(np.max(np.abs(u))) for u in unscaled)
+    assert s["found_inf"] == 0.0 and s["error"] == 0.0
+
+
+@pytest.mark.parametrize("dtype,values,scale", [
+    # f32(g / 0.25) overflows for g = 2^126: found_inf, as the reference's float32 unscale.
+    (torch.bfloat16, [1.0, 2.0 ** 126, -3.0], 0.25),
+    (torch.float32, [1.0, 2.0 ** 126, -3.0], 0.25),
+    # Below-overflow neighbour: stays finite.
+    (torch.bfloat16, [1.0, 2.0 ** 125, -3.0], 0.25),
+    # fp16 with a tiny scale (2^-20): the bit-level pass declines it (2^(1008+20) is not a
+    # double); the conversion path gives the same answer.
+    (torch.float16, [1.0, 60000.0, -2.0 ** -24], 2.0 ** -20),
+    # Exact zeros and subnormals of every format.
+    (torch.bfloat16, [0.0, -0.0, 2.0 ** -133, 1e-3, 0.0], 1.0),
+    (torch.float16, [0.0, 2.0 ** -24, -2.0 ** -20, 0.5], 65536.0),
+    (torch.float32, [0.0, 2.0 ** -149, -2.0 ** -130, 7.0], 1.0),
+])
+def test_pow2_scale_edges_match_reference_unscale(cuda_device, dtype, values, scale):
+    g = np.asarray(values, np.float32)
+    t = torch.from_numpy(g).cuda().to(dtype)
+    stored = t.float().cpu().numpy()
+    stats = grad_stats_for([t], scale=torch.tensor([scale], dtype=torch.float32, device="cuda"))
+    s = dict(zip(N.STATS_FIELDS, stats.cpu().numpy()))
+    with np.errstate(over="ignore"):
+        u = stored / np.float32(scale)   # the reference's float32 unscale
+    finite = np.isfinite(u)
+    assert s["nonfinite"] == np.count_nonzero(~finite)
+    assert s["found_inf"] == (0.0 if finite.all() else 1.0)
+    if finite.all():
+        ref = float(oclip.total_norm([u], 2.0))
+        assert abs(s["norm"] - ref) <= 1e-12 * ref
+        assert s["maxabs"] == float(np.max(np.abs(u)))
+    else:
+        assert s["norm"] == np.inf
