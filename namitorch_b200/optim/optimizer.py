@@ -167,7 +167,10 @@ class Optimizer:
             "defaults": self._prepare_options(self.defaults, "defaults"),
             "param_groups": groups,
             "param_shapes": [list(parameter.shape) for parameter in parameters],
-            "state": self._export_state(parameters),
+            # Per-parameter fields in sorted order, as the reference's state copy emits them
+            # (so a checkpoint archive of this state has the reference's metadata bytes).
+            "state": {index: {name: values[name] for name in sorted(values)}
+                      for index, values in self._export_state(parameters).items()},
         }
 
     def load_state_dict(self, state_dict: dict) -> None:
@@ -221,8 +224,16 @@ class Optimizer:
                 raise ValueError("Loaded state keys must be registered parameter indices.")
             if not isinstance(values, dict):
                 raise TypeError(f"Loaded state[{index}] must be a dictionary.")
-        self._import_state(index_to_parameter, saved_state)
+        # The loaded groups decide where the state lives (their `fused` option selects the
+        # multi-tensor arenas or per-tensor buffers), so they are installed first and put
+        # back if the state is rejected.
+        previous = (self.defaults, self.param_groups)
         self.defaults, self.param_groups = defaults, restored_groups
+        try:
+            self._import_state(index_to_parameter, saved_state)
+        except BaseException:
+            self.defaults, self.param_groups = previous
+            raise
 
     def __repr__(self) -> str:
         return f"{type(self).__name__}(param_groups={len(self.param_groups)})"
