@@ -372,6 +372,8 @@ def run_ours(args):
                             "floor_ms": link_bytes / 770e9 * 1e3,
                             "frac_of_step": link_bytes / 770e9 * 1e3 / ms}
 
+    if world == 1:
+        result["loop"] = loop_tail(args, opt, scaler, params, loss)
     if not args.no_e2e:
         result["e2e"] = e2e_ours(args, opt, scaler, params, flat_grads, loss, world)
     # The update alone (the HBM-bound part that shards), for the update-scaling figure
@@ -397,6 +399,50 @@ def run_ours(args):
         dist.barrier()
         opt.close()
         dist.destroy_process_group()
+
+
+def loop_tail(args, opt, scaler, params, loss, steps: int = 30):
+    """The training loop's optimizer tail (namitorch/training/runner.py:247-254) two ways:
+    as the reference writes it, reading found_inf, the norm and the step outcome on the host
+    each iteration, and with the scheduler gated on the device (no host reads). Device-timed
+    with CUDA events around `steps` iterations after 3 warm-up iterations."""
+    import torch
+    from namitorch_b200.optim import WarmupCosine, clip_grad_norm_
+
+    def synced(sched):
+        scaler.scale(loss)
+        finite = scaler.unscale_(opt)
+        norm = clip_grad_norm_(params, 1.0).item() if finite else None
+        updated = scaler.step(opt)
+        scaler.update()
+        if updated:
+            sched.step()
+        return norm
+
+    def gated(sched):
+        scaler.scale(loss)
+        scaler.unscale_(opt)
+        clip_grad_norm_(params, 1.0)
+        updated = scaler.step(opt)
+        scaler.update()
+        sched.step(updated)
+
+    out = {}
+    for name, body in (("host_reads", synced), ("device_gated", gated)):
+        sched = WarmupCosine(opt, warmup_steps=100, total_steps=100000)
+        for _ in range(3):
+            body(sched)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            body(sched)
+        end.record()
+        end.synchronize()
+        out[name + "_ms_per_step"] = start.elapsed_time(end) / steps
+    out["what"] = ("unscale_ + clip_grad_norm_ + step + update + WarmupCosine step per iteration; host_reads: "
+                   "the reference loop's found_inf / norm.item() / `if updated` reads")
+    return out
 
 
 def e2e_ours(args, opt, scaler, params, flat_grads, loss, world):

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define NT_ABI_VERSION 2
+#define NT_ABI_VERSION 3
 #define NT_MAX_GROUPS 32      /* coefficient groups per nt_adamw_mt call */
 #define NT_MAX_FOUND_INF 16   /* optimizers combined by one nt_scaler_update call */
 
@@ -120,7 +120,19 @@ typedef struct nt_adamw_group {
   int32_t decay_mode;        /* NT_DECAY_*: decided from the unrounded weight decay != 0 */
   int32_t update_parameter;  /* 0 when lr == 0: moments and step still advance (adam.py:87) */
   int32_t correction_row;    /* row of this group in the bias-correction table */
+  int32_t schedule_column;   /* column of this group in args.lr_schedule (ignored without one) */
+  int32_t reserved;
 } nt_adamw_group;
+
+/* One learning-rate schedule entry of one parameter group for one scheduler step: the three
+   lr-dependent coefficients, computed on the host exactly as the reference computes them
+   from the scheduled lr (_scalar(lr), _scalar(1 - lr*wd), lr != 0). */
+typedef struct nt_lr_entry {
+  float lr;
+  float decay_factor;
+  int32_t update_parameter;
+  int32_t reserved;
+} nt_lr_entry;
 
 enum {
   NT_DECAY_NONE = 0,
@@ -165,6 +177,13 @@ typedef struct nt_adamw_mt_args {
   int32_t* error;                 /* device error word (may be NULL) */
   const nt_adamw_group* groups;   /* host array of num_groups entries */
   int32_t num_groups;             /* 1..NT_MAX_GROUPS */
+  /* Optional device-side learning-rate schedule (no host round trip per step): when set, each
+     group's lr, decay factor and update flag come from
+     lr_schedule[min(*lr_step, rows - 1) * columns + group.schedule_column]. */
+  const nt_lr_entry* lr_schedule; /* device [rows][columns] or NULL */
+  int32_t lr_schedule_rows;
+  int32_t lr_schedule_columns;
+  const int32_t* lr_step;         /* device: the scheduler's step (nt_schedule_step advances it) */
 } nt_adamw_mt_args;
 
 size_t nt_adamw_workspace_size(void);
@@ -232,6 +251,12 @@ int nt_grad_stats(const nt_grad_stats_args* args, void* stream);
 size_t nt_grad_stats_noalloc_scratch_bytes(void);
 int nt_grad_stats_noalloc(const nt_span* spans, int32_t num_spans, int32_t dtype, const float* scale,
                           double norm_type, nt_stats* stats, void* stream);
+
+/* The scheduler step gated on the device: *lr_step += 1 when every found_inf[i] is 0
+   (count == 0: unconditionally). Replaces `if updated: scheduler.step()` of the training
+   loop (namitorch/training/runner.py:250-254), which needs found_inf on the host.
+   `found_inf` is a host array of `count` device pointers (nt_stats.found_inf fields). */
+int nt_schedule_step(int32_t* lr_step, const double* const* found_inf, int32_t count, void* stream);
 
 /* Computes norm and found_inf from the reduced fields (after a ZeRO-1 all-reduce). */
 int nt_grad_stats_finalize(nt_stats* stats, double norm_type, void* stream);

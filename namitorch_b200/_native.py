@@ -22,7 +22,7 @@ NT_DECAY_NONE, NT_DECAY_DECOUPLED, NT_DECAY_COUPLED = 0, 1, 2
 NT_MAX_GROUPS = 32
 NT_MAX_FOUND_INF = 16
 NT_MAX_RANKS = 8
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class Segment(C.Structure):
@@ -34,7 +34,13 @@ class AdamWGroup(C.Structure):
     _fields_ = [("lr", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float), ("one_minus_beta1", C.c_float),
                 ("one_minus_beta2", C.c_float), ("eps", C.c_float), ("weight_decay", C.c_float),
                 ("decay_factor", C.c_float), ("maximize", C.c_int32), ("decay_mode", C.c_int32),
-                ("update_parameter", C.c_int32), ("correction_row", C.c_int32)]
+                ("update_parameter", C.c_int32), ("correction_row", C.c_int32), ("schedule_column", C.c_int32),
+                ("reserved", C.c_int32)]
+
+
+class LrEntry(C.Structure):
+    _fields_ = [("lr", C.c_float), ("decay_factor", C.c_float), ("update_parameter", C.c_int32),
+                ("reserved", C.c_int32)]
 
 
 class Stats(C.Structure):
@@ -54,7 +60,8 @@ class AdamWMtArgs(C.Structure):
                 ("correction_capacity", C.c_int32), ("scale", C.c_void_p), ("stats", C.c_void_p),
                 ("skip_nonfinite", C.c_int32), ("clip", C.c_int32), ("max_norm", C.c_double),
                 ("workspace", C.c_void_p), ("error", C.c_void_p), ("groups", C.POINTER(AdamWGroup)),
-                ("num_groups", C.c_int32)]
+                ("num_groups", C.c_int32), ("lr_schedule", C.c_void_p), ("lr_schedule_rows", C.c_int32),
+                ("lr_schedule_columns", C.c_int32), ("lr_step", C.c_void_p)]
 
 
 class Span(C.Structure):
@@ -112,6 +119,7 @@ SIGNATURES: dict[str, tuple] = {
     "nt_grad_stats_workspace_size": (C.c_size_t, []),
     "nt_grad_stats": (C.c_int, [C.POINTER(GradStatsArgs), C.c_void_p]),
     "nt_grad_stats_finalize": (C.c_int, [C.c_void_p, C.c_double, C.c_void_p]),
+    "nt_schedule_step": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.c_int32, C.c_void_p]),
     "nt_grad_stats_noalloc_scratch_bytes": (C.c_size_t, []),
     "nt_grad_stats_noalloc": (C.c_int, [C.POINTER(Span), C.c_int32, C.c_int32, C.c_void_p, C.c_double,
                                         C.c_void_p, C.c_void_p]),
@@ -183,7 +191,7 @@ def check(status: int, what: str = "") -> None:
 # Kernel launches issued per successful call of each launching entry point (for the
 # benchmark's launch count; the statistics entry point launches one kernel per call).
 LAUNCHES_PER_CALL = {"nt_adamw_f32": 1, "nt_adamw_mt": 1, "nt_adamw_mt_push": 1, "nt_zero_reduce_scatter_stats": 1,
-                     "nt_grad_stats": 1, "nt_grad_stats_finalize": 1,
+                     "nt_grad_stats": 1, "nt_grad_stats_finalize": 1, "nt_schedule_step": 1,
                      "nt_grad_stats_noalloc": 2,
                      "nt_grad_transform": 1, "nt_grad_clip_value": 1, "nt_scaler_update": 1,
                      "nt_softmax_xent": 2, "nt_xent_backward_scale": 1, "nt_cast": 1}

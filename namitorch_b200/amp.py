@@ -215,10 +215,20 @@ class GradScaler:
             raise TypeError("GradScaler requires a NamiTorch optimizer.")
         if not callable(getattr(optimizer, "_amp_unscale_", None)):
             raise TypeError("GradScaler requires a namitorch_b200 optimizer.")
-        gradients = tuple((p, g) for _, p, g in optimizer._parameters_with_grad())
+        entries_of = getattr(optimizer, "_grad_entries", None)
+        if entries_of is None:   # any optimizer exposing the reference's gradient walk
+            entries = [(None, group, p, g) for group, p, g in optimizer._parameters_with_grad()]
+        else:
+            entries = entries_of()
+            cached = getattr(optimizer, "_scaler_gradients", None)
+            if cached is not None and cached[0] is entries:
+                return cached[1]
+        gradients = tuple((p, g) for _, _, p, g in entries)
         for p, g in gradients:
             if not p.dtype.is_floating_point or g.requires_grad or g.grad_fn is not None:
                 raise RuntimeError("GradScaler requires detached floating gradients.")
+        if entries_of is not None:
+            optimizer._scaler_gradients = (entries, gradients)   # valid while the entries list is
         return gradients
 
     def unscale_(self, optimizer):

@@ -122,6 +122,10 @@ struct MtParams {
   int ngroups;
   int npeers;                        // other model copies the update also writes (ZeRO-1)
   void* peers[NT_MAX_RANKS - 1];
+  const nt_lr_entry* sched;          // device lr schedule or NULL
+  int sched_rows;
+  int sched_cols;
+  const int32_t* sched_step;
   nt_adamw_group groups[NT_MAX_GROUPS];
 };
 
@@ -204,6 +208,11 @@ __global__ void __launch_bounds__(256) adamw_mt_kernel(const __grid_constant__ M
     if (c < 1.0) { clip = true; coef = c; }
   }
   const int gsize = GDT == NT_F32 ? 4 : 2;
+  int sched_row = 0;
+  if (P.sched != nullptr) {
+    sched_row = *P.sched_step;
+    sched_row = sched_row < 0 ? 0 : (sched_row >= P.sched_rows ? P.sched_rows - 1 : sched_row);
+  }
 
   // Each block takes a contiguous range of chunks: one segment lookup per block, then the
   // segment's record, coefficients and bias corrections are carried in registers until the
@@ -234,6 +243,10 @@ __global__ void __launch_bounds__(256) adamw_mt_kernel(const __grid_constant__ M
       c.lr = gr.lr; c.b1 = gr.beta1; c.b2 = gr.beta2; c.c1 = gr.one_minus_beta1; c.c2 = gr.one_minus_beta2;
       c.eps = gr.eps; c.wd = gr.weight_decay; c.decay = gr.decay_factor; c.corr1 = corr.x; c.corr2 = corr.y;
       c.decay_mode = gr.decay_mode; c.maximize = gr.maximize != 0; c.update = gr.update_parameter != 0;
+      if (P.sched != nullptr) {   // this step's scheduled lr-dependent coefficients
+        const nt_lr_entry e = P.sched[(int64_t)sched_row * P.sched_cols + gr.schedule_column];
+        c.lr = e.lr; c.decay = e.decay_factor; c.update = e.update_parameter != 0;
+      }
     }
     if (!seg_ok) continue;
 
@@ -342,6 +355,23 @@ static int build_mt_params(const nt_adamw_mt_args* args, MtParams& P) {
   P.error = a.error;
   P.ngroups = a.num_groups;
   for (int i = 0; i < a.num_groups; ++i) P.groups[i] = a.groups[i];
+  P.sched = a.lr_schedule;
+  P.sched_rows = a.lr_schedule_rows;
+  P.sched_cols = a.lr_schedule_columns;
+  P.sched_step = a.lr_step;
+  if (a.lr_schedule) {
+    if (!a.lr_step || a.lr_schedule_rows < 1 || a.lr_schedule_columns < 1) {
+      set_error("nt_adamw_mt: lr_schedule needs lr_step, rows >= 1 and columns >= 1");
+      return NT_EINVAL;
+    }
+    for (int i = 0; i < a.num_groups; ++i) {
+      if (a.groups[i].schedule_column < 0 || a.groups[i].schedule_column >= a.lr_schedule_columns) {
+        set_error("nt_adamw_mt: group %d schedule_column %d outside [0, %d)", i, a.groups[i].schedule_column,
+                  a.lr_schedule_columns);
+        return NT_EINVAL;
+      }
+    }
+  }
   return NT_OK;
 }
 

@@ -311,6 +311,19 @@ __global__ void scaler_update_kernel(const __grid_constant__ ScalerParams P) {
   }
 }
 
+struct ScheduleParams {
+  int32_t* step;
+  const double* found[NT_MAX_FOUND_INF];
+  int count;
+};
+
+__global__ void schedule_step_kernel(const __grid_constant__ ScheduleParams P) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  bool inf = false;
+  for (int i = 0; i < P.count; ++i) inf = inf || (*P.found[i] != 0.0);
+  if (!inf) *P.step += 1;
+}
+
 static int check_spans(const nt_span* spans, int32_t num_spans, int32_t chunk_elems, int64_t num_chunks,
                        int32_t dtype, const char* who) {
   if (num_spans < 0 || num_chunks < 0) { set_error("%s: negative sizes", who); return NT_EINVAL; }
@@ -381,6 +394,23 @@ int nt_grad_stats(const nt_grad_stats_args* args, void* stream) {
   // An empty gradient list still runs one block so the statistics are written.
   const int64_t nchunks = P.nchunks > 0 ? P.nchunks : 1;
   return launch_stats(P, a.dtype, nchunks, s, "nt_grad_stats launch");
+}
+
+int nt_schedule_step(int32_t* lr_step, const double* const* found_inf, int32_t count, void* stream) {
+  if (!lr_step) { set_error("nt_schedule_step: lr_step is NULL"); return NT_EINVAL; }
+  if (count < 0 || count > NT_MAX_FOUND_INF || (count > 0 && !found_inf)) {
+    set_error("nt_schedule_step: count must be in [0, %d] with a pointer array", NT_MAX_FOUND_INF);
+    return NT_EINVAL;
+  }
+  ScheduleParams P;
+  P.step = lr_step;
+  P.count = count;
+  for (int i = 0; i < count; ++i) {
+    if (!found_inf[i]) { set_error("nt_schedule_step: found_inf[%d] is NULL", i); return NT_EINVAL; }
+    P.found[i] = found_inf[i];
+  }
+  schedule_step_kernel<<<1, 32, 0, as_stream(stream)>>>(P);
+  return launch_status("nt_schedule_step launch");
 }
 
 int nt_grad_stats_finalize(nt_stats* stats, double norm_type, void* stream) {

@@ -157,8 +157,9 @@ class FusedAdamEngine:
 
     def step(self, entries: list[tuple[int, torch.Tensor, torch.Tensor]], group_options: list[dict], *,
              decoupled: bool, scale: torch.Tensor | None = None, stats: torch.Tensor | None = None,
-             skip_nonfinite: bool = False, max_norm: float | None = None) -> None:
-        """One update of every (group index, parameter, gradient) entry."""
+             skip_nonfinite: bool = False, max_norm: float | None = None, schedule=None) -> None:
+        """One update of every (group index, parameter, gradient) entry. `schedule` is a
+        device learning-rate schedule (table, rows, columns, step pointer) or None."""
         if not entries:
             return
         self.ensure_moments()
@@ -167,27 +168,39 @@ class FusedAdamEngine:
             batch = used[start:start + N.NT_MAX_GROUPS]
             local = {gi: k for k, gi in enumerate(batch)}
             structs = [self.group_struct(group_options[gi], decoupled) for gi in batch]
-            selected = [e for e in entries if e[0] in local]
-            self._launch(selected, local, structs, scale, stats, skip_nonfinite, max_norm)
+            for gi, st in zip(batch, structs):
+                st.schedule_column = gi
+            selected = entries if len(batch) == len(used) else [e for e in entries if e[0] in local]
+            self._launch(selected, local, structs, scale, stats, skip_nonfinite, max_norm, schedule)
         self.max_step += 1
 
-    def _launch(self, entries, local, structs, scale, stats, skip_nonfinite, max_norm) -> None:
+    def _launch(self, entries, local, structs, scale, stats, skip_nonfinite, max_norm, schedule=None) -> None:
         self.corrections.ensure(self.max_step + 1)
         keep = []
-        rows = []
-        for gi, p, g in entries:
-            i = self.index[id(p)]
-            if not g.is_contiguous():
-                g = g.contiguous()
-                keep.append(g)
-            rows.append((g.data_ptr(), self.layout.offsets[i], p.numel(), local[gi], i))
-        key = tuple(rows)
-        if key != self._segments_key:
-            table, nchunks = segment_table(rows, CHUNK)
-            self._segments = upload(table, self.device)
-            self._segments_key = key
-            self._num_segments = len(rows)
-            self._num_chunks = nchunks
+        # The segment table depends on the entries, their group mapping and every gradient's
+        # address; the addresses are swept every step (a gradient whose storage moved gets a
+        # new table), the rest is compared by identity.
+        fast_key = (id(entries), tuple(local.items()), tuple(map(torch.Tensor.data_ptr, (g for _, _, g in entries))))
+        cached = self.__dict__.get("_rows_cache")
+        if cached is None or cached[0] != fast_key or cached[1] is not entries:
+            rows = []
+            contiguous = True
+            for gi, p, g in entries:
+                i = self.index[id(p)]
+                if not g.is_contiguous():
+                    g = g.contiguous()
+                    keep.append(g)
+                    contiguous = False
+                rows.append((g.data_ptr(), self.layout.offsets[i], p.numel(), local[gi], i))
+            key = tuple(rows)
+            if key != self._segments_key:
+                table, nchunks = segment_table(rows, CHUNK)
+                self._segments = upload(table, self.device)
+                self._segments_key = key
+                self._num_segments = len(rows)
+                self._num_chunks = nchunks
+            # Non-contiguous gradients are copied every step: nothing to reuse then.
+            self._rows_cache = (fast_key, entries) if contiguous else None
         group_array = (N.AdamWGroup * len(structs))(*structs)
         args = N.AdamWMtArgs(
             param=self.master.data_ptr(), exp_avg=self.exp_avg.data_ptr(), exp_avg_sq=self.exp_avg_sq.data_ptr(),
@@ -202,6 +215,8 @@ class FusedAdamEngine:
             max_norm=float(max_norm) if max_norm is not None else 0.0,
             workspace=self.workspace.data_ptr(), error=self.error.data_ptr(),
             groups=group_array, num_groups=len(structs))
+        if schedule is not None:
+            args.lr_schedule, args.lr_schedule_rows, args.lr_schedule_columns, args.lr_step = schedule
         N.call("nt_adamw_mt", N.C.byref(args), N.stream_handle())
         del keep
 

@@ -128,8 +128,14 @@ class _FirstOrderAdam(Optimizer):
         return self._engine
 
     def _entries(self):
-        index = {id(group): k for k, group in enumerate(self.param_groups)}
-        return [(index[id(group)], parameter, gradient) for group, parameter, gradient in self._parameters_with_grad()]
+        """[(group index, parameter, gradient)], the same list object while nothing changed."""
+        full = self._grad_entries()
+        cached = self.__dict__.get("_entries_view")
+        if cached is not None and cached[0] is full:
+            return cached[1]
+        view = [(index, parameter, gradient) for index, _, parameter, gradient in full]
+        self._entries_view = (full, view)
+        return view
 
     def _validated_options(self) -> list[dict]:
         options = [self._prepare_options({k: v for k, v in group.items() if k != "params"}, "param_group")
@@ -165,18 +171,28 @@ class _FirstOrderAdam(Optimizer):
             engine.step(entries, options, decoupled=self._decoupled_weight_decay,
                         scale=None if amp is None else amp.scale, stats=None if amp is None else amp.stats,
                         skip_nonfinite=bool(amp is not None and amp.skip),
-                        max_norm=None if amp is None else amp.max_norm)
+                        max_norm=None if amp is None else amp.max_norm, schedule=self._device_schedule())
         else:
+            if self._device_schedule() is not None:
+                raise RuntimeError("A device-gated learning-rate schedule needs the fused multi-tensor path "
+                                   "(fused=None or True).")
             self._per_tensor_step(options)
         return loss
+
+    def _device_schedule(self):
+        """(table, rows, columns, step) of a scheduler that moved its step to the device."""
+        scheduler = getattr(self, "_lr_schedule", None)
+        return None if scheduler is None else scheduler._schedule_args()
 
     def _per_tensor_step(self, options):
         raise NotImplementedError
 
     # ---- AMP / clipping hooks used by GradScaler and clip_grad_norm_ ------------------------
-    @staticmethod
-    def _grad_key(entries) -> tuple:
-        return tuple((id(p), id(g), g.data_ptr()) for _, p, g in entries)
+    def _grad_key(self, entries) -> tuple:
+        """Identity and storage of every gradient (the GradScaler checks that clipping kept them)."""
+        return (tuple(id(p) for _, p, _ in entries),
+                tuple(map(id, (g for _, _, g in entries))),
+                tuple(map(torch.Tensor.data_ptr, (g for _, _, g in entries))))
 
     def _amp_gradients(self) -> list[torch.Tensor]:
         return [g for _, _, g in self._entries()]

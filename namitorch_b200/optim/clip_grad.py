@@ -11,6 +11,7 @@ are rewritten in place, as the reference does. ``norm.item()`` or
 from __future__ import annotations
 
 import math
+import operator
 from numbers import Real
 
 import numpy as np
@@ -62,10 +63,32 @@ def _norm_type(value: object) -> float:
     return value
 
 
+_LAST_CHECKED = None   # (parameters, their gradients, the validated result) of the last call
+
+
 def _parameters_and_gradients(parameters) -> tuple[list[torch.Tensor], list[torch.Tensor]]:
-    """namitorch/optim/clip_grad.py:36-60 (gradients de-duplicated by identity)."""
+    """namitorch/optim/clip_grad.py:36-60 (gradients de-duplicated by identity). A call with the
+    same parameter objects carrying the same gradient objects as the previous call reuses its
+    validated result."""
+    global _LAST_CHECKED
     if isinstance(parameters, torch.Tensor):
         parameters = (parameters,)
+    if isinstance(parameters, (list, tuple)) or hasattr(parameters, "__next__"):
+        items = list(parameters) if not isinstance(parameters, (list, tuple)) else parameters
+        if all(type(p) is torch.nn.Parameter or type(p) is torch.Tensor for p in items):
+            grads = [p.grad for p in items]
+            last = _LAST_CHECKED
+            if (last is not None and len(last[0]) == len(items) and all(map(operator.is_, last[0], items))
+                    and all(map(operator.is_, last[1], grads))):
+                return last[2]
+            result = _validate_parameters(items)
+            _LAST_CHECKED = (list(items), grads, result)
+            return result
+        parameters = items
+    return _validate_parameters(parameters)
+
+
+def _validate_parameters(parameters) -> tuple[list[torch.Tensor], list[torch.Tensor]]:
     if isinstance(parameters, (dict, str, bytes, set, frozenset)):
         raise TypeError("parameters must be a Tensor or an ordered iterable of Tensors.")
     try:
@@ -161,8 +184,9 @@ def clip_grad_norm_(parameters, max_norm: float, norm_type: float = 2, error_if_
             if not math.isfinite(value):
                 raise RuntimeError(f"Cannot clip gradients with nonfinite total norm {value}.")
 
-    sharded = _sharded_owner(params)
-    owner = sharded if sharded is not None else (_sole_owner(params) if _LAZY else None)
+    sole = _sole_owner(params)
+    sharded = sole if sole is not None and getattr(sole, "_sharded", False) else None
+    owner = sharded if sharded is not None else (sole if _LAZY else None)
     stats = owner._lazy_clip(maximum, order, check) if owner is not None else None
     if stats is not None and sharded is not None and not _LAZY:
         sharded._materialize_pending()   # eager: rewrite the reduced shard now

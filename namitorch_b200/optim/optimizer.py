@@ -71,8 +71,27 @@ class Optimizer:
     def _prepare_options(self, options: dict, path: str) -> dict:
         return _copy_options(options, path)
 
+    def _group_signature(self):
+        """Identity of the group structure and of every registered parameter (cheap)."""
+        try:
+            return tuple((id(group), id(group["params"]), tuple(map(id, group["params"])))
+                         for group in self.param_groups)
+        except Exception:   # malformed groups: the full validation below reports them
+            return None
+
     def _registered_parameters(self) -> list[torch.Tensor]:
-        """namitorch/optim/optimizer.py:148-164."""
+        """namitorch/optim/optimizer.py:148-164. The validated list is kept until the groups or
+        their parameter objects change (an identity check of every entry per call)."""
+        signature = self._group_signature()
+        cached = self.__dict__.get("_registered_cache")
+        if signature is not None and cached is not None and cached[0] == signature:
+            return cached[1]
+        parameters = self._validate_registered()
+        if signature is not None:
+            self._registered_cache = (signature, parameters)
+        return parameters
+
+    def _validate_registered(self) -> list[torch.Tensor]:
         if not self.param_groups:
             raise ValueError("Optimizer must contain at least one parameter group.")
         parameters = []
@@ -113,8 +132,22 @@ class Optimizer:
 
     def _parameters_with_grad(self):
         """namitorch/optim/optimizer.py:181-195."""
-        self._registered_parameters()
-        for group in self.param_groups:
+        for _, group, parameter, gradient in self._grad_entries():
+            yield group, parameter, gradient
+
+    def _grad_entries(self) -> list:
+        """[(group index, group, parameter, gradient)] of the parameters that have gradients,
+        validated as the reference does. The list is kept while the same gradient objects sit
+        on the same parameters (checked by identity every call); a new gradient object is
+        validated again."""
+        parameters = self._registered_parameters()
+        gradients = [parameter.grad for parameter in parameters]
+        key = (id(parameters), tuple(map(id, gradients)), tuple(parameter.requires_grad for parameter in parameters))
+        cached = self.__dict__.get("_entries_cache")
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        entries = []
+        for index, group in enumerate(self.param_groups):
             for parameter in group["params"]:
                 if not parameter.requires_grad or parameter.grad is None:
                     continue
@@ -129,7 +162,10 @@ class Optimizer:
                                      f"{tuple(parameter.shape)}.")
                 if gradient.dtype is not parameter.dtype:
                     raise TypeError(f"Gradient dtype {gradient.dtype} does not match parameter dtype {parameter.dtype}.")
-                yield group, parameter, gradient
+                entries.append((index, group, parameter, gradient))
+        # The gradients list keeps the objects alive, so their ids stay unique while cached.
+        self._entries_cache = (key, entries, gradients)
+        return entries
 
     def zero_grad(self, set_to_none: bool = True) -> None:
         """namitorch/optim/optimizer.py:197-206."""

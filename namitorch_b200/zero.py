@@ -130,7 +130,7 @@ class CudaShardKernels:
         N.call("nt_zero_reduce_scatter_stats", N.C.byref(args), N.stream_handle())
 
     def update(self, *, master, exp_avg, exp_avg_sq, copy, grad_dtype, segments, num_segments, num_chunks, steps,
-               corrections, capacity, scale, stats, skip, max_norm, groups, peers=None):
+               corrections, capacity, scale, stats, skip, max_norm, groups, peers=None, schedule=None):
         group_array = (N.AdamWGroup * len(groups))(*groups)
         args = N.AdamWMtArgs(
             param=master.data_ptr(), exp_avg=exp_avg.data_ptr(), exp_avg_sq=exp_avg_sq.data_ptr(),
@@ -141,6 +141,8 @@ class CudaShardKernels:
             skip_nonfinite=int(skip), clip=int(max_norm is not None), max_norm=float(max_norm or 0.0),
             workspace=self.adamw_workspace.data_ptr(), error=self.error.data_ptr(), groups=group_array,
             num_groups=len(groups))
+        if schedule is not None:
+            args.lr_schedule, args.lr_schedule_rows, args.lr_schedule_columns, args.lr_step = schedule
         if peers:
             array = (N.C.c_void_p * len(peers))(*peers)
             N.call("nt_adamw_mt_push", N.C.byref(args), array, len(peers), N.stream_handle())
@@ -531,6 +533,8 @@ class ZeroAdamW(_FirstOrderAdam):
             raise RuntimeError(f"ZeroAdamW supports at most {N.NT_MAX_GROUPS} parameter groups.")
         local = {gi: k for k, gi in enumerate(used)}
         structs = [self._group_struct(options[gi]) for gi in used]
+        for gi, st in zip(used, structs):
+            st.schedule_column = gi
         self.corrections.ensure(self.max_step + 1)
         return structs, self._piece_tables(local)
 
@@ -538,6 +542,8 @@ class ZeroAdamW(_FirstOrderAdam):
         """The fused AdamW kernel over piece j of the shard (pushing into `peers` if given)."""
         if table is None:
             return
+        scheduler = getattr(self, "_lr_schedule", None)
+        schedule = None if scheduler is None else scheduler._schedule_args()
         segs, nseg, nchunks = table
         self._kernels.update(
             master=self.master, exp_avg=self.exp_avg, exp_avg_sq=self.exp_avg_sq, copy=self._copy_base(j),
@@ -545,7 +551,7 @@ class ZeroAdamW(_FirstOrderAdam):
             steps=self.steps, corrections=self.corrections.tensor, capacity=self.corrections.capacity,
             scale=None if amp is None else amp.scale, stats=None if amp is None else amp.stats,
             skip=bool(amp is not None and amp.skip), max_norm=None if amp is None else amp.max_norm,
-            groups=structs, peers=peers)
+            groups=structs, peers=peers, **({"schedule": schedule} if schedule is not None else {}))
 
     def benchmark_shard_update(self, iters: int) -> float:
         """Mean device time (ms) of the shard's AdamW update alone -- no reduce-scatter, no

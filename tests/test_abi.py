@@ -63,6 +63,7 @@ STRUCTS = {
     "nt_xent_info": (N.XentInfo, None),
     "nt_xent_args": (N.XentArgs, [f for f, _ in N.XentArgs._fields_]),
     "nt_zero_reduce_args": (N.ZeroReduceArgs, [f for f, _ in N.ZeroReduceArgs._fields_]),
+    "nt_lr_entry": (N.LrEntry, [f for f, _ in N.LrEntry._fields_]),
 }
 
 
