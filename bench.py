@@ -50,7 +50,8 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["1p3b", "124m", "small", "xent"], default="1p3b")
+    ap.add_argument("--workload", choices=["1p3b", "124m", "small", "xent", "softmax"], default="1p3b")
+    ap.add_argument("--softmax-dtype", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-sample", type=int, default=1 << 25, help="parameters in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -523,6 +524,86 @@ def run_xent(args):
     print(json.dumps(result), flush=True)
 
 
+def cpu_softmax_sample(rows: int, width: int, threads: int) -> dict:
+    """The oracle's causal softmax forward + backward (the reference's arithmetic) on `rows`
+    rows of [rows / width, width, width] causal scores, split over host threads (NumPy
+    releases the GIL in its ufuncs)."""
+    import concurrent.futures as cf
+    from oracle import softmax as S
+    rng = np.random.default_rng(0)
+    x = rng.normal(0, 2, (rows, width)).astype(np.float32)
+    g = rng.normal(0, 1, (rows, width)).astype(np.float32)
+    per = max(1, -(-rows // threads))
+
+    def part(k):
+        lo, hi = k * per, min(rows, (k + 1) * per)
+        if lo >= hi:
+            return
+        xs, gs = x[lo:hi].reshape(1, hi - lo, width), g[lo:hi].reshape(1, hi - lo, width)
+        y, _ = S.forward(xs, causal=True, offset=lo % width)
+        S.backward(y, gs, causal=True, offset=lo % width)
+
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(threads) as pool:
+        list(pool.map(part, range(threads)))
+    dt = time.perf_counter() - t0
+    return {"value": rows / dt, "unit": "rows/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} rows x {width} causal softmax forward + backward (oracle port of the reference's "
+                      "NumPy arithmetic), float32"}
+
+
+def run_softmax(args):
+    """Causal attention softmax forward + backward on GPT-2-small attention scores
+    (batch 8 x 12 heads x 1024 queries, 1024 keys): the row-softmax seam's hot shape."""
+    import torch
+    from namitorch_b200 import _native as N
+    from namitorch_b200.backends import get_backend
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    dtype = {"f32": torch.float32, "bf16": torch.bfloat16}[args.softmax_dtype]
+    heads, t = 8 * 12, 1024
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    x = torch.randn(heads, t, t, device=device, generator=gen).mul_(2.0).to(dtype)
+    g = torch.randn(heads, t, t, device=device, generator=gen).to(dtype)
+    k = get_backend(x).softmax
+    for _ in range(args.warmup):
+        y = k.run("causal_softmax", (x, None))
+        k.run("causal_softmax_backward", (y, g, None))
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    launches0 = N.launch_count
+    ev[0].record()
+    for _ in range(args.steps):
+        y = k.run("causal_softmax", (x, None))
+    ev[1].record()
+    for _ in range(args.steps):
+        k.run("causal_softmax_backward", (y, g, None))
+    ev[2].record()
+    torch.cuda.synchronize()
+    fwd, bwd = ev[0].elapsed_time(ev[1]) / args.steps, ev[1].elapsed_time(ev[2]) / args.steps
+    elems, es = x.numel(), x.element_size()
+    peak, kind = measured_peak()
+    rows = heads * t
+    achieved = 5 * es * elems / ((fwd + bwd) / 1e3) / 1e9
+    result = {"metric": "causal attention softmax fwd+bwd rows/s", "value": rows / ((fwd + bwd) / 1e3),
+              "unit": "rows/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": fwd + bwd,
+              "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": args.softmax_dtype,
+              "data": "synthetic",
+              "config": {"workload": f"attention scores [{heads} x {t}, {t}] N(0,2), causal (GPT-2 small, batch 8)",
+                         "l2": f"inputs larger than L2 ({elems * es / 1e6:.0f} MB per tensor)"},
+              "kernels_ms": {"forward": fwd, "backward": bwd},
+              "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                           "peak_source": kind,
+                           "algorithmic_bytes": {"forward": 2 * es * elems, "backward": 3 * es * elems},
+                           "forward_gbs": 2 * es * elems / (fwd / 1e3) / 1e9,
+                           "backward_gbs": 3 * es * elems / (bwd / 1e3) / 1e9, "traffic": None},
+              "gpu_launches": N.launch_count - launches0}
+    if not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_softmax_sample(4096, t, os.cpu_count() or 1)
+    print(json.dumps(result), flush=True)
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -538,6 +619,16 @@ def run_reference(args):
         base["value"] = value
         line = {"impl": "reference", "metric": "fused softmax-CE fwd+bwd rows/s", "value": value, "unit": "rows/s",
                 "higher_is_better": True}
+    elif args.workload == "softmax":
+        times = []
+        for i in range(args.warmup + args.steps):
+            base = cpu_softmax_sample(2048, 1024, threads)
+            if i >= args.warmup:
+                times.append(base["value"])
+        value = statistics.median(times)
+        base["value"] = value
+        line = {"impl": "reference", "metric": "causal attention softmax fwd+bwd rows/s", "value": value,
+                "unit": "rows/s", "higher_is_better": True}
     else:
         n = min(args.cpu_sample, 1 << 24)
         base = cpu_amp_sample(n, args.warmup + args.steps, threads)
@@ -558,6 +649,9 @@ def main(argv=None):
         return
     if args.workload == "xent":
         run_xent(args)
+        return
+    if args.workload == "softmax":
+        run_softmax(args)
         return
     run_ours(args)
 

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define NT_ABI_VERSION 3
+#define NT_ABI_VERSION 4
 #define NT_MAX_GROUPS 32      /* coefficient groups per nt_adamw_mt call */
 #define NT_MAX_FOUND_INF 16   /* optimizers combined by one nt_scaler_update call */
 
@@ -280,6 +280,42 @@ int nt_grad_clip_value(const nt_span* spans, int32_t num_spans, int32_t chunk_el
 int nt_scaler_update(float* scale, int32_t* growth_tracker, const double* const* found_inf,
                      int32_t count, double growth_factor, double backoff_factor,
                      int32_t growth_interval, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Row softmax family for attention scores                                               */
+/* ------------------------------------------------------------------------------------ */
+
+#define NT_SOFTMAX_MAX_WIDTH 4096
+enum {
+  NT_SOFTMAX = 0,
+  NT_MASKED_SOFTMAX = 1,
+  NT_CAUSAL_SOFTMAX = 2,
+  NT_SOFTMAX_BACKWARD = 3,
+  NT_MASKED_SOFTMAX_BACKWARD = 4,
+  NT_CAUSAL_SOFTMAX_BACKWARD = 5
+};
+
+typedef struct nt_softmax_args {
+  int32_t op;            /* NT_SOFTMAX ... NT_CAUSAL_SOFTMAX_BACKWARD */
+  int32_t dtype;         /* NT_F32 / NT_F16 / NT_BF16 of input, gradient and output */
+  const void* input;     /* [rows, width] scores (forward) or softmax output (backward), contiguous */
+  const void* gradient;  /* [rows, width] upstream gradient (backward) or NULL */
+  const uint8_t* mask;   /* bool [mask_rows or 1, width] (masked; optional for causal) or NULL */
+  void* output;          /* [rows, width] */
+  void* summary;         /* forward: NULL or device uint64[4] = {0, 0, UINT64_MAX, 0}, receiving
+                            {rows with no allowed key, rows whose max is NaN or +inf, first such row} */
+  int64_t rows;
+  int64_t width;         /* 0..NT_SOFTMAX_MAX_WIDTH */
+  int64_t mask_rows;     /* mask row of `row` is row % mask_rows; 0: one mask row for all */
+  int64_t queries;       /* size of the query dimension (causal: allowed column <= offset + row % queries) */
+  int64_t offset;        /* query position offset, clamped to width */
+} nt_softmax_args;
+
+/* The reference's SoftmaxCUDAKernels operations (namitorch/backends/cuda/softmax.py:6-178):
+   softmax over the last dimension with an optional boolean mask and a causal rule, and the
+   matching backward y * (g - sum(g * y)) restricted to the allowed entries. Float32 as in
+   the reference, plus float16 / bfloat16 rows computed in float32. */
+int nt_row_softmax(const nt_softmax_args* args, void* stream);
 
 /* ------------------------------------------------------------------------------------ */
 /* ZeRO-1 over peer memory (NVLink / NVSwitch)                                           */

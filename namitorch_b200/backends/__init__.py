@@ -46,4 +46,13 @@ def get_backend(value=None):
         return _backends[device]
 
 
-__all__ = ["enable_fused_kernels", "fused_kernels_enabled", "get_backend"]
+def try_fused_softmax(operation, *arrays, **parameters):
+    """namitorch/backends/__init__.py:63-68: the fused row softmax, or None when disabled or
+    not applicable (the caller then uses its own path)."""
+    if not fused_kernels_enabled():
+        return None
+    kernels = getattr(get_backend(arrays[0]), "softmax", None)
+    return None if kernels is None else kernels.run(operation, arrays, **parameters)
+
+
+__all__ = ["enable_fused_kernels", "fused_kernels_enabled", "get_backend", "try_fused_softmax"]

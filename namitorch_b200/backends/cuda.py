@@ -57,12 +57,15 @@ class AdamWCUDAKernel:
 
 
 class CUDABackend:
-    """One per device (namitorch/backends/cuda/__init__.py:23-45); ``adamw`` is the plugin seam."""
+    """One per device (namitorch/backends/cuda/__init__.py:23-45); ``adamw`` and ``softmax`` are the
+    plugin seams."""
 
     def __init__(self, device: torch.device):
         N.load()
         self.device = device
         self.adamw = AdamWCUDAKernel(self)
+        from .softmax import SoftmaxCUDAKernels
+        self.softmax = SoftmaxCUDAKernels(self)
 
     @staticmethod
     def supports_float16() -> bool:

@@ -1,0 +1,331 @@
+// Row softmax family for attention scores (rows of at most 4096 elements): softmax, masked
+// and causal softmax and their backward passes, the operations of the reference's
+// SoftmaxCUDAKernels (namitorch/backends/cuda/softmax.py:6-88).
+//
+// A row stays in registers: one read, max and sum reductions with warp shuffles (shared
+// memory across the warps of a row), one write: 8 bytes per element for float32 forward,
+// 12 for backward. Semantics follow the reference kernel:
+//   allowed(c) = (not causal or c <= offset + row % queries) and (no mask or mask[row % mask_rows][c])
+//   forward:  m = max over allowed values (NaN propagates); empty = m is -inf, invalid = m is
+//             NaN or +inf; y = empty ? 0 : exp(x - m) / sum (NaN everywhere when invalid),
+//             with exp on the SFU and the division as a multiply by 1/sum (each within a few
+//             float32 ulps of expf and IEEE division)
+//   backward: y' = allowed ? y * (g - sum_c g*y) : 0
+// Sum orders differ from the reference's shared-memory tree, so results agree to float32
+// rounding. Half and bfloat16 rows are computed in float32 and rounded once on store.
+#include <cmath>
+
+#include "nt_common.cuh"
+
+namespace nt {
+
+struct SoftmaxParams {
+  const void* x;
+  const void* g;
+  const uint8_t* mask;
+  void* y;
+  unsigned long long* summary;   // {empty rows, invalid rows, first bad row, unused} or NULL
+  int64_t rows;
+  int width;
+  int64_t mask_rows;             // 0: one mask row for every row
+  int64_t queries;
+  int64_t offset;
+  int causal;
+  int vec;                       // rows start on 16-byte boundaries and width fills whole vectors
+};
+
+constexpr int kSoftmaxThreads = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// 2^x on the SFU; results below 2^-126 flush to zero (an entry that far below the row max
+// contributes nothing to the sum, and its probability is below 2^-126 of the largest).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int WARPS>
+__device__ __forceinline__ float row_max(float v, float* smem) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if constexpr (WARPS > 1) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, first = warp - warp % WARPS;
+    __syncwarp();
+    if (lane == 0) smem[warp] = v;
+    __syncthreads();
+    v = smem[first];
+#pragma unroll
+    for (int w = 1; w < WARPS; ++w) v = max_nan(v, smem[first + w]);
+    __syncthreads();
+  }
+  return v;
+}
+
+template <int WARPS>
+__device__ __forceinline__ float row_sum(float v, float* smem) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if constexpr (WARPS > 1) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, first = warp - warp % WARPS;
+    __syncwarp();
+    if (lane == 0) smem[warp] = v;
+    __syncthreads();
+    v = smem[first];
+#pragma unroll
+    for (int w = 1; w < WARPS; ++w) v += smem[first + w];
+    __syncthreads();
+  }
+  return v;
+}
+
+// Column of slot q of thread t (T threads per row): 16-byte vectors of EPV elements dealt
+// round-robin on the vector path, single elements round-robin otherwise.
+template <int EPV>
+__device__ __forceinline__ int slot_column(int q, int t, int T, bool vec) {
+  return vec ? ((q / EPV) * T + t) * EPV + q % EPV : q * T + t;
+}
+
+template <int DT, int NPL, int WARPS>
+__device__ __forceinline__ void load_row(const void* base, int width, int t, bool vec, float (&v)[NPL]) {
+  constexpr int ES = DT == NT_F32 ? 4 : 2;
+  constexpr int EPV = 16 / ES;
+  constexpr int T = 32 * WARPS;
+  if (vec) {
+#pragma unroll
+    for (int c = 0; c < NPL / EPV; ++c) {
+      const int k = c * T + t;
+      if (k * EPV < width) {
+        const uint4 raw = __ldcs(static_cast<const uint4*>(base) + k);
+        unpack16<DT>(raw, v + c * EPV);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) v[c * EPV + e] = 0.0f;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < NPL; ++q) {
+      const int j = q * T + t;
+      v[q] = j < width ? load1<DT>(base, j) : 0.0f;
+    }
+  }
+}
+
+// One 16-byte vector: EPV values rounded to the storage type (round to nearest even; the
+// 16-bit types convert two values per instruction).
+template <int DT>
+__device__ __forceinline__ void store_vec16(void* base, int k, const float* v) {
+  uint4 raw;
+  if constexpr (DT == NT_F32) {
+    raw = make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+  } else if constexpr (DT == NT_BF16) {
+    __nv_bfloat162 h[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+    raw = *reinterpret_cast<const uint4*>(h);
+  } else {
+    __half2 h[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+    raw = *reinterpret_cast<const uint4*>(h);
+  }
+  __stcs(static_cast<uint4*>(base) + k, raw);
+}
+
+template <int DT, int NPL, int WARPS>
+__device__ __forceinline__ void store_row(void* base, int width, int t, bool vec, const float (&v)[NPL]) {
+  constexpr int ES = DT == NT_F32 ? 4 : 2;
+  constexpr int EPV = 16 / ES;
+  constexpr int T = 32 * WARPS;
+  if (vec) {
+#pragma unroll
+    for (int c = 0; c < NPL / EPV; ++c) {
+      const int k = c * T + t;
+      if (k * EPV < width) store_vec16<DT>(base, k, v + c * EPV);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < NPL; ++q) {
+      const int j = q * T + t;
+      if (j < width) store1<DT>(base, j, v[q]);
+    }
+  }
+}
+
+template <int DT, int NPL, int WARPS, bool BACKWARD>
+__global__ void __launch_bounds__(kSoftmaxThreads) row_softmax_kernel(const __grid_constant__ SoftmaxParams P) {
+  __shared__ float smem[kSoftmaxThreads / 32];
+  constexpr int ES = DT == NT_F32 ? 4 : 2;
+  constexpr int EPV = 16 / ES;
+  constexpr int T = 32 * WARPS;
+  constexpr int GROUPS = kSoftmaxThreads / T;   // rows in flight per block
+  const int t = threadIdx.x % T;
+  const int group = threadIdx.x / T;
+  const bool vec = P.vec != 0;
+  const int width = P.width;
+  const float NEG_INF = -INFINITY;
+
+  // Rows are visited in rounds of GROUPS per block so that every warp of the block reaches
+  // the same barriers (a group past the last row computes on an empty row and stores nothing).
+  for (int64_t first = (int64_t)blockIdx.x * GROUPS; first < P.rows; first += (int64_t)gridDim.x * GROUPS) {
+    const int64_t row = first + group;
+    const bool live = row < P.rows;
+    const int64_t r = live ? row : 0;
+    const int64_t base = r * (int64_t)width;
+    // The last allowed column of the row (-1: none): the width, cut by the causal rule.
+    int last = live ? width - 1 : -1;
+    if (P.causal) {
+      const int64_t limit = P.offset + r % P.queries;
+      if (limit < last) last = (int)limit;
+    }
+    const uint8_t* mrow = P.mask == nullptr ? nullptr
+                          : P.mask + (P.mask_rows == 0 ? 0 : (r % P.mask_rows) * (int64_t)width);
+    const char* xrow = static_cast<const char*>(P.x) + base * ES;
+    char* yrow = static_cast<char*>(P.y) + base * ES;
+    float v[NPL];
+    if (live) load_row<DT, NPL, WARPS>(xrow, width, t, vec, v);
+    else {
+#pragma unroll
+      for (int q = 0; q < NPL; ++q) v[q] = 0.0f;
+    }
+    if constexpr (BACKWARD) {
+      float w[NPL];
+      const char* grow = static_cast<const char*>(P.g) + base * ES;
+      if (live) load_row<DT, NPL, WARPS>(grow, width, t, vec, w);
+      else {
+#pragma unroll
+        for (int q = 0; q < NPL; ++q) w[q] = 0.0f;
+      }
+      float dot = 0.0f;
+#pragma unroll
+      for (int q = 0; q < NPL; ++q) dot = __fadd_rn(dot, __fmul_rn(w[q], v[q]));
+      dot = row_sum<WARPS>(dot, smem);
+#pragma unroll
+      for (int q = 0; q < NPL; ++q) {
+        const int j = slot_column<EPV>(q, t, T, vec);
+        const bool ok = j <= last && (mrow == nullptr || __ldg(mrow + j) != 0);
+        v[q] = ok ? __fmul_rn(v[q], __fsub_rn(w[q], dot)) : 0.0f;
+      }
+    } else {
+      float m = NEG_INF;
+#pragma unroll
+      for (int q = 0; q < NPL; ++q) {
+        const int j = slot_column<EPV>(q, t, T, vec);
+        const bool ok = j <= last && (mrow == nullptr || __ldg(mrow + j) != 0);
+        v[q] = ok ? v[q] : NEG_INF;
+        m = max_nan(m, v[q]);
+      }
+      m = row_max<WARPS>(m, smem);
+      const bool empty = m == NEG_INF;
+      const bool invalid = isnan(m) || m == INFINITY;
+      if (live && t == 0 && P.summary != nullptr && (empty || invalid)) {
+        atomicAdd(&P.summary[empty ? 0 : 1], 1ull);
+        atomicMin(&P.summary[2], (unsigned long long)row);
+      }
+      // exp(x - m) = 2^(x log2e - m log2e): one FMA and one SFU op per entry (a disallowed
+      // entry is -inf and gives 0); one reciprocal of the row sum replaces the divisions.
+      float s = 0.0f;
+      if (!empty && !invalid) {
+        const float ml = m * kLog2e;
+#pragma unroll
+        for (int q = 0; q < NPL; ++q) {
+          v[q] = ex2(fmaf(v[q], kLog2e, -ml));
+          s += v[q];
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < NPL; ++q) v[q] = empty ? 0.0f : __int_as_float(0x7fffffff);
+        s = empty ? 0.0f : __int_as_float(0x7fffffff);
+      }
+      s = row_sum<WARPS>(s, smem);
+      const float inv = __frcp_rn(s);
+#pragma unroll
+      for (int q = 0; q < NPL; ++q) v[q] = empty ? 0.0f : v[q] * inv;
+    }
+    if (live) store_row<DT, NPL, WARPS>(yrow, width, t, vec, v);
+  }
+}
+
+template <int DT, int NPL, int WARPS, bool BACKWARD>
+static int launch_softmax(const SoftmaxParams& P, cudaStream_t s) {
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, row_softmax_kernel<DT, NPL, WARPS, BACKWARD>,
+                                                      kSoftmaxThreads, 0) != cudaSuccess || per_sm <= 0)
+      per_sm = 4;
+  }
+  constexpr int GROUPS = kSoftmaxThreads / (32 * WARPS);
+  int64_t grid = (int64_t)current_sm_count() * per_sm;
+  const int64_t need = (P.rows + GROUPS - 1) / GROUPS;
+  if (grid > need) grid = need;
+  if (grid < 1) grid = 1;
+  row_softmax_kernel<DT, NPL, WARPS, BACKWARD><<<(unsigned)grid, kSoftmaxThreads, 0, s>>>(P);
+  return launch_status("nt_row_softmax launch");
+}
+
+template <int DT, bool BACKWARD>
+static int dispatch_width(const SoftmaxParams& P, cudaStream_t s) {
+  if (P.width <= 256) return launch_softmax<DT, 8, 1, BACKWARD>(P, s);
+  if (P.width <= 512) return launch_softmax<DT, 16, 1, BACKWARD>(P, s);
+  if (P.width <= 1024) return launch_softmax<DT, 32, 1, BACKWARD>(P, s);
+  if (P.width <= 2048) return launch_softmax<DT, 32, 2, BACKWARD>(P, s);
+  return launch_softmax<DT, 32, 4, BACKWARD>(P, s);
+}
+
+template <bool BACKWARD>
+static int dispatch_dtype(const SoftmaxParams& P, int dtype, cudaStream_t s) {
+  switch (dtype) {
+    case NT_F32: return dispatch_width<NT_F32, BACKWARD>(P, s);
+    case NT_F16: return dispatch_width<NT_F16, BACKWARD>(P, s);
+    case NT_BF16: return dispatch_width<NT_BF16, BACKWARD>(P, s);
+    default:
+      set_error("nt_row_softmax: unsupported dtype %d", dtype);
+      return NT_EUNSUPPORTED;
+  }
+}
+
+}  // namespace nt
+
+using namespace nt;
+
+extern "C" {
+
+int nt_row_softmax(const nt_softmax_args* args, void* stream) {
+  if (!args) { set_error("nt_row_softmax: args is NULL"); return NT_EINVAL; }
+  const nt_softmax_args& a = *args;
+  if (a.op < NT_SOFTMAX || a.op > NT_CAUSAL_SOFTMAX_BACKWARD) {
+    set_error("nt_row_softmax: unknown operation %d", a.op);
+    return NT_EINVAL;
+  }
+  const bool backward = a.op >= NT_SOFTMAX_BACKWARD;
+  const int kind = backward ? a.op - NT_SOFTMAX_BACKWARD : a.op;   // 0 plain, 1 masked, 2 causal
+  if (a.rows < 0 || a.width < 0 || a.width > NT_SOFTMAX_MAX_WIDTH) {
+    set_error("nt_row_softmax: width must be in [0, %d] and rows nonnegative", NT_SOFTMAX_MAX_WIDTH);
+    return NT_EINVAL;
+  }
+  if (a.rows == 0 || a.width == 0) return NT_OK;
+  if (!a.input || !a.output || (backward && !a.gradient)) {
+    set_error("nt_row_softmax: NULL input/output%s", backward ? "/gradient" : "");
+    return NT_EINVAL;
+  }
+  if (kind == 1 && !a.mask) { set_error("nt_row_softmax: masked softmax needs a mask"); return NT_EINVAL; }
+  if (kind == 2 && a.queries < 1) { set_error("nt_row_softmax: causal softmax needs queries >= 1"); return NT_EINVAL; }
+  if (a.mask_rows < 0 || a.offset < 0) { set_error("nt_row_softmax: negative mask_rows / offset"); return NT_EINVAL; }
+  const int es = dtype_size(a.dtype);
+  if (es == 0) { set_error("nt_row_softmax: unsupported dtype %d", a.dtype); return NT_EUNSUPPORTED; }
+  SoftmaxParams P;
+  P.x = a.input; P.g = a.gradient; P.mask = kind == 0 ? nullptr : a.mask; P.y = a.output;
+  P.summary = backward ? nullptr : reinterpret_cast<unsigned long long*>(a.summary);
+  P.rows = a.rows; P.width = (int)a.width; P.mask_rows = a.mask_rows;
+  P.queries = a.queries < 1 ? 1 : a.queries;
+  P.offset = a.offset < a.width ? a.offset : a.width;
+  P.causal = kind == 2;
+  const int epv = 16 / es;
+  P.vec = aligned16(a.input) && aligned16(a.output) && (!backward || aligned16(a.gradient)) &&
+          (a.width % epv) == 0;
+  cudaStream_t s = as_stream(stream);
+  return backward ? dispatch_dtype<true>(P, a.dtype, s) : dispatch_dtype<false>(P, a.dtype, s);
+}
+
+}  // extern "C"

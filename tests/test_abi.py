@@ -64,6 +64,7 @@ STRUCTS = {
     "nt_xent_args": (N.XentArgs, [f for f, _ in N.XentArgs._fields_]),
     "nt_zero_reduce_args": (N.ZeroReduceArgs, [f for f, _ in N.ZeroReduceArgs._fields_]),
     "nt_lr_entry": (N.LrEntry, [f for f, _ in N.LrEntry._fields_]),
+    "nt_softmax_args": (N.SoftmaxArgs, [f for f, _ in N.SoftmaxArgs._fields_]),
 }
 
 
