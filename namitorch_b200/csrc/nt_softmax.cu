@@ -153,7 +153,105 @@ __device__ __forceinline__ void store_row(void* base, int width, int t, bool vec
   }
 }
 
+// 16-bit rows of the backward pass on the vector path stay packed in registers (EPV values
+// per 16-byte vector) and are unpacked in each of the two passes. That keeps the register
+// count low enough for the warps that hide memory latency when a row is only 2 bytes per
+// element. (The forward keeps its row in float32 and spreads it over more warps instead:
+// repacking it would mean evaluating exp twice.)
 template <int DT, int NPL, int WARPS, bool BACKWARD>
+__device__ __forceinline__ void packed_row(const SoftmaxParams& P, int64_t row, bool live, int last,
+                                           const uint8_t* mrow, int t, float* smem) {
+  constexpr int EPV = 8;
+  constexpr int NC = NPL / EPV;
+  constexpr int T = 32 * WARPS;
+  const int width = P.width;
+  const int64_t base = (live ? row : 0) * (int64_t)width;
+  const uint4* xv = reinterpret_cast<const uint4*>(static_cast<const char*>(P.x) + base * 2);
+  uint4 xr[NC], gr[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int k = c * T + t;
+    xr[c] = live && k * EPV < width ? __ldcs(xv + k) : make_uint4(0, 0, 0, 0);
+  }
+  if constexpr (BACKWARD) {
+    const uint4* gv = reinterpret_cast<const uint4*>(static_cast<const char*>(P.g) + base * 2);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int k = c * T + t;
+      gr[c] = live && k * EPV < width ? __ldcs(gv + k) : make_uint4(0, 0, 0, 0);
+    }
+  }
+  auto ok = [&](int j) { return j <= last && (mrow == nullptr || __ldg(mrow + j) != 0); };
+  uint4* yv = reinterpret_cast<uint4*>(static_cast<char*>(P.y) + base * 2);
+  if constexpr (BACKWARD) {
+    float dot = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float y[EPV], g[EPV];
+      unpack16<DT>(xr[c], y);
+      unpack16<DT>(gr[c], g);
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) dot = __fadd_rn(dot, __fmul_rn(g[e], y[e]));
+    }
+    dot = row_sum<WARPS>(dot, smem);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int k = c * T + t;
+      float y[EPV], g[EPV];
+      unpack16<DT>(xr[c], y);
+      unpack16<DT>(gr[c], g);
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) y[e] = ok(k * EPV + e) ? __fmul_rn(y[e], __fsub_rn(g[e], dot)) : 0.0f;
+      if (live && k * EPV < width) store_vec16<DT>(yv, k, y);
+    }
+    return;
+  }
+  float m = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int k = c * T + t;
+    float x[EPV];
+    unpack16<DT>(xr[c], x);
+#pragma unroll
+    for (int e = 0; e < EPV; ++e) m = max_nan(m, ok(k * EPV + e) ? x[e] : -INFINITY);
+  }
+  m = row_max<WARPS>(m, smem);
+  const bool empty = m == -INFINITY;
+  const bool invalid = isnan(m) || m == INFINITY;
+  if (live && t == 0 && P.summary != nullptr && (empty || invalid)) {
+    atomicAdd(&P.summary[empty ? 0 : 1], 1ull);
+    atomicMin(&P.summary[2], (unsigned long long)row);
+  }
+  const bool normal = !empty && !invalid;
+  const float ml = normal ? m * kLog2e : 0.0f;
+  float s = 0.0f;
+  if (normal) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int k = c * T + t;
+      float x[EPV];
+      unpack16<DT>(xr[c], x);
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) s += ok(k * EPV + e) ? ex2(fmaf(x[e], kLog2e, -ml)) : 0.0f;
+    }
+  }
+  s = row_sum<WARPS>(s, smem);
+  const float inv = __frcp_rn(s);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int k = c * T + t;
+    float x[EPV];
+    unpack16<DT>(xr[c], x);
+#pragma unroll
+    for (int e = 0; e < EPV; ++e) {
+      const float p = ok(k * EPV + e) ? ex2(fmaf(x[e], kLog2e, -ml)) * inv : 0.0f;
+      x[e] = normal ? p : (empty ? 0.0f : __int_as_float(0x7fffffff));
+    }
+    if (live && k * EPV < width) store_vec16<DT>(yv, k, x);
+  }
+}
+
+template <int DT, int NPL, int WARPS, bool BACKWARD, bool VEC>
 __global__ void __launch_bounds__(kSoftmaxThreads) row_softmax_kernel(const __grid_constant__ SoftmaxParams P) {
   __shared__ float smem[kSoftmaxThreads / 32];
   constexpr int ES = DT == NT_F32 ? 4 : 2;
@@ -162,7 +260,7 @@ __global__ void __launch_bounds__(kSoftmaxThreads) row_softmax_kernel(const __gr
   constexpr int GROUPS = kSoftmaxThreads / T;   // rows in flight per block
   const int t = threadIdx.x % T;
   const int group = threadIdx.x / T;
-  const bool vec = P.vec != 0;
+  constexpr bool vec = VEC;
   const int width = P.width;
   const float NEG_INF = -INFINITY;
 
@@ -181,6 +279,10 @@ __global__ void __launch_bounds__(kSoftmaxThreads) row_softmax_kernel(const __gr
     }
     const uint8_t* mrow = P.mask == nullptr ? nullptr
                           : P.mask + (P.mask_rows == 0 ? 0 : (r % P.mask_rows) * (int64_t)width);
+    if constexpr (ES == 2 && VEC && BACKWARD) {
+      packed_row<DT, NPL, WARPS, BACKWARD>(P, row, live, last, mrow, t, smem);
+      continue;
+    }
     const char* xrow = static_cast<const char*>(P.x) + base * ES;
     char* yrow = static_cast<char*>(P.y) + base * ES;
     float v[NPL];
@@ -247,11 +349,11 @@ __global__ void __launch_bounds__(kSoftmaxThreads) row_softmax_kernel(const __gr
   }
 }
 
-template <int DT, int NPL, int WARPS, bool BACKWARD>
-static int launch_softmax(const SoftmaxParams& P, cudaStream_t s) {
+template <int DT, int NPL, int WARPS, bool BACKWARD, bool VEC>
+static int launch_variant(const SoftmaxParams& P, cudaStream_t s) {
   static int per_sm = 0;
   if (per_sm == 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, row_softmax_kernel<DT, NPL, WARPS, BACKWARD>,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, row_softmax_kernel<DT, NPL, WARPS, BACKWARD, VEC>,
                                                       kSoftmaxThreads, 0) != cudaSuccess || per_sm <= 0)
       per_sm = 4;
   }
@@ -260,12 +362,25 @@ static int launch_softmax(const SoftmaxParams& P, cudaStream_t s) {
   const int64_t need = (P.rows + GROUPS - 1) / GROUPS;
   if (grid > need) grid = need;
   if (grid < 1) grid = 1;
-  row_softmax_kernel<DT, NPL, WARPS, BACKWARD><<<(unsigned)grid, kSoftmaxThreads, 0, s>>>(P);
+  row_softmax_kernel<DT, NPL, WARPS, BACKWARD, VEC><<<(unsigned)grid, kSoftmaxThreads, 0, s>>>(P);
   return launch_status("nt_row_softmax launch");
+}
+
+template <int DT, int NPL, int WARPS, bool BACKWARD>
+static int launch_softmax(const SoftmaxParams& P, cudaStream_t s) {
+  return P.vec ? launch_variant<DT, NPL, WARPS, BACKWARD, true>(P, s)
+               : launch_variant<DT, NPL, WARPS, BACKWARD, false>(P, s);
 }
 
 template <int DT, bool BACKWARD>
 static int dispatch_width(const SoftmaxParams& P, cudaStream_t s) {
+  if (DT != NT_F32 && !BACKWARD) {   // float32 rows of 16-bit data: 16 values per thread up to 2048
+    if (P.width <= 256) return launch_softmax<DT, 8, 1, BACKWARD>(P, s);
+    if (P.width <= 512) return launch_softmax<DT, 16, 1, BACKWARD>(P, s);
+    if (P.width <= 1024) return launch_softmax<DT, 16, 2, BACKWARD>(P, s);
+    if (P.width <= 2048) return launch_softmax<DT, 16, 4, BACKWARD>(P, s);
+    return launch_softmax<DT, 32, 4, BACKWARD>(P, s);
+  }
   if (P.width <= 256) return launch_softmax<DT, 8, 1, BACKWARD>(P, s);
   if (P.width <= 512) return launch_softmax<DT, 16, 1, BACKWARD>(P, s);
   if (P.width <= 1024) return launch_softmax<DT, 32, 1, BACKWARD>(P, s);
