@@ -50,7 +50,7 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["1p3b", "124m", "small", "xent", "softmax"], default="1p3b")
+    ap.add_argument("--workload", choices=["1p3b", "124m", "small", "xent", "softmax", "norm"], default="1p3b")
     ap.add_argument("--softmax-dtype", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-sample", type=int, default=1 << 25, help="parameters in the CPU baseline sample")
@@ -604,6 +604,56 @@ def run_softmax(args):
     print(json.dumps(result), flush=True)
 
 
+def run_norm(args):
+    """Layer norm forward + backward (input, weight and bias gradients) on the 1.3B model's
+    activations: 16 sequences x 2048 tokens x d_model 2048, float32."""
+    import torch
+    from namitorch_b200 import _native as N
+    from namitorch_b200.backends import get_backend
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    rows, width = 16 * 2048, 2048
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    x = torch.randn(rows, width, device=device, generator=gen).mul_(2.0).add_(1.0)
+    g = torch.randn(rows, width, device=device, generator=gen)
+    w = torch.randn(width, device=device, generator=gen).mul_(0.1).add_(1.0)
+    b = torch.randn(width, device=device, generator=gen).mul_(0.1)
+    k = get_backend(x).normalization
+    for _ in range(args.warmup):
+        y, st = k.run("layer_norm", (x, w, b), eps=1e-5)
+        k.run("layer_norm_backward", (x, w, g, st))
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    launches0 = N.launch_count
+    ev[0].record()
+    for _ in range(args.steps):
+        y, st = k.run("layer_norm", (x, w, b), eps=1e-5)
+    ev[1].record()
+    for _ in range(args.steps):
+        k.run("layer_norm_backward", (x, w, g, st))
+    ev[2].record()
+    torch.cuda.synchronize()
+    fwd, bwd = ev[0].elapsed_time(ev[1]) / args.steps, ev[1].elapsed_time(ev[2]) / args.steps
+    elems = x.numel()
+    peak, kind = measured_peak()
+    achieved = (8 + 20) * elems / ((fwd + bwd) / 1e3) / 1e9
+    result = {"metric": "layer norm fwd+bwd rows/s", "value": rows / ((fwd + bwd) / 1e3), "unit": "rows/s",
+              "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": fwd + bwd,
+              "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+              "data": "synthetic",
+              "config": {"workload": f"activations [{rows}, {width}] (1.3B model, 16 x 2048 tokens), weight and bias",
+                         "l2": f"inputs larger than L2 ({elems * 4 / 1e6:.0f} MB per tensor)"},
+              "kernels_ms": {"forward": fwd, "backward": bwd},
+              "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                           "peak_source": kind,
+                           "algorithmic_bytes": {"forward": 8 * elems, "backward (input + affine passes)": 20 * elems},
+                           "forward_gbs": 8 * elems / (fwd / 1e3) / 1e9, "backward_gbs": 20 * elems / (bwd / 1e3) / 1e9,
+                           "traffic": None},
+              "gpu_launches": N.launch_count - launches0}
+    print(json.dumps(result), flush=True)
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -652,6 +702,9 @@ def main(argv=None):
         return
     if args.workload == "softmax":
         run_softmax(args)
+        return
+    if args.workload == "norm":
+        run_norm(args)
         return
     run_ours(args)
 

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define NT_ABI_VERSION 4
+#define NT_ABI_VERSION 5
 #define NT_MAX_GROUPS 32      /* coefficient groups per nt_adamw_mt call */
 #define NT_MAX_FOUND_INF 16   /* optimizers combined by one nt_scaler_update call */
 
@@ -316,6 +316,45 @@ typedef struct nt_softmax_args {
    matching backward y * (g - sum(g * y)) restricted to the allowed entries. Float32 as in
    the reference, plus float16 / bfloat16 rows computed in float32. */
 int nt_row_softmax(const nt_softmax_args* args, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* RMS / layer normalization                                                             */
+/* ------------------------------------------------------------------------------------ */
+
+#define NT_NORM_MAX_WIDTH 8192
+enum { NT_RMS_NORM = 0, NT_LAYER_NORM = 1 };
+
+typedef struct nt_norm_args {
+  int32_t op;              /* NT_RMS_NORM / NT_LAYER_NORM */
+  int32_t dtype;           /* NT_F32 / NT_F16 / NT_BF16 of input, weight, bias, output, gradient, grad_input */
+  const void* input;       /* [rows, width] contiguous */
+  const void* weight;      /* [width] or NULL */
+  const void* bias;        /* [width] or NULL (layer norm only) */
+  void* output;            /* forward: [rows, width] */
+  float* statistics;       /* [rows, 2] float32 (shifted mean, 1/sqrt(var + eps)): written by the
+                              forward (NULL: not saved), read by the backward */
+  const void* gradient;    /* backward: [rows, width] upstream gradient */
+  void* grad_input;        /* backward: [rows, width] or NULL */
+  float* grad_weight;      /* backward: float32 [width] or NULL */
+  float* grad_bias;        /* backward: float32 [width] or NULL */
+  void* workspace;         /* backward with grad_weight / grad_bias: nt_norm_workspace_size bytes */
+  size_t workspace_bytes;
+  int64_t rows;
+  int64_t width;           /* 1..NT_NORM_MAX_WIDTH */
+  float eps;               /* forward: positive, finite */
+} nt_norm_args;
+
+/* Bytes of the per-tile partial sums the weight / bias gradients of [rows, width] need. */
+size_t nt_norm_workspace_size(int64_t rows, int64_t width);
+
+/* Forward of the reference's NormalizationCUDAKernels (namitorch/backends/cuda/normalization.py:
+   58-84, 160-202): y = normalized * weight + bias with the statistics above; layer norm
+   centres on the row's first element before the mean, as the reference does. */
+int nt_norm_forward(const nt_norm_args* args, void* stream);
+
+/* Backward (normalization.py:86-157, 204-235): grad_input from the saved statistics, and the
+   weight / bias gradients as per-tile partial sums reduced per column in a fixed order. */
+int nt_norm_backward(const nt_norm_args* args, void* stream);
 
 /* ------------------------------------------------------------------------------------ */
 /* ZeRO-1 over peer memory (NVLink / NVSwitch)                                           */

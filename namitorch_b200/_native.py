@@ -22,7 +22,7 @@ NT_DECAY_NONE, NT_DECAY_DECOUPLED, NT_DECAY_COUPLED = 0, 1, 2
 NT_MAX_GROUPS = 32
 NT_MAX_FOUND_INF = 16
 NT_MAX_RANKS = 8
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 
 class Segment(C.Structure):
@@ -103,6 +103,18 @@ class SoftmaxArgs(C.Structure):
                 ("width", C.c_int64), ("mask_rows", C.c_int64), ("queries", C.c_int64), ("offset", C.c_int64)]
 
 
+NT_NORM_MAX_WIDTH = 8192
+NORM_OPS = {"rms_norm": 0, "layer_norm": 1}
+
+
+class NormArgs(C.Structure):
+    _fields_ = [("op", C.c_int32), ("dtype", C.c_int32), ("input", C.c_void_p), ("weight", C.c_void_p),
+                ("bias", C.c_void_p), ("output", C.c_void_p), ("statistics", C.c_void_p), ("gradient", C.c_void_p),
+                ("grad_input", C.c_void_p), ("grad_weight", C.c_void_p), ("grad_bias", C.c_void_p),
+                ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t), ("rows", C.c_int64),
+                ("width", C.c_int64), ("eps", C.c_float)]
+
+
 class ZeroReduceArgs(C.Structure):
     _fields_ = [("sources", C.c_void_p * NT_MAX_RANKS), ("num_ranks", C.c_int32), ("dtype", C.c_int32),
                 ("count", C.c_int64), ("average", C.c_int32), ("dest", C.c_void_p), ("scale", C.c_void_p),
@@ -147,6 +159,9 @@ SIGNATURES: dict[str, tuple] = {
     "nt_zero_reduce_scatter_stats": (C.c_int, [C.POINTER(ZeroReduceArgs), C.c_void_p]),
     "nt_adamw_mt_push": (C.c_int, [C.POINTER(AdamWMtArgs), C.POINTER(C.c_void_p), C.c_int32, C.c_void_p]),
     "nt_row_softmax": (C.c_int, [C.POINTER(SoftmaxArgs), C.c_void_p]),
+    "nt_norm_workspace_size": (C.c_size_t, [C.c_int64, C.c_int64]),
+    "nt_norm_forward": (C.c_int, [C.POINTER(NormArgs), C.c_void_p]),
+    "nt_norm_backward": (C.c_int, [C.POINTER(NormArgs), C.c_void_p]),
     "nt_xent_workspace_size": (C.c_size_t, []),
     "nt_softmax_xent": (C.c_int, [C.POINTER(XentArgs), C.c_void_p]),
     "nt_xent_backward_scale": (C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_int64, C.c_void_p, C.c_int32,
@@ -203,7 +218,7 @@ def check(status: int, what: str = "") -> None:
 # Kernel launches issued per successful call of each launching entry point (for the
 # benchmark's launch count; the statistics entry point launches one kernel per call).
 LAUNCHES_PER_CALL = {"nt_adamw_f32": 1, "nt_adamw_mt": 1, "nt_adamw_mt_push": 1, "nt_zero_reduce_scatter_stats": 1,
-                     "nt_grad_stats": 1, "nt_grad_stats_finalize": 1, "nt_schedule_step": 1, "nt_row_softmax": 1,
+                     "nt_grad_stats": 1, "nt_grad_stats_finalize": 1, "nt_schedule_step": 1, "nt_row_softmax": 1, "nt_norm_forward": 1,
                      "nt_grad_stats_noalloc": 2,
                      "nt_grad_transform": 1, "nt_grad_clip_value": 1, "nt_scaler_update": 1,
                      "nt_softmax_xent": 2, "nt_xent_backward_scale": 1, "nt_cast": 1}

@@ -55,4 +55,13 @@ def try_fused_softmax(operation, *arrays, **parameters):
     return None if kernels is None else kernels.run(operation, arrays, **parameters)
 
 
-__all__ = ["enable_fused_kernels", "fused_kernels_enabled", "get_backend", "try_fused_softmax"]
+def try_fused_normalization(operation, *arrays, **parameters):
+    """namitorch/backends/__init__.py:71-76: the fused normalization, or None."""
+    if not fused_kernels_enabled():
+        return None
+    kernels = getattr(get_backend(arrays[0]), "normalization", None)
+    return None if kernels is None else kernels.run(operation, arrays, **parameters)
+
+
+__all__ = ["enable_fused_kernels", "fused_kernels_enabled", "get_backend", "try_fused_softmax",
+           "try_fused_normalization"]

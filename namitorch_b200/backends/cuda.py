@@ -57,15 +57,17 @@ class AdamWCUDAKernel:
 
 
 class CUDABackend:
-    """One per device (namitorch/backends/cuda/__init__.py:23-45); ``adamw`` and ``softmax`` are the
-    plugin seams."""
+    """One per device (namitorch/backends/cuda/__init__.py:23-45); ``adamw``, ``softmax`` and
+    ``normalization`` are the plugin seams."""
 
     def __init__(self, device: torch.device):
         N.load()
         self.device = device
         self.adamw = AdamWCUDAKernel(self)
+        from .normalization import NormalizationCUDAKernels
         from .softmax import SoftmaxCUDAKernels
         self.softmax = SoftmaxCUDAKernels(self)
+        self.normalization = NormalizationCUDAKernels(self)
 
     @staticmethod
     def supports_float16() -> bool:

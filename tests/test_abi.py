@@ -65,6 +65,7 @@ STRUCTS = {
     "nt_zero_reduce_args": (N.ZeroReduceArgs, [f for f, _ in N.ZeroReduceArgs._fields_]),
     "nt_lr_entry": (N.LrEntry, [f for f, _ in N.LrEntry._fields_]),
     "nt_softmax_args": (N.SoftmaxArgs, [f for f, _ in N.SoftmaxArgs._fields_]),
+    "nt_norm_args": (N.NormArgs, [f for f, _ in N.NormArgs._fields_]),
 }
 
 
