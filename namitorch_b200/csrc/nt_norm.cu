@@ -8,13 +8,18 @@
 // eps)); RMS norm saves (0, 1/sqrt(mean(x^2) + eps)). y = normalized * weight + bias.
 // Input gradient: dx = inverse * (g*w - mean(g*w) - normalized * mean(g*w * normalized)),
 // without the mean(g*w) term for RMS norm, from the saved statistics.
-// Affine gradient: dweight = sum over rows of g * normalized, dbias = sum of g. Each block
-// owns a tile of rows and a tile of columns (a thread per column, coalesced across the
-// warp), writes per-tile partial sums to the workspace, and a second kernel sums the tiles
-// per column in a fixed order, so the result does not depend on scheduling.
+// Affine gradient: dweight = sum over rows of g * normalized, dbias = sum of g, computed in
+// the same pass as the input gradient. A thread keeps the same columns of every row it
+// visits, so it sums them in registers; the row groups of a block are combined in shared
+// memory and the block writes one partial row per column to the workspace; a second kernel
+// sums the blocks' partial rows per column in a fixed order. The grid and the row order are
+// fixed for a given shape and device, so the result does not depend on scheduling. (The
+// reference splits the rows into tiles for the same reason and re-reads x and g; here x
+// and g are read once for both gradients.)
 // Half and bfloat16 tensors are computed in float32 (statistics and weight/bias gradients
 // are float32).
 #include <cmath>
+#include <type_traits>
 
 #include "nt_rows.cuh"
 
@@ -33,22 +38,15 @@ struct NormParams {
   int64_t rows;
   int width;
   float eps;
-  int64_t tile_rows;
-  int64_t row_tiles;
 };
 
 template <int WARPS> struct NormShape {
   static constexpr int kThreads = WARPS * 32 > 128 ? WARPS * 32 : 128;
 };
 
-// Tiles of rows of the affine-gradient stage: enough tiles for every SM, at most 1024.
-static int64_t norm_row_tiles(int64_t rows, int64_t width) {
-  const int64_t col_tiles = (width + 255) / 256;
-  int64_t tiles = (4 * 148 + col_tiles - 1) / col_tiles;
-  if (tiles > rows) tiles = rows;
-  if (tiles > 1024) tiles = 1024;
-  return tiles < 1 ? 1 : tiles;
-}
+// Most blocks of the backward pass when the weight or bias gradient is requested: one
+// partial row per block in the workspace.
+constexpr int64_t kNormMaxSlots = 1024;
 
 template <int DT, int NPL, int WARPS, bool LAYER, bool VEC>
 __global__ void __launch_bounds__(NormShape<WARPS>::kThreads) norm_forward_kernel(const __grid_constant__ NormParams P) {
@@ -102,8 +100,8 @@ __global__ void __launch_bounds__(NormShape<WARPS>::kThreads) norm_forward_kerne
       P.stats[2 * row + 1] = inv;
     }
     float wv[NPL], bv[NPL];
-    if (P.w != nullptr) load_row<DT, NPL, WARPS>(P.w, width, t, VEC, wv);
-    if (P.b != nullptr) load_row<DT, NPL, WARPS>(P.b, width, t, VEC, bv);
+    if (P.w != nullptr) load_row<DT, NPL, WARPS, false>(P.w, width, t, VEC, wv);
+    if (P.b != nullptr) load_row<DT, NPL, WARPS, false>(P.b, width, t, VEC, bv);
 #pragma unroll
     for (int q = 0; q < NPL; ++q) {
       float y = __fmul_rn(LAYER ? __fsub_rn(v[q], mean) : v[q], inv);
@@ -115,172 +113,204 @@ __global__ void __launch_bounds__(NormShape<WARPS>::kThreads) norm_forward_kerne
   }
 }
 
-template <int DT, int NPL, int WARPS, bool LAYER, bool VEC>
-__global__ void __launch_bounds__(NormShape<WARPS>::kThreads) norm_input_grad_kernel(const __grid_constant__ NormParams P) {
+// Backward over rows: the input gradient (when P.dx is set) and, with AFFINE, the block's
+// partial sums of g * normalized and g per column (when P.part_w / P.part_b are set).
+template <int DT, int NPL, int WARPS, bool LAYER, bool VEC, bool AFFINE>
+__global__ void __launch_bounds__(NormShape<WARPS>::kThreads) norm_backward_kernel(const __grid_constant__ NormParams P) {
   constexpr int THREADS = NormShape<WARPS>::kThreads;
-  __shared__ float smem[THREADS / 32];
   constexpr int ES = DT == NT_F32 ? 4 : 2;
   constexpr int EPV = 16 / ES;
   constexpr int T = 32 * WARPS;
   constexpr int GROUPS = THREADS / T;
+  constexpr int ACC = AFFINE ? NPL : 1;
+  __shared__ float smem[THREADS / 32];
+  __shared__ float combine[AFFINE && GROUPS > 1 ? 2 * (GROUPS - 1) * T * NPL : 1];
   const int t = threadIdx.x % T;
   const int group = threadIdx.x / T;
   const int width = P.width;
   const float fw = (float)width;
+  const bool want_dx = P.dx != nullptr;
+  float aw[ACC], ab[ACC];
+#pragma unroll
+  for (int q = 0; q < ACC; ++q) aw[q] = ab[q] = 0.0f;
   for (int64_t first = (int64_t)blockIdx.x * GROUPS; first < P.rows; first += (int64_t)gridDim.x * GROUPS) {
     const int64_t row = first + group;
     const bool live = row < P.rows;
     const int64_t r = live ? row : 0;
     const int64_t base = r * (int64_t)width;
     const char* xrow = static_cast<const char*>(P.x) + base * ES;
-    float n[NPL], wg[NPL];
+    float n[NPL], g[NPL];
     if (live) {
       load_row<DT, NPL, WARPS>(xrow, width, t, VEC, n);
-      load_row<DT, NPL, WARPS>(static_cast<const char*>(P.g) + base * ES, width, t, VEC, wg);
+      load_row<DT, NPL, WARPS>(static_cast<const char*>(P.g) + base * ES, width, t, VEC, g);
     } else {
 #pragma unroll
-      for (int q = 0; q < NPL; ++q) n[q] = wg[q] = 0.0f;
+      for (int q = 0; q < NPL; ++q) n[q] = g[q] = 0.0f;
     }
     const float mean = P.stats[2 * r], inv = P.stats[2 * r + 1];
     const float anchor = LAYER && live ? load1<DT>(xrow, 0) : 0.0f;
-    if (P.w != nullptr) {
-      float wv[NPL];
-      load_row<DT, NPL, WARPS>(P.w, width, t, VEC, wv);
-#pragma unroll
-      for (int q = 0; q < NPL; ++q) wg[q] = __fmul_rn(wg[q], wv[q]);
-    }
-    float sg = 0.0f, sp = 0.0f;
 #pragma unroll
     for (int q = 0; q < NPL; ++q) {
-      const bool in = slot_column<EPV>(q, t, T, VEC) < width;
+      const bool in = live && slot_column<EPV>(q, t, T, VEC) < width;
       n[q] = in ? __fmul_rn(LAYER ? __fsub_rn(__fsub_rn(n[q], anchor), mean) : n[q], inv) : 0.0f;
-      sg = __fadd_rn(sg, wg[q]);
-      sp = __fadd_rn(sp, __fmul_rn(wg[q], n[q]));
     }
-    const float mg = LAYER ? __fdiv_rn(row_sum<WARPS>(sg, smem), fw) : 0.0f;
-    const float mp = __fdiv_rn(row_sum<WARPS>(sp, smem), fw);
+    if constexpr (AFFINE) {
 #pragma unroll
-    for (int q = 0; q < NPL; ++q) n[q] = __fmul_rn(inv, __fsub_rn(__fsub_rn(wg[q], mg), __fmul_rn(n[q], mp)));
-    if (live) store_row<DT, NPL, WARPS>(static_cast<char*>(P.dx) + base * ES, width, t, VEC, n);
+      for (int q = 0; q < NPL; ++q) {
+        aw[q] = __fadd_rn(aw[q], __fmul_rn(g[q], n[q]));
+        ab[q] = __fadd_rn(ab[q], g[q]);
+      }
+    }
+    if (want_dx) {
+      if (P.w != nullptr) {
+        float wv[NPL];
+        load_row<DT, NPL, WARPS, false>(P.w, width, t, VEC, wv);
+#pragma unroll
+        for (int q = 0; q < NPL; ++q) g[q] = __fmul_rn(g[q], wv[q]);
+      }
+      float sg = 0.0f, sp = 0.0f;
+#pragma unroll
+      for (int q = 0; q < NPL; ++q) {
+        sg = __fadd_rn(sg, g[q]);
+        sp = __fadd_rn(sp, __fmul_rn(g[q], n[q]));
+      }
+      const float mg = LAYER ? __fdiv_rn(row_sum<WARPS>(sg, smem), fw) : 0.0f;
+      const float mp = __fdiv_rn(row_sum<WARPS>(sp, smem), fw);
+#pragma unroll
+      for (int q = 0; q < NPL; ++q) n[q] = __fmul_rn(inv, __fsub_rn(__fsub_rn(g[q], mg), __fmul_rn(n[q], mp)));
+      if (live) store_row<DT, NPL, WARPS>(static_cast<char*>(P.dx) + base * ES, width, t, VEC, n);
+    }
+  }
+  if constexpr (AFFINE) {
+    if constexpr (GROUPS > 1) {
+      // Row groups 1.. hand their sums to group 0, which adds them in group order.
+      if (group > 0) {
+        float* slot = combine + (size_t)(group - 1) * 2 * T * NPL;
+#pragma unroll
+        for (int q = 0; q < NPL; ++q) {
+          slot[q * T + t] = aw[q];
+          slot[(NPL + q) * T + t] = ab[q];
+        }
+      }
+      __syncthreads();
+      if (group > 0) return;
+#pragma unroll 1
+      for (int k = 0; k < GROUPS - 1; ++k) {
+        const float* slot = combine + (size_t)k * 2 * T * NPL;
+#pragma unroll
+        for (int q = 0; q < NPL; ++q) {
+          aw[q] = __fadd_rn(aw[q], slot[q * T + t]);
+          ab[q] = __fadd_rn(ab[q], slot[(NPL + q) * T + t]);
+        }
+      }
+    }
+    const int64_t row_out = (int64_t)blockIdx.x * width;
+#pragma unroll
+    for (int q = 0; q < NPL; ++q) {
+      const int c = slot_column<EPV>(q, t, T, VEC);
+      if (c < width) {
+        if (P.part_w != nullptr) P.part_w[row_out + c] = aw[q];
+        if (P.part_b != nullptr) P.part_b[row_out + c] = ab[q];
+      }
+    }
   }
 }
 
-constexpr int kAffineThreads = 256;
+constexpr int kReduceColumns = 32;
+constexpr int kReduceLanes = 8;
 
-// Block (row tile, column tile): a thread per column sums g * normalized and g over the
-// tile's rows (4 rows in flight) and writes the tile's partial sums.
-template <int DT, bool LAYER>
-__global__ void __launch_bounds__(kAffineThreads) norm_affine_partial_kernel(const __grid_constant__ NormParams P) {
-  const int col_tiles = (P.width + kAffineThreads - 1) / kAffineThreads;
-  const int64_t tiles = P.row_tiles * col_tiles;
-  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-    const int64_t rt = tile / col_tiles;
-    const int c = (int)(tile % col_tiles) * kAffineThreads + threadIdx.x;
-    if (c >= P.width) continue;
-    const int64_t r0 = rt * P.tile_rows;
-    const int64_t r1 = r0 + P.tile_rows < P.rows ? r0 + P.tile_rows : P.rows;
-    float sw = 0.0f, sb = 0.0f;
-    int64_t r = r0;
-    for (; r + 4 <= r1; r += 4) {
-      float xg[4], gg[4], an[4];
+// Column sums of the blocks' partial rows (blockIdx.y: 0 weight, 1 bias). Lane j of a
+// column sums partial rows j, j + 8, ... in order; the 8 lane sums are then added in lane
+// order.
+__global__ void __launch_bounds__(kReduceColumns * kReduceLanes)
+norm_affine_reduce_kernel(const float* part_w, const float* part_b, int64_t slots, int width, float* out_w, float* out_b) {
+  __shared__ float lanes[kReduceLanes][kReduceColumns];
+  const float* part = blockIdx.y == 0 ? part_w : part_b;
+  float* out = blockIdx.y == 0 ? out_w : out_b;
+  if (part == nullptr) return;
+  const int col = threadIdx.x % kReduceColumns;
+  const int lane = threadIdx.x / kReduceColumns;
+  const int c = blockIdx.x * kReduceColumns + col;
+  float s = 0.0f;
+  if (c < width)
+    for (int64_t k = lane; k < slots; k += kReduceLanes) s = __fadd_rn(s, part[k * width + c]);
+  lanes[lane][col] = s;
+  __syncthreads();
+  if (lane == 0 && c < width) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t base = (r + u) * (int64_t)P.width;
-        xg[u] = load1<DT>(P.x, base + c);
-        gg[u] = load1<DT>(P.g, base + c);
-        an[u] = LAYER ? load1<DT>(P.x, base) : 0.0f;
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float mean = P.stats[2 * (r + u)], inv = P.stats[2 * (r + u) + 1];
-        const float nrm = __fmul_rn(LAYER ? __fsub_rn(__fsub_rn(xg[u], an[u]), mean) : xg[u], inv);
-        sw = __fadd_rn(sw, __fmul_rn(gg[u], nrm));
-        sb = __fadd_rn(sb, gg[u]);
-      }
-    }
-    for (; r < r1; ++r) {
-      const int64_t base = r * (int64_t)P.width;
-      const float mean = P.stats[2 * r], inv = P.stats[2 * r + 1];
-      const float gv = load1<DT>(P.g, base + c);
-      const float xv = load1<DT>(P.x, base + c);
-      const float nrm = __fmul_rn(LAYER ? __fsub_rn(__fsub_rn(xv, load1<DT>(P.x, base)), mean) : xv, inv);
-      sw = __fadd_rn(sw, __fmul_rn(gv, nrm));
-      sb = __fadd_rn(sb, gv);
-    }
-    if (P.part_w != nullptr) P.part_w[rt * P.width + c] = sw;
-    if (P.part_b != nullptr) P.part_b[rt * P.width + c] = sb;
-  }
-}
-
-// Column sums of the partial tiles, in tile order.
-__global__ void norm_affine_reduce_kernel(const float* part, int64_t tiles, int width, float* out) {
-  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < width; c += gridDim.x * blockDim.x) {
-    float s = 0.0f;
-    for (int64_t k = 0; k < tiles; ++k) s = __fadd_rn(s, part[k * width + c]);
+    for (int j = 1; j < kReduceLanes; ++j) s = __fadd_rn(s, lanes[j][col]);
     out[c] = s;
   }
 }
 
+// Grid of a row kernel: every resident block, no more blocks than row groups, and at most
+// `cap` blocks. Returns the grid size it launched (0 on error).
 template <typename K>
-static int launch_rows(K kernel, const NormParams& P, int threads, int groups, cudaStream_t s) {
+static int64_t launch_rows(K kernel, const NormParams& P, int threads, int groups, int64_t cap, cudaStream_t s) {
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess || per_sm <= 0)
     per_sm = 2;
   int64_t grid = (int64_t)current_sm_count() * per_sm;
   const int64_t need = (P.rows + groups - 1) / groups;
   if (grid > need) grid = need;
+  if (grid > cap) grid = cap;
   if (grid < 1) grid = 1;
   kernel<<<(unsigned)grid, threads, 0, s>>>(P);
-  return launch_status("nt_norm launch");
+  return launch_status("nt_norm launch") == NT_OK ? grid : 0;
 }
 
-template <int DT, int NPL, int WARPS, bool LAYER, bool BACKWARD>
-static int launch_norm(const NormParams& P, bool vec, cudaStream_t s) {
+// Forward: returns the grid launched (0 on error).
+template <int DT, int NPL, int WARPS, bool LAYER>
+static int64_t launch_forward(const NormParams& P, bool vec, cudaStream_t s) {
   constexpr int THREADS = NormShape<WARPS>::kThreads;
   constexpr int GROUPS = THREADS / (32 * WARPS);
-  if constexpr (BACKWARD) {
-    return vec ? launch_rows(norm_input_grad_kernel<DT, NPL, WARPS, LAYER, true>, P, THREADS, GROUPS, s)
-               : launch_rows(norm_input_grad_kernel<DT, NPL, WARPS, LAYER, false>, P, THREADS, GROUPS, s);
-  } else {
-    return vec ? launch_rows(norm_forward_kernel<DT, NPL, WARPS, LAYER, true>, P, THREADS, GROUPS, s)
-               : launch_rows(norm_forward_kernel<DT, NPL, WARPS, LAYER, false>, P, THREADS, GROUPS, s);
-  }
+  const int64_t cap = INT32_MAX;
+  return vec ? launch_rows(norm_forward_kernel<DT, NPL, WARPS, LAYER, true>, P, THREADS, GROUPS, cap, s)
+             : launch_rows(norm_forward_kernel<DT, NPL, WARPS, LAYER, false>, P, THREADS, GROUPS, cap, s);
 }
 
+// Backward: returns the grid launched, which is the number of partial rows written when
+// the affine sums are requested (0 on error).
+template <int DT, int NPL, int WARPS, bool LAYER>
+static int64_t launch_backward(const NormParams& P, bool vec, cudaStream_t s) {
+  constexpr int THREADS = NormShape<WARPS>::kThreads;
+  constexpr int GROUPS = THREADS / (32 * WARPS);
+  if (P.part_w != nullptr || P.part_b != nullptr)
+    return vec ? launch_rows(norm_backward_kernel<DT, NPL, WARPS, LAYER, true, true>, P, THREADS, GROUPS, kNormMaxSlots, s)
+               : launch_rows(norm_backward_kernel<DT, NPL, WARPS, LAYER, false, true>, P, THREADS, GROUPS, kNormMaxSlots, s);
+  return vec ? launch_rows(norm_backward_kernel<DT, NPL, WARPS, LAYER, true, false>, P, THREADS, GROUPS, INT32_MAX, s)
+             : launch_rows(norm_backward_kernel<DT, NPL, WARPS, LAYER, false, false>, P, THREADS, GROUPS, INT32_MAX, s);
+}
+
+// Row shapes (values per thread, warps per row) by width: at most 16 values per thread, so
+// that the registers leave room for the warps that hide memory latency (at width 2048, 16
+// values over 4 warps beat 32 over 2 warps and 8 over 8 warps in both passes, f32 and bf16).
 template <int DT, bool LAYER, bool BACKWARD>
-static int dispatch_norm_width(const NormParams& P, bool vec, cudaStream_t s) {
-  if (P.width <= 256) return launch_norm<DT, 8, 1, LAYER, BACKWARD>(P, vec, s);
-  if (P.width <= 512) return launch_norm<DT, 16, 1, LAYER, BACKWARD>(P, vec, s);
-  if (P.width <= 1024) return launch_norm<DT, 32, 1, LAYER, BACKWARD>(P, vec, s);
-  if (P.width <= 2048) return launch_norm<DT, 32, 2, LAYER, BACKWARD>(P, vec, s);
-  if (P.width <= 4096) return launch_norm<DT, 32, 4, LAYER, BACKWARD>(P, vec, s);
-  return launch_norm<DT, 32, 8, LAYER, BACKWARD>(P, vec, s);
+static int64_t dispatch_norm_width(const NormParams& P, bool vec, cudaStream_t s) {
+  constexpr auto launch = [](const NormParams& p, bool v, cudaStream_t st, auto npl, auto warps) {
+    if constexpr (BACKWARD) return launch_backward<DT, decltype(npl)::value, decltype(warps)::value, LAYER>(p, v, st);
+    else return launch_forward<DT, decltype(npl)::value, decltype(warps)::value, LAYER>(p, v, st);
+  };
+  using I8 = std::integral_constant<int, 8>;
+  using I16 = std::integral_constant<int, 16>;
+  if (P.width <= 256) return launch(P, vec, s, I8{}, std::integral_constant<int, 1>{});
+  if (P.width <= 512) return launch(P, vec, s, I16{}, std::integral_constant<int, 1>{});
+  if (P.width <= 1024) return launch(P, vec, s, I16{}, std::integral_constant<int, 2>{});
+  if (P.width <= 2048) return launch(P, vec, s, I16{}, std::integral_constant<int, 4>{});
+  if (P.width <= 4096) return launch(P, vec, s, I16{}, std::integral_constant<int, 8>{});
+  return launch(P, vec, s, I16{}, std::integral_constant<int, 16>{});
 }
 
 template <bool BACKWARD>
-static int dispatch_norm(const NormParams& P, int dtype, bool layer, bool vec, cudaStream_t s) {
+static int64_t dispatch_norm(const NormParams& P, int dtype, bool layer, bool vec, cudaStream_t s) {
   switch (dtype) {
     case NT_F32: return layer ? dispatch_norm_width<NT_F32, true, BACKWARD>(P, vec, s)
                               : dispatch_norm_width<NT_F32, false, BACKWARD>(P, vec, s);
     case NT_F16: return layer ? dispatch_norm_width<NT_F16, true, BACKWARD>(P, vec, s)
                               : dispatch_norm_width<NT_F16, false, BACKWARD>(P, vec, s);
-    case NT_BF16: return layer ? dispatch_norm_width<NT_BF16, true, BACKWARD>(P, vec, s)
-                               : dispatch_norm_width<NT_BF16, false, BACKWARD>(P, vec, s);
-    default:
-      set_error("nt_norm: unsupported dtype %d", dtype);
-      return NT_EUNSUPPORTED;
+    default: return layer ? dispatch_norm_width<NT_BF16, true, BACKWARD>(P, vec, s)
+                          : dispatch_norm_width<NT_BF16, false, BACKWARD>(P, vec, s);
   }
-}
-
-template <int DT>
-static int launch_affine(const NormParams& P, bool layer, cudaStream_t s) {
-  const int64_t col_tiles = (P.width + kAffineThreads - 1) / kAffineThreads;
-  int64_t grid = P.row_tiles * col_tiles;
-  const int64_t cap = (int64_t)current_sm_count() * 8;
-  if (grid > cap) grid = cap;
-  if (layer) norm_affine_partial_kernel<DT, true><<<(unsigned)grid, kAffineThreads, 0, s>>>(P);
-  else norm_affine_partial_kernel<DT, false><<<(unsigned)grid, kAffineThreads, 0, s>>>(P);
-  return launch_status("nt_norm_backward (affine) launch");
 }
 
 static int check_norm(const nt_norm_args& a, const char* who) {
@@ -310,7 +340,8 @@ extern "C" {
 
 size_t nt_norm_workspace_size(int64_t rows, int64_t width) {
   if (rows < 1 || width < 1) return 0;
-  return (size_t)norm_row_tiles(rows, width) * (size_t)width * 2 * sizeof(float);
+  const int64_t slots = rows < kNormMaxSlots ? rows : kNormMaxSlots;
+  return (size_t)slots * (size_t)width * 2 * sizeof(float);
 }
 
 int nt_norm_forward(const nt_norm_args* args, void* stream) {
@@ -325,7 +356,7 @@ int nt_norm_forward(const nt_norm_args* args, void* stream) {
   P.x = a.input; P.w = a.weight; P.b = a.bias; P.y = a.output; P.stats = a.statistics;
   P.rows = a.rows; P.width = (int)a.width; P.eps = a.eps;
   const bool vec = norm_vec(a, {a.input, a.output, a.weight, a.bias});
-  return dispatch_norm<false>(P, a.dtype, a.op == NT_LAYER_NORM, vec, as_stream(stream));
+  return dispatch_norm<false>(P, a.dtype, a.op == NT_LAYER_NORM, vec, as_stream(stream)) > 0 ? NT_OK : NT_ECUDA;
 }
 
 int nt_norm_backward(const nt_norm_args* args, void* stream) {
@@ -344,35 +375,29 @@ int nt_norm_backward(const nt_norm_args* args, void* stream) {
     set_error("nt_norm_backward: NULL input/gradient/statistics");
     return NT_EINVAL;
   }
+  if (affine) {
+    const size_t need = nt_norm_workspace_size(a.rows, a.width);
+    if (!a.workspace || a.workspace_bytes < need) {
+      set_error("nt_norm_backward: weight/bias gradients need a workspace of %zu bytes (got %zu)", need, a.workspace_bytes);
+      return NT_EINVAL;
+    }
+  } else if (!a.grad_input) {
+    return NT_OK;
+  }
   NormParams P{};
   P.x = a.input; P.w = a.weight; P.g = a.gradient; P.dx = a.grad_input; P.stats = a.statistics;
   P.rows = a.rows; P.width = (int)a.width;
-  if (a.grad_input) {
-    const bool vec = norm_vec(a, {a.input, a.gradient, a.grad_input, a.weight});
-    rc = dispatch_norm<true>(P, a.dtype, a.op == NT_LAYER_NORM, vec, s);
-    if (rc) return rc;
-  }
-  if (!affine) return NT_OK;
-  const size_t need = nt_norm_workspace_size(a.rows, a.width);
-  if (!a.workspace || a.workspace_bytes < need) {
-    set_error("nt_norm_backward: weight/bias gradients need a workspace of %zu bytes (got %zu)", need, a.workspace_bytes);
-    return NT_EINVAL;
-  }
-  P.row_tiles = norm_row_tiles(a.rows, a.width);
-  P.tile_rows = (a.rows + P.row_tiles - 1) / P.row_tiles;
   float* part = static_cast<float*>(a.workspace);
+  const int64_t slot_cap = a.rows < kNormMaxSlots ? a.rows : kNormMaxSlots;
   P.part_w = a.grad_weight ? part : nullptr;
-  P.part_b = a.grad_bias ? part + P.row_tiles * a.width : nullptr;
-  const bool layer = a.op == NT_LAYER_NORM;
-  switch (a.dtype) {
-    case NT_F32: rc = launch_affine<NT_F32>(P, layer, s); break;
-    case NT_F16: rc = launch_affine<NT_F16>(P, layer, s); break;
-    default: rc = launch_affine<NT_BF16>(P, layer, s); break;
-  }
-  if (rc) return rc;
-  const int blocks = (int)((a.width + 255) / 256);
-  if (a.grad_weight) norm_affine_reduce_kernel<<<blocks, 256, 0, s>>>(P.part_w, P.row_tiles, P.width, a.grad_weight);
-  if (a.grad_bias) norm_affine_reduce_kernel<<<blocks, 256, 0, s>>>(P.part_b, P.row_tiles, P.width, a.grad_bias);
+  P.part_b = a.grad_bias ? part + slot_cap * a.width : nullptr;
+  const bool vec = norm_vec(a, {a.input, a.gradient, a.grad_input, a.weight});
+  const int64_t slots = dispatch_norm<true>(P, a.dtype, a.op == NT_LAYER_NORM, vec, s);
+  if (slots <= 0) return NT_ECUDA;
+  if (!affine) return NT_OK;
+  const dim3 grid((unsigned)((a.width + kReduceColumns - 1) / kReduceColumns), 2);
+  norm_affine_reduce_kernel<<<grid, kReduceColumns * kReduceLanes, 0, s>>>(P.part_w, P.part_b, slots, P.width,
+                                                                           a.grad_weight, a.grad_bias);
   return launch_status("nt_norm_backward (reduce) launch");
 }
 

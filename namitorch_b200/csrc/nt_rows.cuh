@@ -49,7 +49,9 @@ __device__ __forceinline__ int slot_column(int q, int t, int T, bool vec) {
   return vec ? ((q / EPV) * T + t) * EPV + q % EPV : q * T + t;
 }
 
-template <int DT, int NPL, int WARPS>
+// STREAM: the row is read once (evict-first loads); otherwise it is shared by every row of
+// the tensor (a weight or a bias) and kept in the caches.
+template <int DT, int NPL, int WARPS, bool STREAM = true>
 __device__ __forceinline__ void load_row(const void* base, int width, int t, bool vec, float (&v)[NPL]) {
   constexpr int ES = DT == NT_F32 ? 4 : 2;
   constexpr int EPV = 16 / ES;
@@ -59,7 +61,8 @@ __device__ __forceinline__ void load_row(const void* base, int width, int t, boo
     for (int c = 0; c < NPL / EPV; ++c) {
       const int k = c * T + t;
       if (k * EPV < width) {
-        const uint4 raw = __ldcs(static_cast<const uint4*>(base) + k);
+        const uint4* src = static_cast<const uint4*>(base) + k;
+        const uint4 raw = STREAM ? __ldcs(src) : __ldg(src);
         unpack16<DT>(raw, v + c * EPV);
       } else {
 #pragma unroll

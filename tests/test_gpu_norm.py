@@ -107,3 +107,36 @@ def test_without_affine_zero_rows_and_declines(cuda_device):
     finally:
         enable_fused_kernels(True)
     assert try_fused_normalization("layer_norm", x, None, None, eps=1e-5) is not None
+
+
+@pytest.mark.parametrize("rows,width,dt,layer,needs", [
+    (20000, 64, "f32", True, (True, True, True)),       # four rows per block, many rows per block
+    (3001, 999, "f32", True, (False, True, True)),      # per-element path, affine sums only
+    (2500, 2048, "f16", False, (False, True, False)),   # weight gradient alone
+    (1500, 5000, "bf16", True, (True, False, True)),    # bias gradient with the input gradient
+])
+def test_many_rows_affine_sums_match_oracle_and_repeat(cuda_device, rows, width, dt, layer, needs):
+    rng = np.random.default_rng(rows + width)
+    x = _store((rng.normal(0, 1.5, (rows, width)) + 2).astype(np.float32), dt)
+    w = _store(rng.normal(1, 0.3, width).astype(np.float32), dt)
+    b = _store(rng.normal(0, 0.3, width).astype(np.float32), dt) if layer else None
+    g = _store(rng.normal(0, 1, (rows, width)).astype(np.float32), dt)
+    tx, tw, tg = (torch.from_numpy(a).cuda().to(TORCH[dt]) for a in (x, w, g))
+    tb = torch.from_numpy(b).cuda().to(TORCH[dt]) if layer else None
+    op = "layer_norm" if layer else "rms_norm"
+    _, st = _k().run(op, (tx, tw, tb), eps=1e-5)
+    _, want_st = O.forward(x, w, b, 1e-5, layer)
+    want_dx, want_dw, want_db = O.backward(x, w, g, want_st, layer)
+    first = _k().run(op + "_backward", (tx, tw, tg, st), needs=needs)
+    second = _k().run(op + "_backward", (tx, tw, tg, st), needs=needs)
+    for got, again, want, need in zip(first, second, (want_dx, want_dw, want_db), needs):
+        if not need:
+            assert got is None
+            continue
+        assert torch.equal(got, again)                   # a fixed summation order
+    if needs[0]:
+        _close(first[0], _store(want_dx, dt), dt, rel=4e-6)
+    if needs[1]:
+        _close(first[1], _store(want_dw, dt), dt, rel=4e-6, rows=rows)
+    if needs[2]:
+        _close(first[2], _store(want_db, dt), dt, rel=4e-6, rows=rows)
