@@ -10,13 +10,20 @@
 // Non-finite rows follow the reference: a NaN or +inf logit makes the whole row NaN;
 // a row of all -inf has loss +inf and zero gradient.
 //
-// Data movement: each CTA is persistent over rows. A row (V * esize bytes, not 16-byte
-// aligned in general) is fetched with one cp.async.bulk from the 16-byte boundary at or
-// below its start into shared memory, completion tracked by an mbarrier; the few bytes
-// past the last 16-byte boundary of the whole tensor are loaded with plain loads. Three
-// passes then run from shared memory (max, sum of exp, gradient), and the gradient is
-// written with 16-byte streaming stores at the same alignment offset. HBM traffic is one
-// read of the logits and one write of dlogits.
+// Data movement: each CTA is persistent over rows and stages one row at a time in shared
+// memory. A row (V * esize bytes, not 16-byte aligned in general) is fetched from the 16-byte
+// boundary at or below its start by cp.async.bulk (kXentChunks copies, each completing on its
+// own mbarrier); the few bytes past the last 16-byte boundary of the whole tensor are loaded
+// with plain loads. Three passes run from shared memory: the row max (packed two-lane
+// max.NaN for 16-bit types), the sum of exp(x - max), and the gradient. The last warp to
+// finish a chunk in the gradient pass refills it with the CTA's next row (a shared-memory
+// count per chunk; no warp waits for another). At [8192, 50257] bf16 two CTAs share an SM,
+// so one CTA's copy overlaps the other's passes; one chunk per row measured fastest (more
+// chunks let a row's copy start earlier but add per-chunk work to every pass, and the
+// passes, not the copies, bound the kernel: about 17 instructions per logit). The gradient
+// is written with 16-byte streaming stores at the same alignment offset. HBM traffic is one
+// read of the logits and one write of dlogits. Tensors that do not start on a 16-byte
+// boundary take the same three passes over global memory instead.
 #include <cmath>
 
 #include "nt_bulk.cuh"
@@ -46,8 +53,11 @@ struct XentParams {
   XentWorkspace* ws;
   uintptr_t tensor_end;   // one past the last byte of the logits
   int staged;
-  int64_t stage_stride;   // bytes per staged row buffer
+  int64_t chunk;          // bytes per staged chunk (a multiple of 128)
 };
+
+constexpr int kXentChunks = 1;
+constexpr int kXentThreads = 512;
 
 // 2^x on the SFU. Results below 2^-126 flush to zero: a logit that far below the row max
 // contributes nothing to the sum and its gradient is below 2^-126 times the row scale.
@@ -110,17 +120,49 @@ __global__ void __launch_bounds__(kPrepThreads) xent_prepare_kernel(const __grid
   }
 }
 
-// One 16-byte vector k of the row (EPV elements starting at element j0).
-template <int DT, int STAGES>
-__device__ __forceinline__ void row_vector(const unsigned char* stage, const void* logits, int64_t row_base,
-                                           int k, int j0, int V, float* x) {
+// Two-lane max of packed 16-bit values; NaN in either operand gives NaN.
+template <int DT>
+__device__ __forceinline__ uint32_t max_nan_x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (DT == NT_BF16) asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+template <int DT>
+__device__ __forceinline__ float max_of_pair(uint32_t r) {
+  float lo, hi;
+  if constexpr (DT == NT_BF16) {
+    lo = __uint_as_float(r << 16);
+    hi = __uint_as_float(r & 0xffff0000u);
+  } else {
+    lo = __half2float(__ushort_as_half((unsigned short)(r & 0xffffu)));
+    hi = __half2float(__ushort_as_half((unsigned short)(r >> 16)));
+  }
+  return max_nan(lo, hi);
+}
+
+// Vector k of the row: from the staged buffer, or (unstaged) element by element from global
+// memory with -inf outside the row. Staged edge vectors hold bytes of the neighbouring rows
+// (or past the tensor) in the lanes outside [0, V); callers mask them.
+// (Plain loads: the mbarrier waits that precede them clobber memory, so the compiler keeps
+// them after the wait.)
+template <int DT, bool STAGED>
+__device__ __forceinline__ uint4 row_raw(const unsigned char* stage, int k) {
+  return reinterpret_cast<const uint4*>(stage)[k];
+}
+
+template <int DT, bool STAGED>
+__device__ __forceinline__ void row_values(const unsigned char* stage, const void* logits, int64_t row_base, int k,
+                                           int j0, int V, bool edge, float* x) {
   constexpr int EPV = DT == NT_F32 ? 4 : 8;
-  if constexpr (STAGES > 0) {
-    uint4 raw;
-    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(raw.x), "=r"(raw.y), "=r"(raw.z), "=r"(raw.w)
-                 : "r"(smem_u32(stage) + (uint32_t)k * 16u));
-    unpack16<DT>(raw, x);
+  if constexpr (STAGED) {
+    unpack16<DT>(row_raw<DT, true>(stage, k), x);
+    if (edge) {
+#pragma unroll
+      for (int q = 0; q < EPV; ++q)
+        if (j0 + q < 0 || j0 + q >= V) x[q] = -INFINITY;
+    }
   } else {
 #pragma unroll
     for (int q = 0; q < EPV; ++q) {
@@ -130,34 +172,48 @@ __device__ __forceinline__ void row_vector(const unsigned char* stage, const voi
   }
 }
 
-// Issues the bulk copy of `row` into `buf` (thread 0) and loads the bytes between the last
-// 16-byte boundary of the tensor and its end with plain loads (all threads). The copy starts
-// at the 16-byte boundary at or below the row start; the kernel indexes from the offset.
+// Stages chunk c of `row` into `buf` (called by one whole warp): bytes [c * chunk,
+// (c + 1) * chunk) counted from the 16-byte boundary at or below the row start, by one bulk
+// copy issued by lane 0 and completing on `bar` (an empty chunk arrives with no bytes, so
+// every chunk's barrier completes once per row). The bytes between the last 16-byte boundary
+// of the tensor and its end (fewer than 16, at the end of the last row) are loaded with
+// plain loads by the warp before lane 0 arrives; the arrival (release) and the readers' wait
+// (acquire) make them visible.
 template <int ES>
-__device__ __forceinline__ void stage_row(const XentParams& P, int64_t row, unsigned char* buf, uint64_t* bar) {
+__device__ __forceinline__ void stage_chunk(const XentParams& P, int64_t row, unsigned char* buf, uint64_t* bar,
+                                            int c, int lane) {
   const uintptr_t start = reinterpret_cast<uintptr_t>(P.logits) + (uintptr_t)(row * P.classes * ES);
   const uintptr_t a = start & ~(uintptr_t)15;
   const int span = (int)(start - a) + (int)P.classes * ES;
-  int64_t bulk = (int64_t)((span + 15) >> 4) * 16;
+  int bulk = ((span + 15) >> 4) << 4;
   const uintptr_t limit = P.tensor_end & ~(uintptr_t)15;
-  if ((int64_t)(limit - a) < bulk) bulk = (int64_t)(limit - a);
-  if (threadIdx.x == 0) {
+  if ((int64_t)(limit - a) < bulk) bulk = (int)(limit - a);
+  const int lo = c * (int)P.chunk;
+  const int end = lo + (int)P.chunk;
+  const int hi = bulk < end ? bulk : end;
+  if (bulk < span && bulk >= lo && bulk < end)
+    for (int k = bulk + lane; k < span; k += 32) buf[k] = *reinterpret_cast<const unsigned char*>(a + k);
+  __syncwarp();
+  if (lane == 0) {
     fence_proxy_async();
-    mbar_arrive_expect_tx(bar, (uint32_t)bulk);
-    if (bulk > 0) bulk_g2s(buf, reinterpret_cast<const void*>(a), (uint32_t)bulk, bar);
+    const uint32_t bytes = hi > lo ? (uint32_t)(hi - lo) : 0u;
+    mbar_arrive_expect_tx(bar, bytes);
+    if (bytes) bulk_g2s(buf + lo, reinterpret_cast<const void*>(a + lo), bytes, bar);
   }
-  for (int k = (int)bulk + threadIdx.x; k < span; k += blockDim.x) buf[k] = *reinterpret_cast<const unsigned char*>(a + k);
 }
 
-// STAGES = 2: double-buffered rows (the next row's copy is in flight while this one is
-// processed); 1: one staged row at a time (rows too large for two buffers); 0: no
-// staging (unaligned tensors), values read from global memory.
-template <int DT, int STAGES, bool WEIGHTED, int THREADS>
-__global__ void __launch_bounds__(THREADS) xent_kernel(const __grid_constant__ XentParams P) {
+// STAGED: rows staged in shared memory in chunks (16-byte aligned logits and dlogits);
+// otherwise the passes read global memory.
+template <int DT, bool STAGED, bool WEIGHTED>
+__global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constant__ XentParams P) {
+  constexpr int THREADS = kXentThreads;
+  constexpr int NCH = kXentChunks;
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ uint64_t bars[2];
+  __shared__ uint64_t bars[NCH];
+  __shared__ unsigned done[NCH];   // warps finished with a chunk of the current row
   __shared__ float red_f[THREADS / 32];
-  __shared__ float red_pair[THREADS / 32];
+  __shared__ float red_s[THREADS / 32];
+  __shared__ float coef[4];   // A, B, G and the row mode of the current row
   __shared__ double red_d[THREADS / 32];
   __shared__ bool last;
   __shared__ int abort_flag;
@@ -173,225 +229,285 @@ __global__ void __launch_bounds__(THREADS) xent_kernel(const __grid_constant__ X
   const float inv_den = zero_all ? 0.0f : (float)(1.0 / D);
   const float e = P.smoothing;
   const bool smooth = e != 0.0f;
+  const int cvec = (int)(P.chunk >> 4);   // vectors per chunk
 
-  if (STAGES > 0) {
+  const int lane = threadIdx.x & 31;
+  if constexpr (STAGED) {
     if (threadIdx.x == 0) {
-      mbar_init(&bars[0], 1);
-      mbar_init(&bars[1], 1);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        mbar_init(&bars[c], 1);
+        done[c] = 0;
+      }
       abort_flag = 0;
       fence_proxy_async();
     }
     __syncthreads();
-  }
-  uint32_t phase0 = 0, phase1 = 0;
-  int64_t row = blockIdx.x;
-  if (STAGES > 0 && row < P.rows) stage_row<ES>(P, row, smem, &bars[0]);
-
-  for (int it = 0; row < P.rows; row += gridDim.x, ++it) {
-    const int buf = STAGES == 2 ? (it & 1) : 0;
-    const unsigned char* stage = smem + (size_t)buf * P.stage_stride;
-    const int64_t next = row + gridDim.x;
-    if (STAGES == 2 && next < P.rows)
-      stage_row<ES>(P, next, smem + (size_t)(buf ^ 1) * P.stage_stride, &bars[buf ^ 1]);
-    if (STAGES > 0) {
-      if (threadIdx.x == 0 && !wait_stage(&bars[buf], buf ? phase1 : phase0)) abort_flag = 1;
-      __syncthreads();
-      if (buf) phase1 ^= 1u; else phase0 ^= 1u;
-      if (abort_flag) {
-        if (threadIdx.x == 0) {
-          atomicAdd(&P.info->error, 1.0);
-          // Let a copy still in flight into the other buffer land (bounded) before leaving.
-          if (STAGES == 2 && next < P.rows) wait_stage(&bars[buf ^ 1], buf ? phase0 : phase1);
-        }
-        return;
-      }
+    if (threadIdx.x < 32 && (int64_t)blockIdx.x < P.rows) {
+#pragma unroll 1
+      for (int c = 0; c < NCH; ++c) stage_chunk<ES>(P, blockIdx.x, smem, &bars[c], c, lane);
     }
+  }
 
-    const int64_t t64 = P.targets[row];
+  uint32_t parity = 0;
+  // The target of the CTA's next row is loaded one row ahead.
+  int64_t t_next = (int64_t)blockIdx.x < P.rows ? P.targets[blockIdx.x] : 0;
+  for (int64_t row = blockIdx.x; row < P.rows; row += gridDim.x, parity ^= 1u) {
+    const int64_t next = row + gridDim.x;
+    const int64_t t64 = t_next;
+    if (next < P.rows) t_next = P.targets[next];
     const bool valid = t64 != P.ignore && t64 >= 0 && t64 < V;
     const int t = valid ? (int)t64 : -1;
     const int64_t row_base = row * (int64_t)V;
     const uintptr_t start = reinterpret_cast<uintptr_t>(P.logits) + (uintptr_t)(row_base * ES);
-    const int head = (int)(start & 15u);
+    const int head = STAGED ? (int)(start & 15u) : 0;
     const int span = head + V * ES;           // bytes from the 16-byte boundary to the row end
     const int nvec = (span + 15) >> 4;
     const int full_lo = head ? 1 : 0;         // vectors [full_lo, full_hi) hold only row elements
     const int full_hi = span >> 4;
-    const int dj = THREADS * EPV;
+    auto first_elem = [&](int k) { return (k * 16 - head) / ES; };
 
-    // Pass A: online max / sum of exp per thread. The running max propagates NaN
-    // (max.NaN.f32), so one value carries both; label smoothing also needs sum_c w_c x_c.
-    // Interior vectors need no bounds checks; the <= 2 edge vectors of the row are
-    // masked and taken by the first threads after the interior loop.
-    float m = -INFINITY, s = 0.0f;
-    double swx = 0.0;
-    auto accumulate = [&](const float* x, int j0, bool edge) {
-      float vmax = x[0];
-#pragma unroll
-      for (int q = 1; q < EPV; ++q) vmax = max_nan(vmax, x[q]);
-      const float mn = max_nan(m, vmax);
-      if (mn != m) {
-        s = m > -INFINITY ? s * ex2((m - mn) * kLog2e) : 0.0f;
-        m = mn;
+    // Vectors [lo, hi) of this thread, two per iteration (independent work for the
+    // scheduler to interleave).
+    auto for_vectors = [&](int lo, int hi, auto&& body) {
+      int k = lo + (int)threadIdx.x;
+      for (; k + THREADS < hi; k += 2 * THREADS) {
+        body(k);
+        body(k + THREADS);
       }
-      if (m > -INFINITY) {
-        const float sh = m * kLog2e;
-#pragma unroll
-        for (int q = 0; q < EPV; ++q) s += ex2(fmaf(x[q], kLog2e, -sh));
-      }
-      if (smooth) {
-#pragma unroll
-        for (int q = 0; q < EPV; ++q) {
-          const int j = j0 + q;
-          if (!edge || (j >= 0 && j < V)) swx += WEIGHTED ? (double)P.weight[j] * (double)x[q] : (double)x[q];
-        }
-      }
+      if (k < hi) body(k);
     };
+    // The <= 2 edge vectors (the head vector when the row starts inside it, the tail vector
+    // when the row ends inside it; one vector when the whole row fits in it), taken by
+    // threads 0 and 1; `in_range(k)` limits them to a chunk.
+    const int tail_k = full_hi < nvec && full_hi >= full_lo ? full_hi : -1;
+    auto edge_vector = [&](int lo, int hi) {
+      int k = -1;
+      if (threadIdx.x == 0 && full_lo) k = 0;
+      if (threadIdx.x == (full_lo ? 1 : 0)) k = tail_k;
+      return k >= lo && k < hi ? k : -1;
+    };
+    auto interior = [&](int lo, int hi, int& a, int& b) {
+      a = lo > full_lo ? lo : full_lo;
+      b = hi < full_hi ? hi : full_hi;
+    };
+
+    // Pass 1: the row max, chunk by chunk as the chunks land. NaN propagates (max.NaN).
+    float m = -INFINITY;
     {
-      int j0 = ((full_lo + (int)threadIdx.x) * 16 - head) / ES;
-      for (int k = full_lo + threadIdx.x; k < full_hi; k += THREADS, j0 += dj) {
-        float x[EPV];
-        row_vector<DT, STAGES>(stage, P.logits, row_base, k, j0, V, x);
-        accumulate(x, j0, false);
-      }
-      // Edge vectors: the head vector when the row starts inside it and the tail vector when the
-      // row ends inside it; one vector when the whole row fits in it.
-      const int nedge = full_lo + ((full_hi < nvec && full_hi >= full_lo) ? 1 : 0);
-      if ((int)threadIdx.x < nedge) {
-        const int k = (threadIdx.x == 0 && full_lo) ? 0 : full_hi;
-        const int j0e = (k * 16 - head) / ES;
-        float x[EPV];
-        row_vector<DT, STAGES>(stage, P.logits, row_base, k, j0e, V, x);
+      uint32_t m2 = DT == NT_BF16 ? 0xff80ff80u : 0xfc00fc00u;   // a pair of -inf
+#pragma unroll 1
+      for (int c = 0; c < (STAGED ? NCH : 1); ++c) {
+        int k0 = 0, k1 = nvec;
+        if constexpr (STAGED) {
+          k0 = c * cvec;
+          k1 = k0 + cvec < nvec ? k0 + cvec : nvec;
+          if (k0 < k1 && !wait_stage(&bars[c], parity)) abort_flag = 1;
+        }
+        int a, b;
+        interior(k0, k1, a, b);
+        for_vectors(a, b, [&](int k) {
+          if constexpr (STAGED && DT != NT_F32) {
+            const uint4 raw = row_raw<DT, true>(smem, k);
+            m2 = max_nan_x2<DT>(m2, max_nan_x2<DT>(max_nan_x2<DT>(raw.x, raw.y), max_nan_x2<DT>(raw.z, raw.w)));
+          } else {
+            float x[EPV];
+            row_values<DT, STAGED>(smem, P.logits, row_base, k, first_elem(k), V, false, x);
 #pragma unroll
-        for (int q = 0; q < EPV; ++q)
-          if (j0e + q < 0 || j0e + q >= V) x[q] = -INFINITY;
-        accumulate(x, j0e, true);
+            for (int q = 0; q < EPV; ++q) m = max_nan(m, x[q]);
+          }
+        });
       }
-    }
-    // One block-wide merge of the (max, sum) pairs, in a fixed order.
-    {
-      const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+      const int k = edge_vector(0, nvec);
+      if (k >= 0) {
+        float x[EPV];
+        row_values<DT, STAGED>(smem, P.logits, row_base, k, first_elem(k), V, true, x);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-        const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-        const float mm = max_nan(m, m2);
-        s = mm > -INFINITY ? (m > -INFINITY ? s * ex2((m - mm) * kLog2e) : 0.0f) +
-                                 (m2 > -INFINITY ? s2 * ex2((m2 - mm) * kLog2e) : 0.0f)
-                           : 0.0f;
-        m = mm;
+        for (int q = 0; q < EPV; ++q) m = max_nan(m, x[q]);
       }
-      if (lane == 0) { red_f[warp] = m; red_pair[warp] = s; }
-      __syncthreads();
-      float M0 = -INFINITY;
-#pragma unroll 4
-      for (int w = 0; w < THREADS / 32; ++w) M0 = max_nan(M0, red_f[w]);
-      float S0 = 0.0f;
-      if (M0 > -INFINITY) {
-#pragma unroll 4
-        for (int w = 0; w < THREADS / 32; ++w)
-          if (red_f[w] > -INFINITY) S0 += red_pair[w] * ex2((red_f[w] - M0) * kLog2e);
-      }
-      m = M0;
-      s = S0;
+      if constexpr (DT != NT_F32) m = max_nan(m, max_of_pair<DT>(m2));
     }
-    const float M = m;
-    const float S = s;
-    if (smooth) swx = block_reduce(swx, red_d, SumOp(), 0.0);
+    const float M = block_reduce(m, red_f, [](float a, float b) { return max_nan(a, b); }, -INFINITY);
+    if (STAGED && abort_flag) {
+      // A copy did not land in time: report it, let this row's other copies land (each wait
+      // bounded) and leave. No copy of the next row has been issued yet.
+      if (threadIdx.x == 0) {
+        atomicAdd(&P.info->error, 1.0);
+        for (int c = 0; c < NCH; ++c) wait_stage(&bars[c], parity);
+      }
+      return;
+    }
     const bool bad_row = M != M || M == INFINITY;
     const bool neg_row = !bad_row && M == -INFINITY;
 
-    // Row loss and the gradient coefficients: d_c = e_c * A - G_c, minus B at c == t.
-    const float wt = valid ? (WEIGHTED ? P.weight[t] : 1.0f) : 0.0f;
-    int mode = 0;  // 0: zero row, 1: NaN row, 2: regular
-    float loss_i = 0.0f, A = 0.0f, B = 0.0f, G = 0.0f;
-    if (valid && !zero_all) {
-      if (bad_row) {
-        mode = 1;
-        loss_i = __int_as_float(0x7fc00000);
-      } else if (neg_row) {
-        loss_i = INFINITY;
-      } else {
-        mode = 2;
-        float xt;
-        if constexpr (STAGES > 0) {
-          const int off = head + t * ES;
-          if constexpr (DT == NT_F32) xt = *reinterpret_cast<const float*>(stage + off);
-          else if constexpr (DT == NT_BF16) xt = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(stage + off));
-          else xt = __half2float(*reinterpret_cast<const __half*>(stage + off));
-        } else {
-          xt = load1<DT>(P.logits, row_base + t);
-        }
-        const float lse = M + logf(S);
-        const float base = -wt * (xt - lse);
+    // Pass 2: sum of exp(x - M) (2^(x log2e - M log2e): one FMA and one SFU op per element;
+    // masked lanes are -inf and add 0); label smoothing also needs sum_c w_c x_c.
+    // One partial sum per vector lane keeps the additions of a vector independent.
+    float s = 0.0f;
+    double swx = 0.0;
+    if (!bad_row && !neg_row) {
+      const float sh = M * kLog2e;
+      float part[EPV];
+#pragma unroll
+      for (int q = 0; q < EPV; ++q) part[q] = 0.0f;
+      auto add = [&](int k, bool edge) {
+        const int j0 = first_elem(k);
+        float x[EPV];
+        row_values<DT, STAGED>(smem, P.logits, row_base, k, j0, V, edge, x);
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) part[q] += ex2(fmaf(x[q], kLog2e, -sh));
         if (smooth) {
-          const double sm = -(swx - (double)lse * W) / (double)V;
-          loss_i = (1.0f - e) * base + e * (float)sm;
-        } else {
-          loss_i = base;
-        }
-        const float invS = 1.0f / S;
-        const float a_coef = WEIGHTED ? ((1.0f - e) * wt + (float)((double)e * W / (double)V)) * inv_den : inv_den;
-        A = a_coef * invS;
-        B = (1.0f - e) * wt * inv_den;
-        G = smooth ? (float)((double)e / (double)V) * inv_den : 0.0f;
-      }
-    }
-    if (threadIdx.x == 0) P.row_loss[row] = loss_i;
-
-    // Pass B: gradient.
-    if (P.dl != nullptr) {
-      const uintptr_t out_start = reinterpret_cast<uintptr_t>(P.dl) + (uintptr_t)(row_base * ES);
-      const uintptr_t oa = out_start & ~(uintptr_t)15;
-      const bool vec_out = STAGES > 0 && (int)(out_start - oa) == head;
-      const float shM = M * kLog2e;
-      const int kt = valid ? ((head + t * ES) >> 4) : -1;
-      const int lane_t = valid ? (((head + t * ES) & 15) / ES) : 0;
-      const float nanv = __int_as_float(0x7fc00000);
-      auto gradient = [&](int k, int j0, float* d) {
-        if (mode == 2) {
-          float x[EPV];
-          row_vector<DT, STAGES>(stage, P.logits, row_base, k, j0, V, x);
 #pragma unroll
           for (int q = 0; q < EPV; ++q) {
-            const float g = WEIGHTED ? G * ((j0 + q >= 0 && j0 + q < V) ? P.weight[j0 + q] : 0.0f) : G;
-            d[q] = fmaf(ex2(fmaf(x[q], kLog2e, -shM)), A, -g);
+            const int j = j0 + q;
+            if (!edge || (j >= 0 && j < V)) swx += WEIGHTED ? (double)P.weight[j] * (double)x[q] : (double)x[q];
           }
-          if (k == kt) {
-#pragma unroll
-            for (int q = 0; q < EPV; ++q)
-              if (q == lane_t) d[q] -= B;
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < EPV; ++q) d[q] = mode == 1 ? nanv : 0.0f;
         }
       };
-      auto store_scalar = [&](int j0, const float* d) {
+      for_vectors(full_lo, full_hi, [&](int k) { add(k, false); });
+      const int k = edge_vector(0, nvec);
+      if (k >= 0) add(k, true);
 #pragma unroll
-        for (int q = 0; q < EPV; ++q) {
-          const int j = j0 + q;
-          if (j >= 0 && j < V) store1<DT>(P.dl, row_base + j, d[q]);
-        }
-      };
-      int j0 = ((full_lo + (int)threadIdx.x) * 16 - head) / ES;
-      for (int k = full_lo + threadIdx.x; k < full_hi; k += THREADS, j0 += dj) {
-        float d[EPV];
-        gradient(k, j0, d);
-        if (vec_out) __stcs(reinterpret_cast<uint4*>(oa + (uintptr_t)k * 16), pack16<DT>(d));
-        else store_scalar(j0, d);
-      }
-      const int nedge = full_lo + ((full_hi < nvec && full_hi >= full_lo) ? 1 : 0);
-      if ((int)threadIdx.x < nedge) {
-        const int k = (threadIdx.x == 0 && full_lo) ? 0 : full_hi;
-        const int j0e = (k * 16 - head) / ES;
-        float d[EPV];
-        gradient(k, j0e, d);
-        store_scalar(j0e, d);
+      for (int q = 0; q < EPV; ++q) s += part[q];
+    }
+    // Row sum, row loss and the gradient coefficients (d_c = e_c * A - G_c, minus B at
+    // c == t): warp partials in shared memory; warp 0 adds them (a fixed shuffle tree),
+    // computes the row's scalars once and broadcasts them.
+    constexpr int NW = THREADS / 32;
+    {
+      const float sw = warp_sum(s);
+      const double dw = smooth ? warp_sum(swx) : 0.0;
+      if (lane == 0) {
+        red_s[threadIdx.x >> 5] = sw;
+        if (smooth) red_d[threadIdx.x >> 5] = dw;
       }
     }
-    __syncthreads();  // every thread is done with this row's buffer and reduction scratch
-    if (STAGES == 1 && next < P.rows) stage_row<ES>(P, next, smem, &bars[0]);
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const float S = warp_sum(lane < NW ? red_s[lane] : 0.0f);
+      const double sx = smooth ? warp_sum(lane < NW ? red_d[lane] : 0.0) : 0.0;
+      if (lane == 0) {
+        const float wt = valid ? (WEIGHTED ? P.weight[t] : 1.0f) : 0.0f;
+        int mode = 0;  // 0: zero row, 1: NaN row, 2: regular
+        float loss_i = 0.0f, A = 0.0f, B = 0.0f, G = 0.0f, xt = 0.0f;
+        if (valid && !zero_all) {
+          if (bad_row) {
+            mode = 1;
+            loss_i = __int_as_float(0x7fc00000);
+          } else if (neg_row) {
+            loss_i = INFINITY;
+          } else {
+            mode = 2;
+            if constexpr (STAGED) {
+              const int off = head + t * ES;
+              if constexpr (DT == NT_F32) xt = *reinterpret_cast<const float*>(smem + off);
+              else if constexpr (DT == NT_BF16) xt = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(smem + off));
+              else xt = __half2float(*reinterpret_cast<const __half*>(smem + off));
+            } else {
+              xt = load1<DT>(P.logits, row_base + t);
+            }
+            const float lse = M + logf(S);
+            const float base = -wt * (xt - lse);
+            if (smooth) {
+              const double sm = -(sx - (double)lse * W) / (double)V;
+              loss_i = (1.0f - e) * base + e * (float)sm;
+            } else {
+              loss_i = base;
+            }
+            const float invS = 1.0f / S;
+            const float a_coef = WEIGHTED ? ((1.0f - e) * wt + (float)((double)e * W / (double)V)) * inv_den : inv_den;
+            A = a_coef * invS;
+            B = (1.0f - e) * wt * inv_den;
+            G = smooth ? (float)((double)e / (double)V) * inv_den : 0.0f;
+          }
+        }
+        P.row_loss[row] = loss_i;
+        coef[0] = A; coef[1] = B; coef[2] = G; coef[3] = __int_as_float(mode);
+      }
+    }
+    __syncthreads();
+    const float A = coef[0], B = coef[1], G = coef[2];
+    const int mode = __float_as_int(coef[3]);
+
+    // Pass 3: the gradient, chunk by chunk. The last warp to finish a chunk refills it with
+    // the CTA's next row (a shared-memory count per chunk; no warp waits for another).
+    const uintptr_t out_start = reinterpret_cast<uintptr_t>(P.dl) + (uintptr_t)(row_base * ES);
+    const uintptr_t oa = out_start & ~(uintptr_t)15;
+    const bool vec_out = STAGED && (int)(out_start - oa) == head;
+    const float shM = M * kLog2e;
+    const float fill = mode == 1 ? __int_as_float(0x7fc00000) : 0.0f;
+    const int kt = mode == 2 ? ((head + t * ES) >> 4) : -1;
+    const int lane_t = mode == 2 ? (((head + t * ES) & 15) / ES) : 0;
+    auto grad_vector = [&](int k, float* d) {
+      const int j0 = first_elem(k);
+      if (mode == 2) {
+        float x[EPV];
+        row_values<DT, STAGED>(smem, P.logits, row_base, k, j0, V, false, x);
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) {
+          const float g = WEIGHTED ? G * ((j0 + q >= 0 && j0 + q < V) ? P.weight[j0 + q] : 0.0f) : G;
+          d[q] = fmaf(ex2(fmaf(x[q], kLog2e, -shM)), A, -g);
+        }
+        if (k == kt) {
+#pragma unroll
+          for (int q = 0; q < EPV; ++q)
+            if (q == lane_t) d[q] -= B;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) d[q] = fill;
+      }
+    };
+    auto store_scalar = [&](int k, const float* d) {
+      const int j0 = first_elem(k);
+#pragma unroll
+      for (int q = 0; q < EPV; ++q) {
+        const int j = j0 + q;
+        if (j >= 0 && j < V) store1<DT>(P.dl, row_base + j, d[q]);
+      }
+    };
+#pragma unroll 1
+    for (int c = 0; c < (STAGED ? NCH : 1); ++c) {
+      int k0 = 0, k1 = nvec;
+      if constexpr (STAGED) {
+        k0 = c * cvec;
+        k1 = k0 + cvec < nvec ? k0 + cvec : nvec;
+      }
+      if (P.dl != nullptr) {
+        int a, b;
+        interior(k0, k1, a, b);
+        if (vec_out) {
+          for_vectors(a, b, [&](int k) {
+            float d[EPV];
+            grad_vector(k, d);
+            __stcs(reinterpret_cast<uint4*>(oa + (uintptr_t)k * 16), pack16<DT>(d));
+          });
+        } else {
+          for_vectors(a, b, [&](int k) {
+            float d[EPV];
+            grad_vector(k, d);
+            store_scalar(k, d);
+          });
+        }
+        const int k = edge_vector(k0, k1);
+        if (k >= 0) {
+          float d[EPV];
+          grad_vector(k, d);
+          store_scalar(k, d);
+        }
+      }
+      if constexpr (STAGED) {
+        // This warp's reads of chunk c are complete (their values are consumed above).
+        __syncwarp();
+        unsigned last_warp = 0;
+        if (lane == 0) {
+          __threadfence_block();
+          last_warp = atomicAdd(&done[c], 1u) == THREADS / 32 - 1;
+          if (last_warp) done[c] = 0;
+        }
+        if (__shfl_sync(0xffffffffu, last_warp, 0) && next < P.rows) stage_chunk<ES>(P, next, smem, &bars[c], c, lane);
+      }
+    }
   }
 
   // Loss reduction over rows, in a fixed order, by the last block.
@@ -420,20 +536,20 @@ __global__ void __launch_bounds__(256) xent_scale_kernel(void* dl, int64_t rows,
   }
 }
 
-template <int DT, int STAGES, bool WEIGHTED, int THREADS>
+template <int DT, bool STAGED, bool WEIGHTED>
 static int launch_variant(const XentParams& P, size_t smem, cudaStream_t stream) {
-  auto kernel = xent_kernel<DT, STAGES, WEIGHTED, THREADS>;
+  auto kernel = xent_kernel<DT, STAGED, WEIGHTED>;
   if (smem > 0) {
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(xent)");
   }
   int per_sm = 1;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, THREADS, smem) != cudaSuccess || per_sm < 1)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kXentThreads, smem) != cudaSuccess || per_sm < 1)
     per_sm = 1;
   int64_t grid = (int64_t)current_sm_count() * per_sm;
   if (grid > P.rows) grid = P.rows;
   if (grid < 1) grid = 1;
-  kernel<<<(unsigned)grid, THREADS, smem, stream>>>(P);
+  kernel<<<(unsigned)grid, kXentThreads, smem, stream>>>(P);
   return launch_status("nt_softmax_xent launch");
 }
 
@@ -441,20 +557,19 @@ template <int DT, bool WEIGHTED>
 static int launch_xent(const XentParams& P0, cudaStream_t stream) {
   XentParams P = P0;
   constexpr int ES = DT == NT_F32 ? 4 : 2;
-  // Row buffer: the row plus up to 15 leading bytes, rounded to 128 bytes.
-  const size_t stride = (size_t)((P.classes * ES + 16 + 127) / 128 * 128);
-  P.stage_stride = (int64_t)stride;
+  // Row buffer: the row plus up to 15 leading bytes, in kXentChunks chunks of a multiple of
+  // 128 bytes. Two CTAs share an SM where two buffers fit (16-bit rows up to ~56K classes).
+  const int64_t need = (P.classes * ES + 15 + 15) / 16 * 16;
+  const int64_t chunk = (need + kXentChunks - 1) / kXentChunks;
+  P.chunk = (chunk + 127) / 128 * 128;
+  const size_t buffer = (size_t)P.chunk * kXentChunks;
   int max_optin = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   const size_t budget = (size_t)max_optin > 4096 ? (size_t)max_optin - 4096 : 0;
-  // Each CTA stages one row; where two buffers fit on an SM (bf16 / fp16 rows up to
-  // ~56K classes) two CTAs share it and one's copy overlaps the other's compute.
-  int sm_smem = 0;
-  cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-  (void)sm_smem;
-  if (P.staged && stride <= budget) return launch_variant<DT, 1, WEIGHTED, 512>(P, stride, stream);
-  return launch_variant<DT, 0, WEIGHTED, 512>(P, 0, stream);
+  if (P.staged && buffer <= budget) return launch_variant<DT, true, WEIGHTED>(P, buffer, stream);
+  P.chunk = 16;
+  return launch_variant<DT, false, WEIGHTED>(P, 0, stream);
 }
 
 template <int DT>

@@ -179,3 +179,33 @@ def test_full_config4_properties(cuda_device):
     sums = dl.float().sum(dim=1).abs().max().item()
     assert sums < 1e-6
     assert np.isfinite(float(loss.item())) and 10.0 < float(loss.item()) < 14.0
+
+
+@pytest.mark.parametrize("dtype,rows,classes,shift", [
+    (torch.float32, 1500, 1000, 0),      # several rows per block: chunk refills with the next row
+    (torch.bfloat16, 3000, 4097, 0),     # rows start at every 2-byte offset within 16 bytes
+    (torch.float16, 2000, 333, 0),       # rows shorter than a chunk's share of the threads
+    (torch.bfloat16, 700, 999, 1),       # logits not 16-byte aligned: the unstaged passes
+])
+def test_many_rows_and_unaligned_match_oracle(cuda_device, dtype, rows, classes, shift):
+    rng = np.random.default_rng(rows + classes)
+    x32 = rng.normal(0, 2, (rows, classes)).astype(np.float32)
+    if dtype is torch.bfloat16:
+        x32 = round_to_bf16(x32)
+    elif dtype is torch.float16:
+        x32 = x32.astype(np.float16).astype(np.float32)
+    targets = rng.integers(0, classes, rows)
+    targets[::11] = -100
+    flat = torch.empty(rows * classes + shift, dtype=dtype, device="cuda")
+    x = flat[shift:].view(rows, classes)
+    x.copy_(torch.from_numpy(x32).to(dtype))
+    assert (x.data_ptr() % 16 == 0) == (shift == 0)
+    loss, dl = softmax_cross_entropy(x, torch.from_numpy(targets).cuda())
+    ref_loss, ref_dl = oxent.cross_entropy(x32, targets)
+    assert abs(float(loss.item()) - float(ref_loss)) <= 1e-5 * abs(float(ref_loss))
+    if dtype is torch.bfloat16:
+        assert_bf16_close(dl, ref_dl)
+    elif dtype is torch.float16:
+        np.testing.assert_allclose(dl.float().cpu().numpy(), ref_dl, rtol=2e-3, atol=2e-7)
+    else:
+        np.testing.assert_allclose(dl.cpu().numpy(), ref_dl, rtol=1e-5, atol=1e-9)
