@@ -143,6 +143,12 @@ __device__ __forceinline__ void packed_row(const SoftmaxParams& P, int64_t row, 
   }
 }
 
+// r % n, in 32 bits when both fit (a 64-bit division costs several times more).
+__device__ __forceinline__ int64_t row_mod(int64_t r, int64_t n) {
+  if ((uint64_t)r <= 0xffffffffull && (uint64_t)n <= 0xffffffffull) return (int64_t)((uint32_t)r % (uint32_t)n);
+  return r % n;
+}
+
 template <int DT, int NPL, int WARPS, bool BACKWARD, bool VEC>
 __global__ void __launch_bounds__(kSoftmaxThreads) row_softmax_kernel(const __grid_constant__ SoftmaxParams P) {
   __shared__ float smem[kSoftmaxThreads / 32];
@@ -166,11 +172,11 @@ __global__ void __launch_bounds__(kSoftmaxThreads) row_softmax_kernel(const __gr
     // The last allowed column of the row (-1: none): the width, cut by the causal rule.
     int last = live ? width - 1 : -1;
     if (P.causal) {
-      const int64_t limit = P.offset + r % P.queries;
+      const int64_t limit = P.offset + row_mod(r, P.queries);
       if (limit < last) last = (int)limit;
     }
     const uint8_t* mrow = P.mask == nullptr ? nullptr
-                          : P.mask + (P.mask_rows == 0 ? 0 : (r % P.mask_rows) * (int64_t)width);
+                          : P.mask + (P.mask_rows == 0 ? 0 : row_mod(r, P.mask_rows) * (int64_t)width);
     if constexpr (ES == 2 && VEC && BACKWARD) {
       packed_row<DT, NPL, WARPS, BACKWARD>(P, row, live, last, mrow, t, smem);
       continue;
@@ -195,20 +201,52 @@ __global__ void __launch_bounds__(kSoftmaxThreads) row_softmax_kernel(const __gr
 #pragma unroll
       for (int q = 0; q < NPL; ++q) dot = __fadd_rn(dot, __fmul_rn(w[q], v[q]));
       dot = row_sum<WARPS>(dot, smem);
+      if (vec && mrow == nullptr) {
+        // Whole vectors: per-element checks only where a vector reaches past `last`.
 #pragma unroll
-      for (int q = 0; q < NPL; ++q) {
-        const int j = slot_column<EPV>(q, t, T, vec);
-        const bool ok = j <= last && (mrow == nullptr || __ldg(mrow + j) != 0);
-        v[q] = ok ? __fmul_rn(v[q], __fsub_rn(w[q], dot)) : 0.0f;
+        for (int c = 0; c < NPL / EPV; ++c) {
+          const int j0 = (c * T + t) * EPV;
+          if (j0 + EPV - 1 <= last) {
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) v[c * EPV + e] = __fmul_rn(v[c * EPV + e], __fsub_rn(w[c * EPV + e], dot));
+          } else {
+#pragma unroll
+            for (int e = 0; e < EPV; ++e)
+              v[c * EPV + e] = j0 + e <= last ? __fmul_rn(v[c * EPV + e], __fsub_rn(w[c * EPV + e], dot)) : 0.0f;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < NPL; ++q) {
+          const int j = slot_column<EPV>(q, t, T, vec);
+          const bool ok = j <= last && (mrow == nullptr || __ldg(mrow + j) != 0);
+          v[q] = ok ? __fmul_rn(v[q], __fsub_rn(w[q], dot)) : 0.0f;
+        }
       }
     } else {
       float m = NEG_INF;
+      if (vec && mrow == nullptr) {
+        // Whole vectors: only a vector that reaches past the last allowed column (the
+        // diagonal of a causal row, or a vector past the width) needs per-element masking.
 #pragma unroll
-      for (int q = 0; q < NPL; ++q) {
-        const int j = slot_column<EPV>(q, t, T, vec);
-        const bool ok = j <= last && (mrow == nullptr || __ldg(mrow + j) != 0);
-        v[q] = ok ? v[q] : NEG_INF;
-        m = max_nan(m, v[q]);
+        for (int c = 0; c < NPL / EPV; ++c) {
+          const int j0 = (c * T + t) * EPV;
+          if (j0 + EPV - 1 > last) {
+#pragma unroll
+            for (int e = 0; e < EPV; ++e)
+              if (j0 + e > last) v[c * EPV + e] = NEG_INF;
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < NPL; ++q) m = max_nan(m, v[q]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < NPL; ++q) {
+          const int j = slot_column<EPV>(q, t, T, vec);
+          const bool ok = j <= last && (mrow == nullptr || __ldg(mrow + j) != 0);
+          v[q] = ok ? v[q] : NEG_INF;
+          m = max_nan(m, v[q]);
+        }
       }
       m = row_max<WARPS>(m, smem);
       const bool empty = m == NEG_INF;
@@ -222,20 +260,25 @@ __global__ void __launch_bounds__(kSoftmaxThreads) row_softmax_kernel(const __gr
       float s = 0.0f;
       if (!empty && !invalid) {
         const float ml = m * kLog2e;
+        float s2 = 0.0f;   // two partial sums: independent additions
 #pragma unroll
         for (int q = 0; q < NPL; ++q) {
           v[q] = ex2(fmaf(v[q], kLog2e, -ml));
-          s += v[q];
+          if (q & 1) s2 += v[q];
+          else s += v[q];
         }
+        s += s2;
       } else {
 #pragma unroll
         for (int q = 0; q < NPL; ++q) v[q] = empty ? 0.0f : __int_as_float(0x7fffffff);
         s = empty ? 0.0f : __int_as_float(0x7fffffff);
       }
       s = row_sum<WARPS>(s, smem);
-      const float inv = __frcp_rn(s);
+      if (!empty) {
+        const float inv = __frcp_rn(s);
 #pragma unroll
-      for (int q = 0; q < NPL; ++q) v[q] = empty ? 0.0f : v[q] * inv;
+        for (int q = 0; q < NPL; ++q) v[q] *= inv;
+      }
     }
     if (live) store_row<DT, NPL, WARPS>(yrow, width, t, vec, v);
   }
