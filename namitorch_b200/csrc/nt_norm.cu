@@ -99,15 +99,19 @@ __global__ void __launch_bounds__(NormShape<WARPS>::kThreads) norm_forward_kerne
       P.stats[2 * row] = mean;
       P.stats[2 * row + 1] = inv;
     }
-    float wv[NPL], bv[NPL];
-    if (P.w != nullptr) load_row<DT, NPL, WARPS, false>(P.w, width, t, VEC, wv);
-    if (P.b != nullptr) load_row<DT, NPL, WARPS, false>(P.b, width, t, VEC, bv);
 #pragma unroll
-    for (int q = 0; q < NPL; ++q) {
-      float y = __fmul_rn(LAYER ? __fsub_rn(v[q], mean) : v[q], inv);
-      if (P.w != nullptr) y = __fmul_rn(y, wv[q]);
-      if (P.b != nullptr) y = __fadd_rn(y, bv[q]);
-      v[q] = y;
+    for (int c = 0; c < NPL / EPV; ++c) {
+      float wv[EPV], bv[EPV];
+      if (P.w != nullptr) load_group<DT, NPL, WARPS>(P.w, width, t, VEC, c, wv);
+      if (P.b != nullptr) load_group<DT, NPL, WARPS>(P.b, width, t, VEC, c, bv);
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) {
+        const int q = c * EPV + e;
+        float y = __fmul_rn(LAYER ? __fsub_rn(v[q], mean) : v[q], inv);
+        if (P.w != nullptr) y = __fmul_rn(y, wv[e]);
+        if (P.b != nullptr) y = __fadd_rn(y, bv[e]);
+        v[q] = y;
+      }
     }
     if (live) store_row<DT, NPL, WARPS>(static_cast<char*>(P.y) + base * ES, width, t, VEC, v);
   }
@@ -163,10 +167,13 @@ __global__ void __launch_bounds__(NormShape<WARPS>::kThreads) norm_backward_kern
     }
     if (want_dx) {
       if (P.w != nullptr) {
-        float wv[NPL];
-        load_row<DT, NPL, WARPS, false>(P.w, width, t, VEC, wv);
 #pragma unroll
-        for (int q = 0; q < NPL; ++q) g[q] = __fmul_rn(g[q], wv[q]);
+        for (int c = 0; c < NPL / EPV; ++c) {
+          float wv[EPV];
+          load_group<DT, NPL, WARPS>(P.w, width, t, VEC, c, wv);
+#pragma unroll
+          for (int e = 0; e < EPV; ++e) g[c * EPV + e] = __fmul_rn(g[c * EPV + e], wv[e]);
+        }
       }
       float sg = 0.0f, sp = 0.0f;
 #pragma unroll
@@ -217,10 +224,10 @@ __global__ void __launch_bounds__(NormShape<WARPS>::kThreads) norm_backward_kern
 }
 
 constexpr int kReduceColumns = 32;
-constexpr int kReduceLanes = 8;
+constexpr int kReduceLanes = 32;
 
 // Column sums of the blocks' partial rows (blockIdx.y: 0 weight, 1 bias). Lane j of a
-// column sums partial rows j, j + 8, ... in order; the 8 lane sums are then added in lane
+// column sums partial rows j, j + 32, ... in order; the 32 lane sums are then added in lane
 // order.
 __global__ void __launch_bounds__(kReduceColumns * kReduceLanes)
 norm_affine_reduce_kernel(const float* part_w, const float* part_b, int64_t slots, int width, float* out_w, float* out_b) {

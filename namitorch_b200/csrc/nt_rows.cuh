@@ -78,6 +78,31 @@ __device__ __forceinline__ void load_row(const void* base, int width, int t, boo
   }
 }
 
+// The EPV values of slot group c (slots c * EPV .. c * EPV + EPV - 1) of a row shared by every
+// row of the tensor (a weight or a bias), cached; 0 past the width. One group at a time keeps
+// only EPV of those values in registers.
+template <int DT, int NPL, int WARPS>
+__device__ __forceinline__ void load_group(const void* base, int width, int t, bool vec, int c, float* out) {
+  constexpr int ES = DT == NT_F32 ? 4 : 2;
+  constexpr int EPV = 16 / ES;
+  constexpr int T = 32 * WARPS;
+  if (vec) {
+    const int k = c * T + t;
+    if (k * EPV < width) {
+      unpack16<DT>(__ldg(static_cast<const uint4*>(base) + k), out);
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) out[e] = 0.0f;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPV; ++e) {
+      const int j = (c * EPV + e) * T + t;
+      out[e] = j < width ? load1<DT>(base, j) : 0.0f;
+    }
+  }
+}
+
 // One 16-byte vector: EPV values rounded to the storage type (round to nearest even; the
 // 16-bit types convert two values per instruction).
 template <int DT>
