@@ -87,6 +87,13 @@ def committed_traffic(kernel: str, workload: str):
         return None
 
 
+def pair_traffic(kernel: str, workload: str):
+    """Forward + backward dram bytes of one step from the committed ncu summaries, if both exist."""
+    fwd = committed_traffic(f"{kernel}_forward", workload)
+    bwd = committed_traffic(f"{kernel}_backward", workload)
+    return None if fwd is None or bwd is None else {"forward": fwd, "backward": bwd, "step": fwd + bwd}
+
+
 # ---- clocks sampling --------------------------------------------------------------------------
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -597,7 +604,8 @@ def run_softmax(args):
                            "peak_source": kind,
                            "algorithmic_bytes": {"forward": 2 * es * elems, "backward": 3 * es * elems},
                            "forward_gbs": 2 * es * elems / (fwd / 1e3) / 1e9,
-                           "backward_gbs": 3 * es * elems / (bwd / 1e3) / 1e9, "traffic": None},
+                           "backward_gbs": 3 * es * elems / (bwd / 1e3) / 1e9,
+                           "traffic": pair_traffic("row_softmax", f"softmax_{args.softmax_dtype}")},
               "gpu_launches": N.launch_count - launches0}
     if not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_softmax_sample(4096, t, os.cpu_count() or 1)
@@ -677,7 +685,7 @@ def run_norm(args):
                            "peak_source": kind,
                            "algorithmic_bytes": {"forward": 8 * elems, "backward": 12 * elems},
                            "forward_gbs": 8 * elems / (fwd / 1e3) / 1e9, "backward_gbs": 12 * elems / (bwd / 1e3) / 1e9,
-                           "traffic": None},
+                           "traffic": pair_traffic("norm", "norm")},
               "gpu_launches": N.launch_count - launches0}
     if not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_norm_sample(8192, width, os.cpu_count() or 1)
