@@ -50,7 +50,8 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["1p3b", "124m", "small", "xent", "softmax", "norm"], default="1p3b")
+    ap.add_argument("--workload", choices=["1p3b", "124m", "small", "xent", "softmax", "norm", "activation"],
+                    default="1p3b")
     ap.add_argument("--softmax-dtype", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-sample", type=int, default=1 << 25, help="parameters in the CPU baseline sample")
@@ -692,6 +693,83 @@ def run_norm(args):
     print(json.dumps(result), flush=True)
 
 
+def cpu_activation_sample(rows: int, width: int, threads: int) -> dict:
+    """The oracle's bias + gelu(tanh) forward and backward (the reference's arithmetic) on
+    `rows` rows of `width`, split over host threads."""
+    import concurrent.futures as cf
+    from oracle import activations as A
+    rng = np.random.default_rng(0)
+    x = rng.normal(0, 1, (rows, width)).astype(np.float32)
+    g = rng.normal(0, 1, (rows, width)).astype(np.float32)
+    b = rng.normal(0, 0.1, width).astype(np.float32)
+    per = max(1, -(-rows // threads))
+
+    def part(k):
+        lo, hi = k * per, min(rows, (k + 1) * per)
+        if lo < hi:
+            A.apply("bias_gelu_tanh", (x[lo:hi], b))
+            A.apply("bias_gelu_tanh_backward", (x[lo:hi], b, g[lo:hi]))
+
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(threads) as pool:
+        list(pool.map(part, range(threads)))
+    dt = time.perf_counter() - t0
+    return {"value": rows / dt, "unit": "rows/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} rows x {width} bias + gelu(tanh) forward + backward (oracle port of the reference's "
+                      "NumPy arithmetic), float32"}
+
+
+def run_activation(args):
+    """bias + gelu(tanh) forward and backward (the fused-elementwise seam) on the 1.3B model's
+    MLP activations: 16 sequences x 2048 tokens x 8192 hidden, float32."""
+    import torch
+    from namitorch_b200 import _native as N
+    from namitorch_b200.backends import get_backend
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    rows, width = 16 * 2048, 4 * 2048
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    x = torch.randn(rows, width, device=device, generator=gen)
+    g = torch.randn(rows, width, device=device, generator=gen)
+    b = torch.randn(width, device=device, generator=gen).mul_(0.1)
+    k = get_backend(x).fused
+    for _ in range(args.warmup):
+        k.run("bias_gelu_tanh", (x, b))
+        k.run("bias_gelu_tanh_backward", (x, b, g))
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    launches0 = N.launch_count
+    ev[0].record()
+    for _ in range(args.steps):
+        k.run("bias_gelu_tanh", (x, b))
+    ev[1].record()
+    for _ in range(args.steps):
+        k.run("bias_gelu_tanh_backward", (x, b, g))
+    ev[2].record()
+    torch.cuda.synchronize()
+    fwd, bwd = ev[0].elapsed_time(ev[1]) / args.steps, ev[1].elapsed_time(ev[2]) / args.steps
+    elems = x.numel()
+    peak, kind = measured_peak()
+    achieved = (8 + 12) * elems / ((fwd + bwd) / 1e3) / 1e9
+    result = {"metric": "bias+gelu(tanh) fwd+bwd rows/s", "value": rows / ((fwd + bwd) / 1e3), "unit": "rows/s",
+              "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": fwd + bwd,
+              "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+              "data": "synthetic",
+              "config": {"workload": f"MLP activations [{rows}, {width}] (1.3B model, 16 x 2048 tokens), bias [{width}]",
+                         "l2": f"inputs larger than L2 ({elems * 4 / 1e6:.0f} MB per tensor)"},
+              "kernels_ms": {"forward": fwd, "backward": bwd},
+              "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                           "peak_source": kind,
+                           "algorithmic_bytes": {"forward": 8 * elems, "backward": 12 * elems},
+                           "forward_gbs": 8 * elems / (fwd / 1e3) / 1e9, "backward_gbs": 12 * elems / (bwd / 1e3) / 1e9,
+                           "traffic": pair_traffic("fused_bias_gelu", "activation")},
+              "gpu_launches": N.launch_count - launches0}
+    if not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_activation_sample(2048, width, os.cpu_count() or 1)
+    print(json.dumps(result), flush=True)
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -717,6 +795,16 @@ def run_reference(args):
         base["value"] = value
         line = {"impl": "reference", "metric": "causal attention softmax fwd+bwd rows/s", "value": value,
                 "unit": "rows/s", "higher_is_better": True}
+    elif args.workload == "activation":
+        times = []
+        for i in range(args.warmup + args.steps):
+            base = cpu_activation_sample(1024, 8192, threads)
+            if i >= args.warmup:
+                times.append(base["value"])
+        value = statistics.median(times)
+        base["value"] = value
+        line = {"impl": "reference", "metric": "bias+gelu(tanh) fwd+bwd rows/s", "value": value, "unit": "rows/s",
+                "higher_is_better": True}
     elif args.workload == "norm":
         times = []
         for i in range(args.warmup + args.steps):
@@ -753,6 +841,9 @@ def main(argv=None):
         return
     if args.workload == "norm":
         run_norm(args)
+        return
+    if args.workload == "activation":
+        run_activation(args)
         return
     run_ours(args)
 

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define NT_ABI_VERSION 5
+#define NT_ABI_VERSION 6
 #define NT_MAX_GROUPS 32      /* coefficient groups per nt_adamw_mt call */
 #define NT_MAX_FOUND_INF 16   /* optimizers combined by one nt_scaler_update call */
 
@@ -355,6 +355,61 @@ int nt_norm_forward(const nt_norm_args* args, void* stream);
 /* Backward (normalization.py:86-157, 204-235): grad_input from the saved statistics, and the
    weight / bias gradients as per-tile partial sums reduced per column in a fixed order. */
 int nt_norm_backward(const nt_norm_args* args, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Fused elementwise activations                                                         */
+/* ------------------------------------------------------------------------------------ */
+
+/* The operations of the reference's FusedCUDAKernels (namitorch/backends/cuda/fused.py:44-69).
+   Operand roles per operation (count elements each unless noted):
+     NT_FUSED_SIGMOID, _SILU, _GELU_TANH                 output = f(a)
+     NT_FUSED_SIGMOID_BACKWARD                           output = b * a * (1 - a)   (a = sigmoid output)
+     NT_FUSED_SILU_BACKWARD, _GELU_TANH_BACKWARD         output = b * f'(a)
+     NT_FUSED_SWIGLU                                     output = silu(a) * b
+     NT_FUSED_SWIGLU_BACKWARD                            output = c * b * silu'(a), second = c * silu(a)
+     NT_FUSED_BIAS_<F>        (b: [width])               output = f(a + b[i % width])
+     NT_FUSED_BIAS_<F>_BACKWARD (b: [width], c: grad)    output = c * f'(a + b[i % width])
+     NT_FUSED_CLAMP           (b, c: one element or NULL) output = clamp(a, b[0], c[0])
+     NT_FUSED_CLAMP_BACKWARD  (d: grad)                   output = d where b[0] < a < c[0], else 0
+   with the reference's special cases (stable sigmoid, silu(-inf) = 0, gelu beyond |x| > 20,
+   NaN propagation in relu' and clamp). */
+enum {
+  NT_FUSED_SIGMOID = 0,
+  NT_FUSED_SILU = 1,
+  NT_FUSED_GELU_TANH = 2,
+  NT_FUSED_SIGMOID_BACKWARD = 3,
+  NT_FUSED_SILU_BACKWARD = 4,
+  NT_FUSED_GELU_TANH_BACKWARD = 5,
+  NT_FUSED_SWIGLU = 6,
+  NT_FUSED_SWIGLU_BACKWARD = 7,
+  NT_FUSED_BIAS_SIGMOID = 8,
+  NT_FUSED_BIAS_SILU = 9,
+  NT_FUSED_BIAS_GELU_TANH = 10,
+  NT_FUSED_BIAS_RELU = 11,
+  NT_FUSED_BIAS_SIGMOID_BACKWARD = 12,
+  NT_FUSED_BIAS_SILU_BACKWARD = 13,
+  NT_FUSED_BIAS_GELU_TANH_BACKWARD = 14,
+  NT_FUSED_BIAS_RELU_BACKWARD = 15,
+  NT_FUSED_CLAMP = 16,
+  NT_FUSED_CLAMP_BACKWARD = 17
+};
+
+typedef struct nt_fused_args {
+  int32_t op;            /* NT_FUSED_* */
+  int32_t dtype;         /* NT_F32 / NT_F16 / NT_BF16 of every operand and output */
+  const void* a;
+  const void* b;         /* second operand, bias [width], or the clamp minimum (NULL: none) */
+  const void* c;         /* third operand, or the clamp maximum (NULL: none) */
+  const void* d;         /* clamp backward: upstream gradient */
+  void* output;
+  void* second;          /* swiglu backward: gradient of the second operand */
+  int64_t count;         /* elements of `a` */
+  int64_t width;         /* bias operations: size of the last dimension (count % width == 0) */
+} nt_fused_args;
+
+/* One fused elementwise operation, the kernel bodies of namitorch/backends/cuda/fused.py:
+   8-69 (float32 there; float16 / bfloat16 here too, computed in float32 and rounded once). */
+int nt_fused_elementwise(const nt_fused_args* args, void* stream);
 
 /* ------------------------------------------------------------------------------------ */
 /* ZeRO-1 over peer memory (NVLink / NVSwitch)                                           */

@@ -22,7 +22,7 @@ NT_DECAY_NONE, NT_DECAY_DECOUPLED, NT_DECAY_COUPLED = 0, 1, 2
 NT_MAX_GROUPS = 32
 NT_MAX_FOUND_INF = 16
 NT_MAX_RANKS = 8
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 
 class Segment(C.Structure):
@@ -106,6 +106,17 @@ class SoftmaxArgs(C.Structure):
 NT_NORM_MAX_WIDTH = 8192
 NORM_OPS = {"rms_norm": 0, "layer_norm": 1}
 
+FUSED_OPS = {"sigmoid": 0, "silu": 1, "gelu_tanh": 2, "sigmoid_backward": 3, "silu_backward": 4,
+             "gelu_tanh_backward": 5, "swiglu": 6, "swiglu_backward": 7, "bias_sigmoid": 8, "bias_silu": 9,
+             "bias_gelu_tanh": 10, "bias_relu": 11, "bias_sigmoid_backward": 12, "bias_silu_backward": 13,
+             "bias_gelu_tanh_backward": 14, "bias_relu_backward": 15, "clamp": 16, "clamp_backward": 17}
+
+
+class FusedArgs(C.Structure):
+    _fields_ = [("op", C.c_int32), ("dtype", C.c_int32), ("a", C.c_void_p), ("b", C.c_void_p), ("c", C.c_void_p),
+                ("d", C.c_void_p), ("output", C.c_void_p), ("second", C.c_void_p), ("count", C.c_int64),
+                ("width", C.c_int64)]
+
 
 class NormArgs(C.Structure):
     _fields_ = [("op", C.c_int32), ("dtype", C.c_int32), ("input", C.c_void_p), ("weight", C.c_void_p),
@@ -162,6 +173,7 @@ SIGNATURES: dict[str, tuple] = {
     "nt_norm_workspace_size": (C.c_size_t, [C.c_int64, C.c_int64]),
     "nt_norm_forward": (C.c_int, [C.POINTER(NormArgs), C.c_void_p]),
     "nt_norm_backward": (C.c_int, [C.POINTER(NormArgs), C.c_void_p]),
+    "nt_fused_elementwise": (C.c_int, [C.POINTER(FusedArgs), C.c_void_p]),
     "nt_xent_workspace_size": (C.c_size_t, []),
     "nt_softmax_xent": (C.c_int, [C.POINTER(XentArgs), C.c_void_p]),
     "nt_xent_backward_scale": (C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_int64, C.c_void_p, C.c_int32,
@@ -221,14 +233,16 @@ LAUNCHES_PER_CALL = {"nt_adamw_f32": 1, "nt_adamw_mt": 1, "nt_adamw_mt_push": 1,
                      "nt_grad_stats": 1, "nt_grad_stats_finalize": 1, "nt_schedule_step": 1, "nt_row_softmax": 1, "nt_norm_forward": 1,
                      "nt_grad_stats_noalloc": 2,
                      "nt_grad_transform": 1, "nt_grad_clip_value": 1, "nt_scaler_update": 1,
-                     "nt_softmax_xent": 2, "nt_xent_backward_scale": 1, "nt_cast": 1}
+                     "nt_softmax_xent": 2, "nt_xent_backward_scale": 1, "nt_cast": 1, "nt_fused_elementwise": 1}
 launch_count = 0
 
 
-def call(name: str, *args) -> None:
+def call(name: str, *args, launches: int | None = None) -> None:
+    """Calls an entry point and raises on failure; counts the kernels it launched (the table
+    above, or `launches` for entry points whose count depends on the arguments)."""
     global launch_count
     check(getattr(load(), name)(*args), name)
-    launch_count += LAUNCHES_PER_CALL.get(name, 0)
+    launch_count += LAUNCHES_PER_CALL.get(name, 0) if launches is None else launches
 
 
 def stream_handle(stream=None) -> int:

@@ -46,6 +46,15 @@ def get_backend(value=None):
         return _backends[device]
 
 
+def try_fused(operation, *arrays):
+    """namitorch/backends/__init__.py:55-60: the fused elementwise operation, or None when
+    disabled or not applicable (the caller then uses its own path)."""
+    if not fused_kernels_enabled():
+        return None
+    kernels = getattr(get_backend(arrays[0]), "fused", None)
+    return None if kernels is None else kernels.run(operation, arrays)
+
+
 def try_fused_softmax(operation, *arrays, **parameters):
     """namitorch/backends/__init__.py:63-68: the fused row softmax, or None when disabled or
     not applicable (the caller then uses its own path)."""
@@ -63,5 +72,5 @@ def try_fused_normalization(operation, *arrays, **parameters):
     return None if kernels is None else kernels.run(operation, arrays, **parameters)
 
 
-__all__ = ["enable_fused_kernels", "fused_kernels_enabled", "get_backend", "try_fused_softmax",
+__all__ = ["enable_fused_kernels", "fused_kernels_enabled", "get_backend", "try_fused", "try_fused_softmax",
            "try_fused_normalization"]

@@ -57,15 +57,17 @@ class AdamWCUDAKernel:
 
 
 class CUDABackend:
-    """One per device (namitorch/backends/cuda/__init__.py:23-45); ``adamw``, ``softmax`` and
-    ``normalization`` are the plugin seams."""
+    """One per device (namitorch/backends/cuda/__init__.py:23-45); ``adamw``, ``fused``,
+    ``softmax`` and ``normalization`` are the plugin seams."""
 
     def __init__(self, device: torch.device):
         N.load()
         self.device = device
         self.adamw = AdamWCUDAKernel(self)
+        from .fused import FusedCUDAKernels
         from .normalization import NormalizationCUDAKernels
         from .softmax import SoftmaxCUDAKernels
+        self.fused = FusedCUDAKernels(self)
         self.softmax = SoftmaxCUDAKernels(self)
         self.normalization = NormalizationCUDAKernels(self)
 

@@ -107,7 +107,8 @@ class NormalizationCUDAKernels:
                           workspace=None if workspace is None else workspace.data_ptr(),
                           workspace_bytes=0 if workspace is None else workspace.numel(), rows=rows, width=width)
         with torch.cuda.device(value.device):
-            N.call("nt_norm_backward", N.C.byref(args), N.stream_handle())
+            N.call("nt_norm_backward", N.C.byref(args), N.stream_handle(),
+                   launches=int(rows > 0 and (dx is not None or workspace is not None)) + int(workspace is not None))
         cast = (lambda t: t if t is None or t.dtype == value.dtype else t.to(value.dtype))
         return dx, cast(dw), cast(db)
 

@@ -66,6 +66,7 @@ STRUCTS = {
     "nt_lr_entry": (N.LrEntry, [f for f, _ in N.LrEntry._fields_]),
     "nt_softmax_args": (N.SoftmaxArgs, [f for f, _ in N.SoftmaxArgs._fields_]),
     "nt_norm_args": (N.NormArgs, [f for f, _ in N.NormArgs._fields_]),
+    "nt_fused_args": (N.FusedArgs, [f for f, _ in N.FusedArgs._fields_]),
 }
 
 
@@ -87,3 +88,25 @@ def test_struct_layouts_match_the_c_compiler(tmp_path):
         assert int(out[cname]) == ctypes.sizeof(cls), cname
         for cf, (pf, _) in zip(fields or [], cls._fields_):
             assert int(out[f"{cname}.{cf}"]) == getattr(cls, pf).offset, f"{cname}.{cf}"
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
+def test_operation_codes_match_the_header(tmp_path):
+    """The Python operation tables carry the header's enum values."""
+    text = HEADER.read_text()
+    names = {f"NT_FUSED_{k.upper()}": v for k, v in N.FUSED_OPS.items()}
+    names.update({f"NT_{k.upper()}": v for k, v in N.SOFTMAX_OPS.items()})
+    names.update({"NT_RMS_NORM": N.NORM_OPS["rms_norm"], "NT_LAYER_NORM": N.NORM_OPS["layer_norm"]})
+    for name in names:
+        assert re.search(rf"\b{name}\b", text), name
+    lines = ["#include <stdio.h>", '#include "namitorch_b200.h"', "int main(void) {"]
+    lines += [f'  printf("{n} %d\\n", (int){n});' for n in names]
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "codes.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "codes"
+    subprocess.run(["gcc", "-I", str(REPO / "include"), str(src), "-o", str(exe)], check=True)
+    out = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                       check=True).stdout.splitlines())
+    for name, value in names.items():
+        assert int(out[name]) == value, name
