@@ -10,11 +10,12 @@
 // grid stride modulo the width instead of a division per vector. Half and bfloat16 operands
 // are computed in float32 and rounded once.
 //
-// The arithmetic follows the reference's device helpers, with CUDA's expf and tanhf:
+// The arithmetic follows the reference's device helpers, with CUDA's expf:
 //   sigmoid(x) = 1 / (1 + e) for x >= 0, e / (1 + e) otherwise, e = exp(-|x|)
 //   silu(x) = x * sigmoid(x) (0 at -inf); silu'(x) = s + x * s * (1 - s) (s alone where x is
 //   not finite); gelu(x) = 0.5 x (1 + tanh(k (x + 0.044715 x^3))), x itself (or -0) beyond
-//   |x| > 20, and its derivative; relu'(x) = NaN for NaN, else [x > 0].
+//   |x| > 20, and its derivative (evaluated through sigmoid, below); relu'(x) = NaN for NaN,
+//   else [x > 0].
 #include <cmath>
 
 #include "nt_common.cuh"
@@ -52,16 +53,26 @@ __device__ __forceinline__ float sigmoid_grad(float x) {
   const float s = sigmoid_of(x);
   return s * (1.0f - s);
 }
+// gelu with the tanh approximation through the identity 0.5 (1 + tanh(u)) = sigmoid(2u):
+// gelu(x) = x * sigmoid(2u) and gelu'(x) = s + 2 x s (1 - s) u', s = sigmoid(2u),
+// u = sqrt(2/pi) (x + 0.044715 x^3). One SFU exp2 and one reciprocal replace tanhf, with no
+// cancellation where tanh(u) is near -1; results agree with the tanh form to a few float32
+// ulps. 2^(-2u log2 e) overflows to +inf for very negative u, which gives s = 0.
+__device__ __forceinline__ float sigmoid_2u(float x) {
+  const float u = kGeluScale * (x + kGeluCubic * x * x * x);
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(u * -2.8853900817779268f));   // -2 log2(e) u
+  return __frcp_rn(1.0f + e);
+}
 __device__ __forceinline__ float gelu_of(float x) {
   if (fabsf(x) > 20.0f) return x > 0.0f ? x : -0.0f;
-  const float t = tanhf(kGeluScale * (x + kGeluCubic * x * x * x));
-  return (0.5f * x) * (1.0f + t);
+  return x * sigmoid_2u(x);
 }
 __device__ __forceinline__ float gelu_grad(float x) {
   if (fabsf(x) > 20.0f) return x > 0.0f ? 1.0f : 0.0f;
-  const float t = tanhf(kGeluScale * (x + kGeluCubic * x * x * x));
+  const float s = sigmoid_2u(x);
   const float inner = kGeluScale * (1.0f + kGeluCubic3 * x * x);
-  return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * inner;
+  return s + 2.0f * x * (s * (1.0f - s)) * inner;
 }
 __device__ __forceinline__ float relu_of(float x) { return x <= 0.0f ? 0.0f : x; }
 __device__ __forceinline__ float relu_grad(float x) { return isnan(x) ? x : (x > 0.0f ? 1.0f : 0.0f); }
