@@ -152,7 +152,10 @@ class _FirstOrderAdam(Optimizer):
     def step(self, closure=None):
         """namitorch/optim/_common.py:133-167, with every parameter updated by one launch."""
         if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
-            raise RuntimeError("Optimizer steps are not allowed during CUDA graph capture.")
+            from ..training import capture_in_progress
+            if not capture_in_progress():
+                raise RuntimeError("Optimizer steps are not allowed during CUDA graph capture (use "
+                                   "namitorch_b200.training.CapturedOptimizerStep).")
         if closure is not None and not callable(closure):
             raise TypeError("Optimizer closure must be callable or None.")
         loss = None

@@ -222,10 +222,8 @@ class LRScheduler:
         self._apply(values)
         self._host_step = step
 
-    def _device_step(self, gate) -> None:
-        self._validate_groups()
-        if gate is not None and not gate._invert:
-            raise TypeError("step(gate) expects the flag GradScaler.step returned.")
+    def _ensure_device_counter(self) -> "_DeviceCounter":
+        """Moves the step counter to the device (once) and attaches the schedule to the optimizer."""
         if self._device is None:
             params = self.optimizer._registered_parameters()
             device = params[0].device
@@ -233,7 +231,13 @@ class LRScheduler:
                 raise RuntimeError("A device-gated scheduler step needs the optimizer on a CUDA device.")
             self._device = _DeviceCounter(self, device)
             self.optimizer._lr_schedule = self
-        counter = self._device
+        return self._device
+
+    def _device_step(self, gate) -> None:
+        self._validate_groups()
+        if gate is not None and not gate._invert:
+            raise TypeError("step(gate) expects the flag GradScaler.step returned.")
+        counter = self._ensure_device_counter()
         with torch.cuda.device(counter.device):
             if gate is None:
                 N.call("nt_schedule_step", counter.step.data_ptr(), None, 0, N.stream_handle())
