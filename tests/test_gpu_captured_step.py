@@ -98,7 +98,7 @@ def test_replays_match_the_eager_loop_bit_for_bit(cuda_device, dtype):
         assert graph[key] == eager[key], key
     assert graph["last_step"] == STEPS - len(OVERFLOW)
     assert torch.equal(torch.stack(norms_graph), torch.stack(norms_eager))
-    # The host view stays usable after replays: one more eager iteration matches too.
+    # The host view (the groups' "lr") reads the device counter the replays advanced.
     assert [g["lr"] for g in opt.param_groups] == [float.fromhex(h) for h in eager["lrs"]]
 
 
