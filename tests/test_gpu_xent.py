@@ -209,3 +209,19 @@ def test_many_rows_and_unaligned_match_oracle(cuda_device, dtype, rows, classes,
         np.testing.assert_allclose(dl.float().cpu().numpy(), ref_dl, rtol=2e-3, atol=2e-7)
     else:
         np.testing.assert_allclose(dl.cpu().numpy(), ref_dl, rtol=1e-5, atol=1e-9)
+
+
+@pytest.mark.parametrize("shift", [0, 1])
+def test_forward_only_writes_no_gradient(cuda_device, shift):
+    """Logits that do not require grad: the launch has no dlogits; the loss still matches."""
+    rng = np.random.default_rng(9 + shift)
+    rows, classes = 600, 2049
+    x32 = round_to_bf16(rng.normal(0, 2, (rows, classes)).astype(np.float32))
+    t = rng.integers(0, classes, rows)
+    flat = torch.empty(rows * classes + shift, dtype=torch.bfloat16, device="cuda")
+    x = flat[shift:].view(rows, classes)
+    x.copy_(torch.from_numpy(x32).to(torch.bfloat16))
+    loss = cross_entropy(x, torch.from_numpy(t).cuda())
+    assert loss.grad_fn is None
+    ref_loss, _ = oxent.cross_entropy(x32, t, with_grad=False)
+    assert abs(float(loss.item()) - float(ref_loss)) <= 1e-5 * abs(float(ref_loss))
