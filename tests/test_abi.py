@@ -53,6 +53,45 @@ def test_errors_are_reported_without_a_gpu():
         N.check(lib.nt_softmax_xent(ctypes.byref(args), None))
 
 
+def test_kernel_seams_validate_before_touching_the_gpu():
+    """The softmax, normalization and elementwise entry points reject malformed calls (and
+    accept empty ones) without a CUDA call, so these run on a machine without a GPU."""
+    lib = N.load()
+    assert lib.nt_fused_elementwise(None, None) == N.NT_EINVAL
+    bad_op = N.FusedArgs(op=99, dtype=N.NT_F32, count=4)
+    assert lib.nt_fused_elementwise(ctypes.byref(bad_op), None) == N.NT_EINVAL
+    assert b"unknown operation" in lib.nt_last_error()
+    ragged = N.FusedArgs(op=N.FUSED_OPS["bias_relu"], dtype=N.NT_F32, count=10, width=4)
+    assert lib.nt_fused_elementwise(ctypes.byref(ragged), None) == N.NT_EINVAL
+    assert b"width" in lib.nt_last_error()
+    unbounded = N.FusedArgs(op=N.FUSED_OPS["clamp"], dtype=N.NT_F32, count=4)
+    assert lib.nt_fused_elementwise(ctypes.byref(unbounded), None) == N.NT_EINVAL
+    assert b"minimum or a maximum" in lib.nt_last_error()
+    double = N.FusedArgs(op=N.FUSED_OPS["silu"], dtype=7, count=4)
+    assert lib.nt_fused_elementwise(ctypes.byref(double), None) == N.NT_EUNSUPPORTED
+    missing = N.FusedArgs(op=N.FUSED_OPS["swiglu"], dtype=N.NT_BF16, count=8, a=16, output=16)
+    assert lib.nt_fused_elementwise(ctypes.byref(missing), None) == N.NT_EINVAL
+    assert b"operand b is NULL" in lib.nt_last_error()
+    empty = N.FusedArgs(op=N.FUSED_OPS["gelu_tanh"], dtype=N.NT_F16, count=0)
+    assert lib.nt_fused_elementwise(ctypes.byref(empty), None) == N.NT_OK
+    assert lib.nt_row_softmax(None, None) == N.NT_EINVAL
+    assert lib.nt_norm_forward(None, None) == N.NT_EINVAL
+    wide = N.NormArgs(op=N.NORM_OPS["layer_norm"], dtype=N.NT_F32, rows=2, width=N.NT_NORM_MAX_WIDTH + 1, eps=1e-5)
+    assert lib.nt_norm_forward(ctypes.byref(wide), None) == N.NT_EINVAL
+    rms_bias = N.NormArgs(op=N.NORM_OPS["rms_norm"], dtype=N.NT_F32, rows=2, width=8, bias=16, eps=1e-5)
+    assert lib.nt_norm_forward(ctypes.byref(rms_bias), None) == N.NT_EINVAL
+    assert b"RMS norm takes no bias" in lib.nt_last_error()
+    no_eps = N.NormArgs(op=N.NORM_OPS["layer_norm"], dtype=N.NT_F32, rows=2, width=8, input=16, output=16, eps=0.0)
+    assert lib.nt_norm_forward(ctypes.byref(no_eps), None) == N.NT_EINVAL
+    no_ws = N.NormArgs(op=N.NORM_OPS["layer_norm"], dtype=N.NT_F32, rows=2, width=8, input=16, gradient=16,
+                       statistics=16, grad_weight=16)
+    assert lib.nt_norm_backward(ctypes.byref(no_ws), None) == N.NT_EINVAL
+    assert b"workspace" in lib.nt_last_error()
+    lib.nt_norm_workspace_size.restype = ctypes.c_size_t
+    assert lib.nt_norm_workspace_size(0, 8) == 0
+    assert lib.nt_norm_workspace_size(3, 8) == 3 * 8 * 2 * 4
+
+
 STRUCTS = {
     "nt_segment": (N.Segment, ["grad", "offset", "count", "chunk_begin", "group", "step_slot"]),
     "nt_adamw_group": (N.AdamWGroup, [f for f, _ in N.AdamWGroup._fields_]),

@@ -225,3 +225,17 @@ def test_forward_only_writes_no_gradient(cuda_device, shift):
     assert loss.grad_fn is None
     ref_loss, _ = oxent.cross_entropy(x32, t, with_grad=False)
     assert abs(float(loss.item()) - float(ref_loss)) <= 1e-5 * abs(float(ref_loss))
+
+
+def test_rows_wider_than_the_shared_memory_buffer(cuda_device):
+    """150000 bf16 classes (300 KB rows) exceed one CTA's shared memory: the passes read
+    global memory instead of a staged row."""
+    rng = np.random.default_rng(21)
+    rows, classes = 24, 150_000
+    x32 = round_to_bf16(rng.normal(0, 2, (rows, classes)).astype(np.float32))
+    t = rng.integers(0, classes, rows)
+    t[5] = -100
+    loss, dl = softmax_cross_entropy(torch.from_numpy(x32).cuda().to(torch.bfloat16), torch.from_numpy(t).cuda())
+    ref_loss, ref_dl = oxent.cross_entropy(x32, t)
+    assert abs(float(loss.item()) - float(ref_loss)) <= 1e-5 * abs(float(ref_loss))
+    assert_bf16_close(dl, ref_dl)
