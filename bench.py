@@ -14,7 +14,11 @@ sharded: bf16 gradients are reduce-scattered, each rank updates its 1/N shard an
 model copy is all-gathered (NCCL over NVLink); ``value`` is whole-model params/s.
 
 ``--workload xent`` times the fused softmax cross-entropy forward + backward on
-configuration 4 ([8192, 50257] bf16 logits).
+configuration 4 ([8192, 50257] bf16 logits). ``124m`` and ``small`` run the AMP step on
+configurations 2 and 0/1; the step line also reports ``captured`` (the same tail replayed
+from one CUDA graph). The kernel seams of the reference's CUDA backend have their own
+workloads: ``softmax`` (causal attention softmax, GPT-2 small scores), ``norm`` (layer norm
+on 1.3B activations) and ``activation`` (bias + gelu on 1.3B MLP activations).
 
 ``--impl reference`` times the reference algorithm on the host CPU (the NumPy oracle port,
 all host threads) on a bounded sample of the same workload.
