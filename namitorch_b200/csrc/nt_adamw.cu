@@ -395,6 +395,7 @@ extern "C" {
 int nt_adamw_f32(float* param, const float* grad, float* exp_avg, float* exp_avg_sq,
                  const float coefficients[10], int maximize, int update_parameter,
                  uint64_t count, void* stream) {
+  nt::TraceRange trace("nt_adamw_f32");
   if (!coefficients) { set_error("nt_adamw_f32: coefficients is NULL"); return NT_EINVAL; }
   for (int i = 0; i < 10; ++i) {
     if (!isfinite(coefficients[i])) {
@@ -429,6 +430,7 @@ int nt_adamw_f32(float* param, const float* grad, float* exp_avg, float* exp_avg
 size_t nt_adamw_workspace_size(void) { return sizeof(AdamwWorkspace); }
 
 int nt_adamw_mt(const nt_adamw_mt_args* args, void* stream) {
+  nt::TraceRange trace("nt_adamw_mt");
   MtParams P;
   const int rc = build_mt_params(args, P);
   if (rc != NT_OK || P.nchunks == 0) return rc;
@@ -436,6 +438,7 @@ int nt_adamw_mt(const nt_adamw_mt_args* args, void* stream) {
 }
 
 int nt_adamw_mt_push(const nt_adamw_mt_args* args, void* const* peer_copies, int32_t num_peers, void* stream) {
+  nt::TraceRange trace("nt_adamw_mt_push");
   MtParams P;
   const int rc = build_mt_params(args, P);
   if (rc != NT_OK || P.nchunks == 0) return rc;

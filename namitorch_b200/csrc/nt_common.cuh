@@ -8,8 +8,18 @@
 #include <stdint.h>
 
 #include "namitorch_b200.h"
+#include <nvtx3/nvToolsExt.h>
 
 namespace nt {
+
+// An NVTX range around one entry point, named after it: each call shows up as a range in
+// Nsight Systems / Compute timelines. Header-only NVTX; a no-op unless a tool is attached.
+struct TraceRange {
+  explicit TraceRange(const char* name) { nvtxRangePushA(name); }
+  ~TraceRange() { nvtxRangePop(); }
+  TraceRange(const TraceRange&) = delete;
+  TraceRange& operator=(const TraceRange&) = delete;
+};
 
 // ---- host-side error plumbing (nt_runtime.cu) ----------------------------------------
 void set_error(const char* fmt, ...);

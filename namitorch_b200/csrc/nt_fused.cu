@@ -289,6 +289,7 @@ static int fused_operands(int op) {
 using namespace nt;
 
 extern "C" int nt_fused_elementwise(const nt_fused_args* args, void* stream) {
+  nt::TraceRange trace("nt_fused_elementwise");
   if (!args) { set_error("nt_fused_elementwise: args is NULL"); return NT_EINVAL; }
   const nt_fused_args& a = *args;
   const int need = fused_operands(a.op);

@@ -352,6 +352,7 @@ size_t nt_norm_workspace_size(int64_t rows, int64_t width) {
 }
 
 int nt_norm_forward(const nt_norm_args* args, void* stream) {
+  nt::TraceRange trace("nt_norm_forward");
   if (!args) { set_error("nt_norm_forward: args is NULL"); return NT_EINVAL; }
   const nt_norm_args& a = *args;
   int rc = check_norm(a, "nt_norm_forward");
@@ -367,6 +368,7 @@ int nt_norm_forward(const nt_norm_args* args, void* stream) {
 }
 
 int nt_norm_backward(const nt_norm_args* args, void* stream) {
+  nt::TraceRange trace("nt_norm_backward");
   if (!args) { set_error("nt_norm_backward: args is NULL"); return NT_EINVAL; }
   const nt_norm_args& a = *args;
   int rc = check_norm(a, "nt_norm_backward");

@@ -158,6 +158,7 @@ int nt_stream_synchronize(void* stream) {
 }
 
 int nt_cast(void* dst, int dst_dtype, const void* src, int src_dtype, int64_t count, void* stream) {
+  nt::TraceRange trace("nt_cast");
   if (count < 0) { set_error("nt_cast: negative count"); return NT_EINVAL; }
   if (count == 0) return NT_OK;
   if (!dst || !src) { set_error("nt_cast: NULL pointer"); return NT_EINVAL; }

@@ -342,6 +342,7 @@ using namespace nt;
 extern "C" {
 
 int nt_row_softmax(const nt_softmax_args* args, void* stream) {
+  nt::TraceRange trace("nt_row_softmax");
   if (!args) { set_error("nt_row_softmax: args is NULL"); return NT_EINVAL; }
   const nt_softmax_args& a = *args;
   if (a.op < NT_SOFTMAX || a.op > NT_CAUSAL_SOFTMAX_BACKWARD) {

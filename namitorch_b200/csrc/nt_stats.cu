@@ -374,6 +374,7 @@ extern "C" {
 size_t nt_grad_stats_workspace_size(void) { return sizeof(StatsWorkspace); }
 
 int nt_grad_stats(const nt_grad_stats_args* args, void* stream) {
+  nt::TraceRange trace("nt_grad_stats");
   if (!args) { set_error("nt_grad_stats: args is NULL"); return NT_EINVAL; }
   const nt_grad_stats_args& a = *args;
   int rc = check_spans(a.spans, a.num_spans, a.chunk_elems, a.num_chunks, a.dtype, "nt_grad_stats");
@@ -397,6 +398,7 @@ int nt_grad_stats(const nt_grad_stats_args* args, void* stream) {
 }
 
 int nt_schedule_step(int32_t* lr_step, const double* const* found_inf, int32_t count, void* stream) {
+  nt::TraceRange trace("nt_schedule_step");
   if (!lr_step) { set_error("nt_schedule_step: lr_step is NULL"); return NT_EINVAL; }
   if (count < 0 || count > NT_MAX_FOUND_INF || (count > 0 && !found_inf)) {
     set_error("nt_schedule_step: count must be in [0, %d] with a pointer array", NT_MAX_FOUND_INF);
@@ -414,6 +416,7 @@ int nt_schedule_step(int32_t* lr_step, const double* const* found_inf, int32_t c
 }
 
 int nt_grad_stats_finalize(nt_stats* stats, double norm_type, void* stream) {
+  nt::TraceRange trace("nt_grad_stats_finalize");
   if (!stats) { set_error("nt_grad_stats_finalize: stats is NULL"); return NT_EINVAL; }
   if (!(norm_type > 0.0)) { set_error("nt_grad_stats_finalize: norm_type must be positive"); return NT_EINVAL; }
   stats_finalize_kernel<<<1, 32, 0, as_stream(stream)>>>(stats, norm_type);
@@ -432,6 +435,7 @@ static int transform_common(TransformParams& P, int32_t dtype, cudaStream_t s) {
 int nt_grad_transform(const nt_span* spans, int32_t num_spans, int32_t chunk_elems, int64_t num_chunks,
                       int32_t dtype, const float* scale, const nt_stats* stats, int32_t clip,
                       double max_norm, void* stream) {
+  nt::TraceRange trace("nt_grad_transform");
   int rc = check_spans(spans, num_spans, chunk_elems, num_chunks, dtype, "nt_grad_transform");
   if (rc) return rc;
   if (clip && !stats) { set_error("nt_grad_transform: clip needs stats"); return NT_EINVAL; }
@@ -443,6 +447,7 @@ int nt_grad_transform(const nt_span* spans, int32_t num_spans, int32_t chunk_ele
 
 int nt_grad_clip_value(const nt_span* spans, int32_t num_spans, int32_t chunk_elems, int64_t num_chunks,
                        int32_t dtype, double clip_value, void* stream) {
+  nt::TraceRange trace("nt_grad_clip_value");
   int rc = check_spans(spans, num_spans, chunk_elems, num_chunks, dtype, "nt_grad_clip_value");
   if (rc) return rc;
   if (!(clip_value >= 0.0) || !isfinite(clip_value)) {
@@ -457,6 +462,7 @@ int nt_grad_clip_value(const nt_span* spans, int32_t num_spans, int32_t chunk_el
 
 int nt_scaler_update(float* scale, int32_t* growth_tracker, const double* const* found_inf, int32_t count,
                      double growth_factor, double backoff_factor, int32_t growth_interval, void* stream) {
+  nt::TraceRange trace("nt_scaler_update");
   if (!scale || !growth_tracker) { set_error("nt_scaler_update: NULL scale / tracker"); return NT_EINVAL; }
   if (count < 1 || count > NT_MAX_FOUND_INF || !found_inf) {
     set_error("nt_scaler_update: count must be in [1, %d]", NT_MAX_FOUND_INF);
@@ -539,6 +545,7 @@ size_t nt_grad_stats_noalloc_scratch_bytes(void) { return sizeof(nt::NoAllocScra
 
 int nt_grad_stats_noalloc(const nt_span* spans, int32_t num_spans, int32_t dtype, const float* scale,
                           double norm_type, nt_stats* stats, void* stream) {
+  nt::TraceRange trace("nt_grad_stats_noalloc");
   using namespace nt;
   if (num_spans < 0) { set_error("nt_grad_stats_noalloc: negative span count"); return NT_EINVAL; }
   if (num_spans > NT_NOALLOC_MAX_SPANS) {

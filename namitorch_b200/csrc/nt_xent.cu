@@ -586,6 +586,7 @@ extern "C" {
 size_t nt_xent_workspace_size(void) { return sizeof(XentWorkspace); }
 
 int nt_softmax_xent(const nt_xent_args* args, void* stream) {
+  nt::TraceRange trace("nt_softmax_xent");
   if (!args) { set_error("nt_softmax_xent: args is NULL"); return NT_EINVAL; }
   const nt_xent_args& a = *args;
   if (a.rows < 0) { set_error("nt_softmax_xent: negative row count"); return NT_EINVAL; }
@@ -635,6 +636,7 @@ int nt_softmax_xent(const nt_xent_args* args, void* stream) {
 
 int nt_xent_backward_scale(void* dlogits, int32_t dtype, int64_t rows, int64_t classes, const float* grad_output,
                            int32_t per_row, void* stream) {
+  nt::TraceRange trace("nt_xent_backward_scale");
   if (rows < 0 || classes < 0) { set_error("nt_xent_backward_scale: negative sizes"); return NT_EINVAL; }
   if (rows == 0 || classes == 0) return NT_OK;
   if (!dlogits || !grad_output) { set_error("nt_xent_backward_scale: NULL pointer"); return NT_EINVAL; }

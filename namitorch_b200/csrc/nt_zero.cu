@@ -229,6 +229,7 @@ int nt_can_access_peer(int32_t peer, int32_t* ok) {
 }
 
 int nt_zero_reduce_scatter_stats(const nt_zero_reduce_args* args, void* stream) {
+  nt::TraceRange trace("nt_zero_reduce_scatter_stats");
   if (!args) { set_error("nt_zero_reduce_scatter_stats: args is NULL"); return NT_EINVAL; }
   const nt_zero_reduce_args& a = *args;
   if (a.num_ranks < 1 || a.num_ranks > NT_MAX_RANKS) {
