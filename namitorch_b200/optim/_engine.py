@@ -114,7 +114,10 @@ class FusedAdamEngine:
         self.loaded: set[int] = set()
         self.max_step = 0
         self.corrections = CorrectionTable(device)
-        self._segments_key = None
+        # Device segment tables by (gradient address, offset, count, group, index) rows: a few
+        # are kept, so gradients that alternate between buffers (double-buffered host
+        # copies) find their table without a new upload.
+        self._segment_tables: dict[tuple, tuple[torch.Tensor, int, int]] = {}
         self._segments = None
         self._num_segments = 0
         self._num_chunks = 0
@@ -193,12 +196,13 @@ class FusedAdamEngine:
                     contiguous = False
                 rows.append((g.data_ptr(), self.layout.offsets[i], p.numel(), local[gi], i))
             key = tuple(rows)
-            if key != self._segments_key:
+            hit = self._segment_tables.get(key)
+            if hit is None:
                 table, nchunks = segment_table(rows, CHUNK)
-                self._segments = upload(table, self.device)
-                self._segments_key = key
-                self._num_segments = len(rows)
-                self._num_chunks = nchunks
+                if len(self._segment_tables) >= 4:
+                    self._segment_tables.clear()
+                hit = self._segment_tables[key] = (upload(table, self.device), len(rows), nchunks)
+            self._segments, self._num_segments, self._num_chunks = hit
             # Non-contiguous gradients are copied every step: nothing to reuse then.
             self._rows_cache = (fast_key, entries) if contiguous else None
         group_array = (N.AdamWGroup * len(structs))(*structs)
@@ -261,4 +265,4 @@ class FusedAdamEngine:
                 self.loaded.add(i)
             self.steps.copy_(torch.tensor(steps, dtype=torch.int32))
         self.max_step = max(steps) if steps else 0
-        self._segments_key = None
+        self._segment_tables.clear()
