@@ -688,7 +688,11 @@ def run_softmax(args):
     elems, es = x.numel(), x.element_size()
     peak, kind = measured_peak()
     rows = heads * t
-    achieved = 5 * es * elems / ((fwd + bwd) / 1e3) / 1e9
+    # The causal forward reads only the allowed scores (t (t + 1) / 2 of a head's t^2; the
+    # masked part is never used) and writes every output; the backward reads y and g whole.
+    allowed = heads * t * (t + 1) // 2
+    fwd_bytes, bwd_bytes = es * (allowed + elems), 3 * es * elems
+    achieved = (fwd_bytes + bwd_bytes) / ((fwd + bwd) / 1e3) / 1e9
     result = {"metric": "causal attention softmax fwd+bwd rows/s", "value": rows / ((fwd + bwd) / 1e3),
               "unit": "rows/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": fwd + bwd,
               "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": args.softmax_dtype,
@@ -698,9 +702,9 @@ def run_softmax(args):
               "kernels_ms": {"forward": fwd, "backward": bwd},
               "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                            "peak_source": kind,
-                           "algorithmic_bytes": {"forward": 2 * es * elems, "backward": 3 * es * elems},
-                           "forward_gbs": 2 * es * elems / (fwd / 1e3) / 1e9,
-                           "backward_gbs": 3 * es * elems / (bwd / 1e3) / 1e9,
+                           "algorithmic_bytes": {"forward": fwd_bytes, "backward": bwd_bytes},
+                           "forward_gbs": fwd_bytes / (fwd / 1e3) / 1e9,
+                           "backward_gbs": bwd_bytes / (bwd / 1e3) / 1e9,
                            "traffic": pair_traffic("row_softmax", f"softmax_{args.softmax_dtype}")},
               "gpu_launches": N.launch_count - launches0}
     if not args.no_cpu_baseline:

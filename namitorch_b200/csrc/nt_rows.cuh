@@ -78,6 +78,26 @@ __device__ __forceinline__ void load_row(const void* base, int width, int t, boo
   }
 }
 
+// load_row on the vector path for the forward of a row whose columns past `last` are masked
+// out: a vector that starts past `last` is never read and enters as -inf (the masked part of
+// a causal row is not part of the result, whatever it holds).
+template <int DT, int NPL, int WARPS>
+__device__ __forceinline__ void load_row_upto(const void* base, int last, int t, float (&v)[NPL]) {
+  constexpr int ES = DT == NT_F32 ? 4 : 2;
+  constexpr int EPV = 16 / ES;
+  constexpr int T = 32 * WARPS;
+#pragma unroll
+  for (int c = 0; c < NPL / EPV; ++c) {
+    const int k = c * T + t;
+    if (k * EPV <= last) {
+      unpack16<DT>(__ldcs(static_cast<const uint4*>(base) + k), v + c * EPV);
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) v[c * EPV + e] = -INFINITY;
+    }
+  }
+}
+
 // The EPV values of slot group c (slots c * EPV .. c * EPV + EPV - 1) of a row shared by every
 // row of the tensor (a weight or a bias), cached; 0 past the width. One group at a time keeps
 // only EPV of those values in registers.

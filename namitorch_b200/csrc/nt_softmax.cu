@@ -184,7 +184,12 @@ __global__ void __launch_bounds__(kSoftmaxThreads) row_softmax_kernel(const __gr
     const char* xrow = static_cast<const char*>(P.x) + base * ES;
     char* yrow = static_cast<char*>(P.y) + base * ES;
     float v[NPL];
-    if (live) load_row<DT, NPL, WARPS>(xrow, width, t, vec, v);
+    // Forward over whole vectors without a mask tensor: the vectors past the last allowed
+    // column (half of a causal row on average) are neither read nor exponentiated.
+    constexpr bool kUpto = !BACKWARD && VEC;
+    const bool upto = kUpto && mrow == nullptr;
+    if (live && upto) load_row_upto<DT, NPL, WARPS>(xrow, last, t, v);
+    else if (live) load_row<DT, NPL, WARPS>(xrow, width, t, vec, v);
     else {
 #pragma unroll
       for (int q = 0; q < NPL; ++q) v[q] = 0.0f;
@@ -262,10 +267,21 @@ __global__ void __launch_bounds__(kSoftmaxThreads) row_softmax_kernel(const __gr
         const float ml = m * kLog2e;
         float s2 = 0.0f;   // two partial sums: independent additions
 #pragma unroll
-        for (int q = 0; q < NPL; ++q) {
-          v[q] = ex2(fmaf(v[q], kLog2e, -ml));
-          if (q & 1) s2 += v[q];
-          else s += v[q];
+        for (int c = 0; c < NPL / EPV; ++c) {
+          // A vector that starts past `last` holds only -inf: its exponentials are 0 and add
+          // nothing (s + 0 is s), so it is skipped.
+          if (upto && (c * T + t) * EPV > last) {
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) v[c * EPV + e] = 0.0f;
+            continue;
+          }
+#pragma unroll
+          for (int e = 0; e < EPV; ++e) {
+            const int q = c * EPV + e;
+            v[q] = ex2(fmaf(v[q], kLog2e, -ml));
+            if (q & 1) s2 += v[q];
+            else s += v[q];
+          }
         }
         s += s2;
       } else {

@@ -131,3 +131,23 @@ def test_attention_sized_causal_rows_are_distributions(cuda_device):
     assert torch.allclose(sums, torch.ones_like(sums), atol=2e-2)
     upper = torch.triu(torch.ones(1024, 1024, dtype=torch.bool, device="cuda"), diagonal=1)
     assert not torch.any(y[:, upper])
+
+
+@pytest.mark.parametrize("dt", list(TORCH))
+@pytest.mark.parametrize("width,offset", [(64, 0), (1024, 0), (1024, 37), (4096, 5)])
+def test_causal_forward_ignores_the_masked_part(cuda_device, dt, width, offset):
+    """The causal forward never uses scores past the diagonal (the reference's rule: a
+    disallowed column enters as -inf). NaN and +inf planted there leave every row as the
+    oracle computes it; vectors wholly past the diagonal are not read at all."""
+    rng = np.random.default_rng(width + offset)
+    queries = 24
+    x = _store(rng.normal(0, 3, (2, queries, width)).astype(np.float32), dt)
+    for q in range(queries):
+        lo = offset + q + 1
+        if lo < width:
+            x[:, q, lo:] = np.where(rng.random((2, width - lo)) < 0.5, np.nan, np.inf)
+    xt = torch.from_numpy(x).cuda().to(TORCH[dt])
+    y = _run("causal_softmax", xt, None, query_position_offset=offset)
+    want, _ = S.forward(x, causal=True, offset=offset)
+    assert not np.isnan(want).any()
+    _check(y, want, dt)
