@@ -494,7 +494,7 @@ typedef struct nt_xent_args {
   void* dlogits;             /* [rows, classes] same dtype, or NULL for forward only */
   float* loss;               /* [rows] for NONE, [1] otherwise */
   float* row_loss;           /* scratch [rows] (may alias loss for NONE) */
-  nt_xent_info* info;        /* device */
+  nt_xent_info* info;        /* device; the call resets it before use */
   void* workspace;           /* nt_xent_workspace_size() bytes, zero-filled once */
   size_t workspace_bytes;
 } nt_xent_args;

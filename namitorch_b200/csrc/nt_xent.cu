@@ -23,7 +23,9 @@
 // passes, not the copies, bound the kernel: about 17 instructions per logit). The gradient
 // is written with 16-byte streaming stores at the same alignment offset. HBM traffic is one
 // read of the logits and one write of dlogits. Tensors that do not start on a 16-byte
-// boundary take the same three passes over global memory instead.
+// boundary take the same three passes over global memory instead. Without class weights
+// each CTA counts the valid targets (the mean's denominator) itself while its first row is
+// in flight; with weights a one-block prepare kernel sums the weights first.
 #include <cmath>
 
 #include "nt_bulk.cuh"
@@ -53,6 +55,7 @@ struct XentParams {
   XentWorkspace* ws;
   uintptr_t tensor_end;   // one past the last byte of the logits
   int staged;
+  int self_count;         // the main kernel counts the targets (no prepare launch)
   int64_t chunk;          // bytes per staged chunk (a multiple of 128)
 };
 
@@ -223,10 +226,6 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
   const int V = (int)P.classes;
   const nt_xent_info* info = P.info;
   const bool mean = P.reduction == NT_REDUCTION_MEAN;
-  const double D = mean ? info->denominator : 1.0;
-  const bool zero_all = mean && D == 0.0;
-  const double W = info->weight_sum;
-  const float inv_den = zero_all ? 0.0f : (float)(1.0 / D);
   const float e = P.smoothing;
   const bool smooth = e != 0.0f;
   const int cvec = (int)(P.chunk >> 4);   // vectors per chunk
@@ -248,6 +247,36 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
       for (int c = 0; c < NCH; ++c) stage_chunk<ES>(P, blockIdx.x, smem, &bars[c], c, lane);
     }
   }
+
+  // The mean's denominator. Without class weights every CTA counts the targets itself while
+  // its first row's copy is in flight (the same counts as xent_prepare_kernel, which then is
+  // not launched), and CTA 0 records them; with weights the prepare kernel has.
+  double D = 1.0, W;
+  if (!WEIGHTED && P.self_count) {
+    double valid = 0.0, bad = 0.0;
+    for (int64_t i = threadIdx.x; i < P.rows; i += THREADS) {
+      const int64_t t = P.targets[i];
+      if (t == P.ignore) continue;
+      if (t < 0 || t >= V) bad += 1.0;
+      else valid += 1.0;
+    }
+    valid = block_reduce(valid, red_d, SumOp(), 0.0);
+    bad = block_reduce(bad, red_d, SumOp(), 0.0);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      nt_xent_info* out = P.info;
+      out->n_valid = valid;
+      out->bad_targets = bad;
+      out->denominator = valid;
+      out->weight_sum = (double)V;
+    }
+    if (mean) D = valid;
+    W = (double)V;
+  } else {
+    if (mean) D = info->denominator;
+    W = info->weight_sum;
+  }
+  const bool zero_all = mean && D == 0.0;
+  const float inv_den = zero_all ? 0.0f : (float)(1.0 / D);
 
   uint32_t parity = 0;
   // The target of the CTA's next row is loaded one row ahead.
@@ -624,9 +653,18 @@ int nt_softmax_xent(const nt_xent_args* args, void* stream) {
   P.tensor_end = reinterpret_cast<uintptr_t>(a.logits) + (uintptr_t)(a.rows * a.classes * es);
   P.staged = aligned16(a.logits) && (a.dlogits == nullptr || aligned16(a.dlogits));
   cudaStream_t s = as_stream(stream);
-  xent_prepare_kernel<<<1, kPrepThreads, 0, s>>>(P);
-  int rc = launch_status("nt_softmax_xent prepare launch");
-  if (rc || a.rows == 0) return rc;
+  // Without class weights the main kernel counts the targets itself; the one-block prepare
+  // kernel runs for weighted losses and for zero rows (where it writes the zero loss).
+  P.self_count = a.class_weight == nullptr && a.rows > 0;
+  if (P.self_count) {
+    // The record starts from zero (loss_sum stays 0 for reduction NONE; error accumulates).
+    const cudaError_t err = cudaMemsetAsync(a.info, 0, sizeof(nt_xent_info), s);
+    if (err != cudaSuccess) return cuda_fail(err, "nt_softmax_xent: clearing the info record");
+  } else {
+    xent_prepare_kernel<<<1, kPrepThreads, 0, s>>>(P);
+    const int rc = launch_status("nt_softmax_xent prepare launch");
+    if (rc || a.rows == 0) return rc;
+  }
   switch (a.dtype) {
     case NT_F32: return launch_xent_dt<NT_F32>(P, s);
     case NT_F16: return launch_xent_dt<NT_F16>(P, s);

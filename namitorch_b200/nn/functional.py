@@ -76,7 +76,7 @@ def _launch(logits, targets, weight, ignore_index, reduction, smoothing, want_gr
         row_loss = loss if reduction == N.NT_REDUCTION_NONE else torch.empty(max(rows, 1), dtype=torch.float32,
                                                                              device=device)
         dlogits = torch.empty_like(logits) if want_grad else None
-        info = torch.zeros(len(N.XENT_INFO_FIELDS), dtype=torch.float64, device=device)
+        info = torch.empty(len(N.XENT_INFO_FIELDS), dtype=torch.float64, device=device)   # reset by the call
         ws = xent_workspace(device)
         args = N.XentArgs(
             logits=logits.data_ptr() if rows else None, dtype=N.dtype_code(logits.dtype), rows=rows, classes=classes,
@@ -85,7 +85,10 @@ def _launch(logits, targets, weight, ignore_index, reduction, smoothing, want_gr
             reduction=reduction, dlogits=None if dlogits is None or rows == 0 else dlogits.data_ptr(),
             loss=loss.data_ptr(), row_loss=row_loss.data_ptr(), info=info.data_ptr(), workspace=ws.data_ptr(),
             workspace_bytes=ws.numel())
-        N.call("nt_softmax_xent", N.C.byref(args), N.stream_handle())
+        # One kernel (with a memset of the info record) without class weights; the one-block
+        # prepare kernel first with them, or alone for zero rows.
+        N.call("nt_softmax_xent", N.C.byref(args), N.stream_handle(),
+               launches=(1 if rows else 0) + (0 if weight is None and rows else 1))
     return loss, dlogits, info
 
 
