@@ -57,6 +57,7 @@ def parse_args(argv=None):
     ap.add_argument("--workload", choices=["1p3b", "124m", "small", "xent", "softmax", "norm", "activation"],
                     default="1p3b")
     ap.add_argument("--softmax-dtype", choices=["f32", "bf16"], default="f32")
+    ap.add_argument("--activation-dtype", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-sample", type=int, default=1 << 25, help="parameters in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -820,7 +821,8 @@ def cpu_activation_sample(rows: int, width: int, threads: int) -> dict:
 
 def run_activation(args):
     """bias + gelu(tanh) forward and backward (the fused-elementwise seam) on the 1.3B model's
-    MLP activations: 16 sequences x 2048 tokens x 8192 hidden, float32."""
+    MLP activations: 16 sequences x 2048 tokens x 8192 hidden, float32 or bfloat16
+    (--activation-dtype)."""
     import torch
     from namitorch_b200 import _native as N
     from namitorch_b200.backends import get_backend
@@ -829,9 +831,10 @@ def run_activation(args):
     rows, width = 16 * 2048, 4 * 2048
     gen = torch.Generator(device=device)
     gen.manual_seed(0)
-    x = torch.randn(rows, width, device=device, generator=gen)
-    g = torch.randn(rows, width, device=device, generator=gen)
-    b = torch.randn(width, device=device, generator=gen).mul_(0.1)
+    dtype = {"f32": torch.float32, "bf16": torch.bfloat16}[args.activation_dtype]
+    x = torch.randn(rows, width, device=device, generator=gen).to(dtype)
+    g = torch.randn(rows, width, device=device, generator=gen).to(dtype)
+    b = torch.randn(width, device=device, generator=gen).mul_(0.1).to(dtype)
     k = get_backend(x).fused
     for _ in range(args.warmup):
         k.run("bias_gelu_tanh", (x, b))
@@ -848,21 +851,23 @@ def run_activation(args):
     ev[2].record()
     torch.cuda.synchronize()
     fwd, bwd = ev[0].elapsed_time(ev[1]) / args.steps, ev[1].elapsed_time(ev[2]) / args.steps
-    elems = x.numel()
+    elems, es = x.numel(), x.element_size()
     peak, kind = measured_peak()
-    achieved = (8 + 12) * elems / ((fwd + bwd) / 1e3) / 1e9
+    # forward R x + W y, backward R x, g + W dx per element (the bias row stays in cache)
+    fwd_bytes, bwd_bytes = 2 * es * elems, 3 * es * elems
+    achieved = (fwd_bytes + bwd_bytes) / ((fwd + bwd) / 1e3) / 1e9
     result = {"metric": "bias+gelu(tanh) fwd+bwd rows/s", "value": rows / ((fwd + bwd) / 1e3), "unit": "rows/s",
               "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": fwd + bwd,
-              "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+              "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": args.activation_dtype,
               "data": "synthetic",
               "config": {"workload": f"MLP activations [{rows}, {width}] (1.3B model, 16 x 2048 tokens), bias [{width}]",
-                         "l2": f"inputs larger than L2 ({elems * 4 / 1e6:.0f} MB per tensor)"},
+                         "l2": f"inputs larger than L2 ({elems * es / 1e6:.0f} MB per tensor)"},
               "kernels_ms": {"forward": fwd, "backward": bwd},
               "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                            "peak_source": kind,
-                           "algorithmic_bytes": {"forward": 8 * elems, "backward": 12 * elems},
-                           "forward_gbs": 8 * elems / (fwd / 1e3) / 1e9, "backward_gbs": 12 * elems / (bwd / 1e3) / 1e9,
-                           "traffic": pair_traffic("fused_bias_gelu", "activation")},
+                           "algorithmic_bytes": {"forward": fwd_bytes, "backward": bwd_bytes},
+                           "forward_gbs": fwd_bytes / (fwd / 1e3) / 1e9, "backward_gbs": bwd_bytes / (bwd / 1e3) / 1e9,
+                           "traffic": pair_traffic("fused_bias_gelu", "activation") if es == 4 else None},
               "gpu_launches": N.launch_count - launches0}
     if not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_activation_sample(2048, width, os.cpu_count() or 1)

@@ -8,7 +8,7 @@
 // thread per iteration keep loads in flight. Bias rows are read through the read-only cache
 // (every row of the tensor reads them); the column of a thread's vector advances by the
 // grid stride modulo the width instead of a division per vector. Half and bfloat16 operands
-// are computed in float32 and rounded once.
+// are computed in float32 and rounded once, with the SFU's exp / reciprocal / divide (below).
 //
 // The arithmetic follows the reference's device helpers, with CUDA's expf:
 //   sigmoid(x) = 1 / (1 + e) for x >= 0, e / (1 + e) otherwise, e = exp(-|x|)
@@ -38,19 +38,33 @@ constexpr float kGeluScale = 0.7978845608028654f;   // sqrt(2 / pi)
 constexpr float kGeluCubic = 0.044715f;
 constexpr float kGeluCubic3 = 0.134145f;            // 3 * 0.044715
 
+// FAST (16-bit operands): the SFU's exp and reciprocal (`__expf`, `rcp.approx`,
+// `__fdividef`, each within a few float32 ulps) instead of the rounded `expf`, `__frcp_rn`
+// and IEEE division; the result is rounded to 8 or 11 significant bits on store, where the
+// difference almost never shows (the tests allow one unit of the stored type).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+template <bool FAST>
 __device__ __forceinline__ float sigmoid_of(float x) {
-  const float e = expf(-fabsf(x));
+  const float e = FAST ? __expf(-fabsf(x)) : expf(-fabsf(x));   // in [0, 1]
+  if constexpr (FAST) return x >= 0.0f ? rcp_approx(1.0f + e) : __fdividef(e, 1.0f + e);
   return x >= 0.0f ? 1.0f / (1.0f + e) : e / (1.0f + e);
 }
+template <bool FAST>
 __device__ __forceinline__ float silu_of(float x) {
-  return (isinf(x) && x < 0.0f) ? 0.0f : x * sigmoid_of(x);
+  return (isinf(x) && x < 0.0f) ? 0.0f : x * sigmoid_of<FAST>(x);
 }
+template <bool FAST>
 __device__ __forceinline__ float silu_grad(float x) {
-  const float s = sigmoid_of(x);
+  const float s = sigmoid_of<FAST>(x);
   return isfinite(x) ? s + x * (s * (1.0f - s)) : s;
 }
+template <bool FAST>
 __device__ __forceinline__ float sigmoid_grad(float x) {
-  const float s = sigmoid_of(x);
+  const float s = sigmoid_of<FAST>(x);
   return s * (1.0f - s);
 }
 // gelu with the tanh approximation through the identity 0.5 (1 + tanh(u)) = sigmoid(2u):
@@ -58,19 +72,22 @@ __device__ __forceinline__ float sigmoid_grad(float x) {
 // u = sqrt(2/pi) (x + 0.044715 x^3). One SFU exp2 and one reciprocal replace tanhf, with no
 // cancellation where tanh(u) is near -1; results agree with the tanh form to a few float32
 // ulps. 2^(-2u log2 e) overflows to +inf for very negative u, which gives s = 0.
+template <bool FAST>
 __device__ __forceinline__ float sigmoid_2u(float x) {
   const float u = kGeluScale * (x + kGeluCubic * x * x * x);
   float e;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(u * -2.8853900817779268f));   // -2 log2(e) u
-  return __frcp_rn(1.0f + e);
+  return FAST ? rcp_approx(1.0f + e) : __frcp_rn(1.0f + e);
 }
+template <bool FAST>
 __device__ __forceinline__ float gelu_of(float x) {
   if (fabsf(x) > 20.0f) return x > 0.0f ? x : -0.0f;
-  return x * sigmoid_2u(x);
+  return x * sigmoid_2u<FAST>(x);
 }
+template <bool FAST>
 __device__ __forceinline__ float gelu_grad(float x) {
   if (fabsf(x) > 20.0f) return x > 0.0f ? 1.0f : 0.0f;
-  const float s = sigmoid_2u(x);
+  const float s = sigmoid_2u<FAST>(x);
   const float inner = kGeluScale * (1.0f + kGeluCubic3 * x * x);
   return s + 2.0f * x * (s * (1.0f - s)) * inner;
 }
@@ -89,27 +106,27 @@ template <int OP> struct FusedOp {
 };
 
 // One element. `lo` / `hi` are the clamp bounds (has_lo / has_hi: present).
-template <int OP>
+template <int OP, bool FAST>
 __device__ __forceinline__ float fused_value(float a, float b, float c, float d, float lo, float hi, bool has_lo,
                                              bool has_hi, float& second) {
   switch (OP) {
-    case NT_FUSED_SIGMOID: return sigmoid_of(a);
-    case NT_FUSED_SILU: return silu_of(a);
-    case NT_FUSED_GELU_TANH: return gelu_of(a);
+    case NT_FUSED_SIGMOID: return sigmoid_of<FAST>(a);
+    case NT_FUSED_SILU: return silu_of<FAST>(a);
+    case NT_FUSED_GELU_TANH: return gelu_of<FAST>(a);
     case NT_FUSED_SIGMOID_BACKWARD: return b * (a * (1.0f - a));
-    case NT_FUSED_SILU_BACKWARD: return b * silu_grad(a);
-    case NT_FUSED_GELU_TANH_BACKWARD: return b * gelu_grad(a);
-    case NT_FUSED_SWIGLU: return silu_of(a) * b;
+    case NT_FUSED_SILU_BACKWARD: return b * silu_grad<FAST>(a);
+    case NT_FUSED_GELU_TANH_BACKWARD: return b * gelu_grad<FAST>(a);
+    case NT_FUSED_SWIGLU: return silu_of<FAST>(a) * b;
     case NT_FUSED_SWIGLU_BACKWARD:
-      second = c * silu_of(a);
-      return (c * b) * silu_grad(a);
-    case NT_FUSED_BIAS_SIGMOID: return sigmoid_of(a + b);
-    case NT_FUSED_BIAS_SILU: return silu_of(a + b);
-    case NT_FUSED_BIAS_GELU_TANH: return gelu_of(a + b);
+      second = c * silu_of<FAST>(a);
+      return (c * b) * silu_grad<FAST>(a);
+    case NT_FUSED_BIAS_SIGMOID: return sigmoid_of<FAST>(a + b);
+    case NT_FUSED_BIAS_SILU: return silu_of<FAST>(a + b);
+    case NT_FUSED_BIAS_GELU_TANH: return gelu_of<FAST>(a + b);
     case NT_FUSED_BIAS_RELU: return relu_of(a + b);
-    case NT_FUSED_BIAS_SIGMOID_BACKWARD: return c * sigmoid_grad(a + b);
-    case NT_FUSED_BIAS_SILU_BACKWARD: return c * silu_grad(a + b);
-    case NT_FUSED_BIAS_GELU_TANH_BACKWARD: return c * gelu_grad(a + b);
+    case NT_FUSED_BIAS_SIGMOID_BACKWARD: return c * sigmoid_grad<FAST>(a + b);
+    case NT_FUSED_BIAS_SILU_BACKWARD: return c * silu_grad<FAST>(a + b);
+    case NT_FUSED_BIAS_GELU_TANH_BACKWARD: return c * gelu_grad<FAST>(a + b);
     case NT_FUSED_BIAS_RELU_BACKWARD: return c * relu_grad(a + b);
     case NT_FUSED_CLAMP: {
       const float l = has_lo ? lo : 0.0f, h = has_hi ? hi : 0.0f;
@@ -193,7 +210,7 @@ __global__ void __launch_bounds__(kFusedThreads) fused_kernel(const __grid_const
 #pragma unroll
     for (int e = 0; e < EPV; ++e) {
       float s = 0.0f;
-      out[e] = fused_value<OP>(a[e], O::kReadB || O::kBias ? b[e] : 0.0f, O::kReadC ? c[e] : 0.0f,
+      out[e] = fused_value<OP, DT != NT_F32>(a[e], O::kReadB || O::kBias ? b[e] : 0.0f, O::kReadC ? c[e] : 0.0f,
                                O::kReadD ? d[e] : 0.0f, lo, hi, has_lo, has_hi, s);
       sec[e] = s;
     }
