@@ -3,7 +3,8 @@
 Cases (float32): plain softmax over the last dimension of [4, 7, 33] with some -inf scores;
 masked softmax of [2, 3, 5, 40] scores with a [5, 40] boolean mask broadcast over batch and
 heads (the reference's attention path: masked_fill(-inf) then softmax); causal softmax of
-[2, 5, 9] scores with query_position_offset 2. For each, the upstream gradient and the
+[2, 5, 9] scores with query_position_offset 2, and causal softmax of [2, 6, 40] scores whose
+blocked positions hold NaN and +inf. For each, the upstream gradient and the
 gradient the reference's autograd returns for the scores.
 
 Usage (needs the reference checkout; not run by the tests):
@@ -53,6 +54,15 @@ def main(reference: str) -> None:
     allowed = np.arange(9)[None, :] - min(offset, 9) <= np.arange(5)[:, None]
     out["causal_offset"] = np.array(offset)
     run("causal", x, np.broadcast_to(~allowed, x.shape).copy())
+
+    # The same causal rule with NaN and +inf planted in the blocked (future) positions: the
+    # reference fills them with -inf before the softmax, so they change nothing.
+    x = rng.normal(0, 2, (2, 6, 40)).astype(np.float32)
+    allowed = np.arange(40)[None, :] - min(offset, 40) <= np.arange(6)[:, None]
+    blocked = np.broadcast_to(~allowed, x.shape)
+    poison = np.where(rng.random(x.shape) < 0.5, np.float32(np.nan), np.float32(np.inf))
+    x = np.where(blocked, poison, x).astype(np.float32)
+    run("causal_poisoned", x, blocked.copy())
 
     np.savez(HERE / "softmax.npz", **out)
     print("wrote softmax.npz", sorted(out))

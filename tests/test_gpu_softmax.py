@@ -43,7 +43,9 @@ def _check(got, want, dt, rtol=1e-5, atol=1e-7):
         np.testing.assert_allclose(got, want, rtol=ulp, atol=atol)
 
 
-@pytest.mark.parametrize("name", ["plain", "masked", "causal"])
+# causal_poisoned: NaN and +inf in the blocked positions, which the reference ignores (the
+# forward never reads whole blocked vectors).
+@pytest.mark.parametrize("name", ["plain", "masked", "causal", "causal_poisoned"])
 def test_reference_golden_cases(cuda_device, name):
     x = torch.from_numpy(GOLDEN[f"{name}_x"]).cuda()
     g = torch.from_numpy(GOLDEN[f"{name}_g"]).cuda()

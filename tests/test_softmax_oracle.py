@@ -7,7 +7,9 @@ from oracle import softmax as S
 
 GOLDEN = np.load(REPO / "tests" / "golden" / "softmax.npz")
 CASES = {"plain": {}, "masked": {"mask": GOLDEN["masked_mask"]},
-         "causal": {"causal": True, "offset": int(GOLDEN["causal_offset"])}}
+         "causal": {"causal": True, "offset": int(GOLDEN["causal_offset"])},
+         # NaN / +inf in the blocked positions: the reference fills them with -inf first
+         "causal_poisoned": {"causal": True, "offset": int(GOLDEN["causal_offset"])}}
 
 
 @pytest.mark.parametrize("name", list(CASES))
