@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define NT_ABI_VERSION 6
+#define NT_ABI_VERSION 7
 #define NT_MAX_GROUPS 32      /* coefficient groups per nt_adamw_mt call */
 #define NT_MAX_FOUND_INF 16   /* optimizers combined by one nt_scaler_update call */
 
@@ -243,8 +243,10 @@ int nt_grad_stats(const nt_grad_stats_args* args, void* stream);
    NT_NOALLOC_MAX_SPANS {ptr, count} pairs; chunk_begin is ignored), the device loss scale
    (or NULL) and the device nt_stats output. More spans are rejected with NT_EINVAL.
    Same result as nt_grad_stats with finalize = 1 (two passes for a general p).
-   The first call on each device looks up the array's device address with that device
-   current; make that first call before any stream capture. All calls share the one array,
+   The first call in each CUDA context (normally once per device: the runtime's primary
+   context; again after cudaDeviceReset, or in a context the caller created with the driver
+   API) looks up the array's device address in that context and caches it under the
+   context's ID; make that first call before any stream capture. All calls share the one array,
    so calls that overlap on the GPU (different streams, different host threads) race;
    serialise them. Nothing here calls cudaMalloc, cudaFree or an allocating library. */
 #define NT_NOALLOC_MAX_SPANS 64
@@ -465,6 +467,14 @@ int nt_zero_reduce_scatter_stats(const nt_zero_reduce_args* args, void* stream);
    peer_copies[k] + offset (same dtype), which fuses the ZeRO-1 all-gather of the model
    copy into the update. `peer_copies` is a host array of device pointers. */
 int nt_adamw_mt_push(const nt_adamw_mt_args* args, void* const* peer_copies, int32_t num_peers, void* stream);
+
+/* No counterpart in the reference: copies `count` (1..NT_MAX_RANKS) independent ranges of
+   `bytes_each` bytes (a multiple of 16; 16-byte aligned pointers), src[k] -> dst[k], with
+   the plain 16-byte SM loads and stores that the two ZeRO-1 kernels above use (no copy
+   engine, no multicast). With src pointing at peers' memory (nt_ipc_open) it measures the
+   inbound peer bandwidth the reduce-scatter pull sees; with dst at peers, the outbound
+   bandwidth of the all-gather push. `src` and `dst` are host arrays of device pointers. */
+int nt_peer_copy(const void* const* src, void* const* dst, int32_t count, uint64_t bytes_each, void* stream);
 
 /* ------------------------------------------------------------------------------------ */
 /* Fused softmax cross-entropy forward + backward                                        */

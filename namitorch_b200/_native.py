@@ -22,7 +22,7 @@ NT_DECAY_NONE, NT_DECAY_DECOUPLED, NT_DECAY_COUPLED = 0, 1, 2
 NT_MAX_GROUPS = 32
 NT_MAX_FOUND_INF = 16
 NT_MAX_RANKS = 8
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 
 class Segment(C.Structure):
@@ -169,6 +169,7 @@ SIGNATURES: dict[str, tuple] = {
     "nt_can_access_peer": (C.c_int, [C.c_int32, C.POINTER(C.c_int32)]),
     "nt_zero_reduce_scatter_stats": (C.c_int, [C.POINTER(ZeroReduceArgs), C.c_void_p]),
     "nt_adamw_mt_push": (C.c_int, [C.POINTER(AdamWMtArgs), C.POINTER(C.c_void_p), C.c_int32, C.c_void_p]),
+    "nt_peer_copy": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int32, C.c_uint64, C.c_void_p]),
     "nt_row_softmax": (C.c_int, [C.POINTER(SoftmaxArgs), C.c_void_p]),
     "nt_norm_workspace_size": (C.c_size_t, [C.c_int64, C.c_int64]),
     "nt_norm_forward": (C.c_int, [C.POINTER(NormArgs), C.c_void_p]),
@@ -229,9 +230,8 @@ def check(status: int, what: str = "") -> None:
 
 # Kernel launches issued per successful call of each launching entry point (for the
 # benchmark's launch count; the statistics entry point launches one kernel per call).
-LAUNCHES_PER_CALL = {"nt_adamw_f32": 1, "nt_adamw_mt": 1, "nt_adamw_mt_push": 1, "nt_zero_reduce_scatter_stats": 1,
+LAUNCHES_PER_CALL = {"nt_adamw_f32": 1, "nt_adamw_mt": 1, "nt_adamw_mt_push": 1, "nt_zero_reduce_scatter_stats": 1, "nt_peer_copy": 1,
                      "nt_grad_stats": 1, "nt_grad_stats_finalize": 1, "nt_schedule_step": 1, "nt_row_softmax": 1, "nt_norm_forward": 1,
-                     "nt_grad_stats_noalloc": 2,
                      "nt_grad_transform": 1, "nt_grad_clip_value": 1, "nt_scaler_update": 1,
                      "nt_softmax_xent": 2, "nt_xent_backward_scale": 1, "nt_cast": 1, "nt_fused_elementwise": 1}
 launch_count = 0
@@ -279,6 +279,12 @@ def ipc_open(handle: bytes, offset: int) -> int:
 
 def ipc_close(ptr: int) -> None:
     call("nt_ipc_close", C.c_void_p(ptr))
+
+
+def peer_copy(src: list[int], dst: list[int], bytes_each: int, stream=None) -> None:
+    """src[k] -> dst[k] for every k, ``bytes_each`` bytes each, by 16-byte SM loads/stores."""
+    n = len(src)
+    call("nt_peer_copy", (C.c_void_p * n)(*src), (C.c_void_p * n)(*dst), n, int(bytes_each), stream_handle(stream))
 
 
 def can_access_peer(peer: int) -> bool:

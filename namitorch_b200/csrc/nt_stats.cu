@@ -1,5 +1,9 @@
 // Gradient statistics (found_inf + total norm), in-place gradient transforms
 // (unscale / clip-by-norm / clip-by-value) and the device-side dynamic loss-scale update.
+#include <cuda.h>
+
+#include <mutex>
+
 #include "nt_stats.cuh"
 
 namespace nt {
@@ -517,23 +521,90 @@ __global__ void noalloc_prepare_kernel(const __grid_constant__ NoAllocSpans S) {
   if (threadIdx.x == 0) scratch->ws.counter = 0u;
 }
 
-static void* g_noalloc_address[64] = {nullptr};
+// Device address of the scratch array in the CUDA context current on this thread.
+//
+// The host-side name of a __device__ array is only a stand-in for its device address,
+// and that address belongs to a context, not to a device: the primary context that
+// cudaDeviceReset destroyed, or a context the caller created with the driver API, each
+// load this library's module at their own address. So the address is looked up with
+// cudaGetSymbolAddress once per context and cached under the context's unique ID
+// (cuCtxGetId; a context handle can be reused by a later context, an ID is not). The
+// lookup is serialised by a mutex, so two host threads making the first call at once
+// are safe. When no context is current yet, the lookup itself creates the runtime's
+// primary context for the current device, and the cache entry is made after it.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
 
-// Device address of the scratch array on the current device. The host-side name of a
-// __device__ array is only a stand-in for its device address, so the address is looked
-// up once per device with that device current.
-static int noalloc_scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
-  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
-  if (dev < 0 || dev >= 64) { set_error("nt_grad_stats_noalloc: device index %d out of range", dev); return NT_EINVAL; }
-  if (g_noalloc_address[dev] == nullptr) {
-    void* ptr = nullptr;
-    err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(noalloc scratch)");
-    g_noalloc_address[dev] = ptr;
+struct NoAllocContextSlot {
+  unsigned long long context_id;
+  void* address;
+};
+
+constexpr int kNoAllocContextSlots = 64;
+static std::mutex g_noalloc_lock;
+static NoAllocContextSlot g_noalloc_slots[kNoAllocContextSlots];
+static int g_noalloc_slots_used = 0;
+static CtxGetCurrentFn g_ctx_get_current = nullptr;
+static CtxGetIdFn g_ctx_get_id = nullptr;
+
+// Called with g_noalloc_lock held.
+static int resolve_context_calls() {
+  if (g_ctx_get_current && g_ctx_get_id) return NT_OK;
+  void* current = nullptr;
+  void* id = nullptr;
+  cudaDriverEntryPointQueryResult q1 = cudaDriverEntryPointSymbolNotFound, q2 = cudaDriverEntryPointSymbolNotFound;
+  cudaError_t e1 = cudaGetDriverEntryPoint("cuCtxGetCurrent", &current, cudaEnableDefault, &q1);
+  cudaError_t e2 = cudaGetDriverEntryPoint("cuCtxGetId", &id, cudaEnableDefault, &q2);
+  if (e1 != cudaSuccess) return cuda_fail(e1, "cudaGetDriverEntryPoint(cuCtxGetCurrent)");
+  if (e2 != cudaSuccess) return cuda_fail(e2, "cudaGetDriverEntryPoint(cuCtxGetId)");
+  if (q1 != cudaDriverEntryPointSuccess || q2 != cudaDriverEntryPointSuccess || !current || !id) {
+    set_error("nt_grad_stats_noalloc: the driver does not provide cuCtxGetCurrent / cuCtxGetId");
+    return NT_ECUDA;
   }
-  *out = g_noalloc_address[dev];
+  g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(current);
+  g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(id);
+  return NT_OK;
+}
+
+// Called with g_noalloc_lock held. *id = 0 when no context is current.
+static int current_context_id(unsigned long long* id) {
+  *id = 0;
+  CUcontext ctx = nullptr;
+  CUresult r = g_ctx_get_current(&ctx);
+  if (r != CUDA_SUCCESS) { set_error("nt_grad_stats_noalloc: cuCtxGetCurrent failed (%d)", int(r)); return NT_ECUDA; }
+  if (!ctx) return NT_OK;
+  r = g_ctx_get_id(ctx, id);
+  if (r != CUDA_SUCCESS) { set_error("nt_grad_stats_noalloc: cuCtxGetId failed (%d)", int(r)); return NT_ECUDA; }
+  return NT_OK;
+}
+
+static int noalloc_scratch_address(void** out) {
+  std::lock_guard<std::mutex> guard(g_noalloc_lock);
+  int rc = resolve_context_calls();
+  if (rc) return rc;
+  unsigned long long id = 0;
+  rc = current_context_id(&id);
+  if (rc) return rc;
+  if (id != 0) {
+    for (int i = 0; i < g_noalloc_slots_used; ++i) {
+      if (g_noalloc_slots[i].context_id == id) { *out = g_noalloc_slots[i].address; return NT_OK; }
+    }
+  }
+  void* ptr = nullptr;
+  cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(noalloc scratch)");
+  if (id == 0) {   // the lookup above created the primary context: key the entry by it
+    rc = current_context_id(&id);
+    if (rc) return rc;
+  }
+  // A process that has used more contexts than the table holds still gets the right
+  // address; it is then looked up on every call instead of being cached.
+  if (id != 0 && g_noalloc_slots_used < kNoAllocContextSlots) {
+    g_noalloc_slots[g_noalloc_slots_used].context_id = id;
+    g_noalloc_slots[g_noalloc_slots_used].address = ptr;
+    ++g_noalloc_slots_used;
+  }
+  *out = ptr;
   return NT_OK;
 }
 

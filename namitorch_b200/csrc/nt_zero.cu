@@ -142,6 +142,42 @@ static int dispatch_ranks(const ZeroReduceParams& P, cudaStream_t s) {
   }
 }
 
+
+// Copies count independent ranges (src[k] -> dst[k], `vectors` 16-byte vectors each) with
+// plain 16-byte loads and stores from the SMs, the access pattern of the ZeRO-1 pull and
+// push: pointing src at peers measures the inbound link, dst at peers the outbound one.
+struct PeerCopyParams {
+  const uint4* src[NT_MAX_RANKS];
+  uint4* dst[NT_MAX_RANKS];
+  int count;
+  int64_t vectors;
+};
+
+constexpr int kPeerCopyThreads = 256;
+constexpr int kPeerCopyUnroll = 4;
+
+__global__ void __launch_bounds__(kPeerCopyThreads) peer_copy_kernel(const __grid_constant__ PeerCopyParams P) {
+  const int k = blockIdx.x % P.count;              // the blocks are dealt round robin to the ranges
+  const int64_t block = blockIdx.x / P.count;
+  const int64_t blocks = gridDim.x / P.count;
+  const uint4* src = P.src[k];
+  uint4* dst = P.dst[k];
+  const int64_t step = blocks * kPeerCopyThreads * kPeerCopyUnroll;
+  for (int64_t v0 = block * kPeerCopyThreads * kPeerCopyUnroll + threadIdx.x; v0 < P.vectors; v0 += step) {
+    uint4 r[kPeerCopyUnroll];
+#pragma unroll
+    for (int u = 0; u < kPeerCopyUnroll; ++u) {
+      const int64_t v = v0 + (int64_t)u * kPeerCopyThreads;
+      if (v < P.vectors) r[u] = __ldcs(src + v);
+    }
+#pragma unroll
+    for (int u = 0; u < kPeerCopyUnroll; ++u) {
+      const int64_t v = v0 + (int64_t)u * kPeerCopyThreads;
+      if (v < P.vectors) __stcs(dst + v, r[u]);
+    }
+  }
+}
+
 typedef CUresult (*GetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
 
 static GetAddressRangeFn address_range_fn() {
@@ -273,6 +309,35 @@ int nt_zero_reduce_scatter_stats(const nt_zero_reduce_args* args, void* stream) 
       set_error("nt_zero_reduce_scatter_stats: unsupported dtype %d", a.dtype);
       return NT_EUNSUPPORTED;
   }
+}
+
+int nt_peer_copy(const void* const* src, void* const* dst, int32_t count, uint64_t bytes_each, void* stream) {
+  nt::TraceRange trace("nt_peer_copy");
+  if (count < 1 || count > NT_MAX_RANKS) {
+    set_error("nt_peer_copy: count must be in [1, %d] (got %d)", NT_MAX_RANKS, count);
+    return NT_EINVAL;
+  }
+  if (!src || !dst) { set_error("nt_peer_copy: NULL pointer array"); return NT_EINVAL; }
+  if (bytes_each % 16 != 0) { set_error("nt_peer_copy: bytes_each must be a multiple of 16"); return NT_EINVAL; }
+  PeerCopyParams P;
+  for (int k = 0; k < NT_MAX_RANKS; ++k) { P.src[k] = nullptr; P.dst[k] = nullptr; }
+  for (int k = 0; k < count; ++k) {
+    if (bytes_each > 0 && (!src[k] || !dst[k] || !aligned16(src[k]) || !aligned16(dst[k]))) {
+      set_error("nt_peer_copy: range %d has a NULL or not 16-byte aligned pointer", k);
+      return NT_EINVAL;
+    }
+    P.src[k] = static_cast<const uint4*>(src[k]);
+    P.dst[k] = static_cast<uint4*>(dst[k]);
+  }
+  P.count = count;
+  P.vectors = (int64_t)(bytes_each / 16);
+  if (P.vectors == 0) return NT_OK;
+  int per = current_sm_count() * 4 / count;   // four 256-thread blocks per SM in all
+  if (per < 1) per = 1;
+  const int64_t want = (P.vectors + kPeerCopyThreads * kPeerCopyUnroll - 1) / (kPeerCopyThreads * kPeerCopyUnroll);
+  if (want < per) per = (int)want;
+  peer_copy_kernel<<<per * count, kPeerCopyThreads, 0, as_stream(stream)>>>(P);
+  return launch_status("nt_peer_copy launch");
 }
 
 }  // extern "C"
