@@ -59,11 +59,14 @@ def parse_args(argv=None):
     ap.add_argument("--softmax-dtype", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--activation-dtype", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--e2e-steps", type=int, default=5)
-    ap.add_argument("--cpu-sample", type=int, default=1 << 25, help="parameters in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--zero-transport", choices=["auto", "p2p", "nccl"], default="auto",
                     help="ZeRO-1 exchange at N>1: fused kernels over peer memory, or NCCL collectives")
+    ap.add_argument("--no-nccl-compare", action="store_true",
+                    help="at N>1 with the p2p transport, skip the NCCL-transport comparison run")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="at N=1, skip the cross-entropy and 124M figures added to the default line")
     return ap.parse_args(argv)
 
 
@@ -141,23 +144,112 @@ class ClockSampler:
 
 
 # ---- CPU baseline (reference algorithm on the host) ------------------------------------------
-def cpu_amp_sample(n: int, steps: int, threads: int) -> dict:
-    """The reference AMP step (unscale, finite check, two-pass norm, clip, AdamW) on a sample of
-    ``n`` parameters, split into per-thread chunks (NumPy ufuncs release the GIL)."""
-    from oracle import adamw as oadamw
-    from oracle.casts import round_to_bf16
+REFERENCE_INSTALL = REPO / "baseline" / "_ref"
+# The CPU sample of the 1.3B workload: layer 0's attention block at d_model 2048 (ln1 weight
+# and bias, qkv weight and bias, proj weight and bias), 16,789,504 parameters in two
+# parameter groups (decay on the matrices), the same for every CPU figure in a line.
+CPU_SAMPLE_SHAPES = [(2048,), (2048,), (2048, 6144), (6144,), (2048, 2048), (2048,)]
+CPU_SAMPLE_DECAY = (2, 4)
+CPU_SAMPLE_PARAMS = sum(int(np.prod(s)) for s in CPU_SAMPLE_SHAPES)
+CPU_SAMPLE_TEXT = (f"{CPU_SAMPLE_PARAMS} parameters (layer 0 attention block of the 1.3B set: ln1 w/b, qkv W/b, "
+                   "proj W/b; two groups, wd 0.1 on the matrices), bf16-valued grads x 65536")
+
+
+def host_info() -> dict:
+    """CPU model and the host threads this process may use."""
+    model = None
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    usable = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    return {"cpu_model": model, "cpu_count": os.cpu_count(), "usable_threads": usable}
+
+
+def _cpu_sample_arrays():
+    import torch
     rng = np.random.default_rng(0)
-    p = rng.normal(0, 0.02, n).astype(np.float32)
-    g0 = round_to_bf16((rng.normal(0, 1e-3, n) * 65536.0).astype(np.float32))
+    params = [rng.normal(0, 0.02, s).astype(np.float32) for s in CPU_SAMPLE_SHAPES]
+    grads = [torch.from_numpy((rng.normal(0, 1e-3, s) * 65536.0).astype(np.float32)).to(torch.bfloat16)
+             .to(torch.float32).numpy() for s in CPU_SAMPLE_SHAPES]   # bf16-valued, round to nearest even
+    return params, grads
+
+
+def load_reference_package():
+    """The reference installed under baseline/_ref (its own code, unmodified), or None."""
+    if not (REFERENCE_INSTALL / "namitorch" / "__init__.py").exists():
+        return None
+    if str(REFERENCE_INSTALL) not in sys.path:
+        sys.path.insert(0, str(REFERENCE_INSTALL))
+    import namitorch
+    from namitorch import amp, optim
+    from namitorch.nn import Parameter
+    return namitorch, optim, amp, Parameter
+
+
+def reference_amp_sample(steps: int, warmup: int = 1) -> dict | None:
+    """The reference's own AMP step, through its public API and stock NumPy path
+    (namitorch/amp.py:127-234, namitorch/optim/clip_grad.py:96-112, namitorch/optim/adam.py:28-42):
+    scaler.scale(loss); scaler.unscale_(opt); clip_grad_norm_(params, 1.0); scaler.step(opt);
+    scaler.update(), with AdamW(fused=False) on CPU tensors, over the CPU sample. NumPy runs
+    these elementwise passes on one thread. Returns the median per-step throughput of
+    `steps` timed steps after `warmup`, or None without the install."""
+    ref = load_reference_package()
+    if ref is None:
+        return None
+    nt, optim, amp, Parameter = ref
+    params_np, grads_np = _cpu_sample_arrays()
+    params = [Parameter(nt.tensor(a)) for a in params_np]
+    decay = [params[i] for i in CPU_SAMPLE_DECAY]
+    no_decay = [p for i, p in enumerate(params) if i not in CPU_SAMPLE_DECAY]
+    opt = optim.AdamW([{"params": decay, "weight_decay": 0.1}, {"params": no_decay, "weight_decay": 0.0}],
+                      lr=3e-4, betas=(0.9, 0.999), eps=1e-8, fused=False)
+    scaler = amp.GradScaler(init_scale=65536.0, growth_factor=2.0, backoff_factor=0.5, growth_interval=2000)
+    loss = nt.tensor(np.float32(1.0))
+    times = []
+    for k in range(warmup + steps):
+        for p, g in zip(params, grads_np):
+            p._grad = nt.tensor(g.copy())
+        t0 = time.perf_counter()
+        scaler.scale(loss)
+        scaler.unscale_(opt)
+        optim.clip_grad_norm_(params, 1.0)
+        scaler.step(opt)
+        scaler.update()
+        if k >= warmup:
+            times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": CPU_SAMPLE_PARAMS / t, "unit": "params/s", "cores": 1, "kind": "reference",
+            "sample": CPU_SAMPLE_TEXT + "; the reference's own GradScaler + clip_grad_norm_ 1.0 + AdamW(fused=False) "
+                      f"from baseline/_ref (NumPy, one thread), median of {steps} steps after {warmup}",
+            "step_seconds": t, "host": host_info()}
+
+
+def cpu_amp_sample(steps: int, threads: int, warmup: int = 1) -> dict:
+    """The oracle port of the same AMP step (unscale, finite, two-pass fp64 norm, clip, AdamW)
+    on the same sample, split into per-thread chunks (NumPy ufuncs release the GIL)."""
+    from oracle import adamw as oadamw
+    params_np, grads_np = _cpu_sample_arrays()
+    wd = np.concatenate([np.full(a.size, 0.1 if i in CPU_SAMPLE_DECAY else 0.0) for i, a in enumerate(params_np)])
+    p = np.concatenate([a.reshape(-1) for a in params_np])
+    g0 = np.concatenate([a.reshape(-1) for a in grads_np])
+    n = p.size
     m = np.zeros_like(p)
     v = np.zeros_like(p)
-    chunk = max(1 << 20, n // max(threads, 1) // 4)
-    bounds = [(i, min(n, i + chunk)) for i in range(0, n, chunk)]
+    # chunks never straddle a weight-decay boundary
+    edges = np.cumsum([0] + [a.size for a in params_np])
+    bounds = []
+    chunk = max(1 << 18, n // max(threads, 1) // 4)
+    for lo, hi in zip(edges[:-1], edges[1:]):
+        bounds += [(i, min(int(hi), i + chunk)) for i in range(int(lo), int(hi), chunk)]
     scale = 65536.0
     pool = ThreadPoolExecutor(max_workers=threads)
     times = []
     step = 0
-    for _ in range(steps):
+    for k in range(warmup + steps):
         g = g0.copy()
         t0 = time.perf_counter()
 
@@ -184,16 +276,18 @@ def cpu_amp_sample(n: int, steps: int, threads: int) -> dict:
                 if coef < 1:
                     g[s:e] = (np.asarray(g[s:e], np.float64) * coef).astype(np.float32)
                 oadamw.adam_update(p[s:e], g[s:e], m[s:e], v[s:e], step, lr=3e-4, beta1=0.9, beta2=0.999,
-                                   eps=1e-8, weight_decay=0.1)
+                                   eps=1e-8, weight_decay=float(wd[s]))
 
             list(pool.map(clip_and_update, bounds))
             step += 1
-        times.append(time.perf_counter() - t0)
+        if k >= warmup:
+            times.append(time.perf_counter() - t0)
     pool.shutdown()
     t = statistics.median(times)
     return {"value": n / t, "unit": "params/s", "cores": threads, "kind": "port",
-            "sample": f"{n} parameters of the workload's flat buffer (bf16-valued grads x 65536), "
-                      f"AMP step = unscale + finite + two-pass fp64 norm + clip 1.0 + AdamW, median of {steps} steps"}
+            "sample": CPU_SAMPLE_TEXT + "; AMP step = unscale + finite + two-pass fp64 norm + clip 1.0 + AdamW "
+                      f"(oracle port, {threads} threads by chunk), median of {steps} steps after {warmup}",
+            "step_seconds": t, "host": host_info()}
 
 
 def cpu_xent_sample(rows: int, threads: int) -> dict:
@@ -252,28 +346,19 @@ def group_params(shape, params, wd=0.1):
             {"params": [params[i] for i in no_decay], "weight_decay": 0.0}]
 
 
-def run_ours(args):
+def build_step(shape, device, rank, world, transport, seed_params=0):
+    """(optimizer, scaler, params, flat gradient buffer, loss, step function) of the AMP step
+    on `shape`: AdamW (ZeroAdamW over the process group at N > 1) with a bf16 model copy and
+    bf16 gradients N(0, 1e-3) x 65536, GradScaler(65536), clip_grad_norm_ 1.0."""
     import torch
-    import torch.distributed as dist
-    from namitorch_b200 import _native as N
     from namitorch_b200 import GradScaler
     from namitorch_b200.optim import AdamW, clip_grad_norm_
-
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
-    shape = shape_for(args.workload)
-    P = shape.numel()
     init_scale = 65536.0
-
-    params = make_params(shape, device)
+    params = make_params(shape, device, seed=seed_params)
     if world > 1:
         from namitorch_b200.zero import ZeroAdamW
         opt = ZeroAdamW(group_params(shape, params), lr=3e-4, betas=(0.9, 0.999), eps=1e-8,
-                        model_dtype=torch.bfloat16, transport=args.zero_transport)
+                        model_dtype=torch.bfloat16, transport=transport)
         flat_grads = opt.flat_grads
         with torch.no_grad():
             gen = torch.Generator(device=device)
@@ -285,10 +370,61 @@ def run_ours(args):
     else:
         opt = AdamW(group_params(shape, params), lr=3e-4, betas=(0.9, 0.999), eps=1e-8, model_dtype=torch.bfloat16)
         flat_grads, views = make_flat_grads(params, device, init_scale)
-        for p, g in zip(params, views):
-            p.grad = g
+        for prm, g in zip(params, views):
+            prm.grad = g
     scaler = GradScaler(init_scale=init_scale, growth_factor=2.0, backoff_factor=0.5, growth_interval=2000)
     loss = torch.ones((), device=device)
+
+    def step():
+        scaler.scale(loss)
+        scaler.unscale_(opt)
+        clip_grad_norm_(params, 1.0)
+        scaler.step(opt)
+        scaler.update()
+
+    return opt, scaler, params, flat_grads, loss, step
+
+
+def device_timed(step, steps: int, warmup: int, world: int) -> float:
+    """Mean ms per step over `steps` steps after `warmup`, CUDA events on the current stream,
+    barriers and synchronisation on both sides, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=torch.cuda.current_device())
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from namitorch_b200 import _native as N
+    from namitorch_b200.optim import clip_grad_norm_
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        pin_host_threads(local)
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    shape = shape_for(args.workload)
+    P = shape.numel()
+    opt, scaler, params, flat_grads, loss, plain_step = build_step(shape, device, rank, world, args.zero_transport)
     stream = torch.cuda.current_stream()
     ev = []
     phases = []   # ZeRO-1: the optimizer's own events (reduce-scatter, stats, update, all-gather tail)
@@ -356,10 +492,11 @@ def run_ours(args):
         update_ms = upd_ms   # the update kernels alone (all-gathers overlap them on the side stream)
     peak, peak_kind = measured_peak()
     shard = P / world
+    traffic = committed_traffic("adamw_mt", args.workload)
     result = {
         "metric": METRIC, "value": P / (ms / 1e3), "unit": "params/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "strong", "vs_baseline": None, "dtype": "f32",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": f"{shape.name} AdamW+AMP step (BASELINE config 3; fp32 master/moments, bf16 grads "
                                "and model copy, GradScaler, clip_grad_norm_ 1.0, 2 param groups)",
@@ -373,24 +510,25 @@ def run_ours(args):
                      "unit": "GB/s", "frac": BYTES_UPDATE * shard / (update_ms / 1e3) / 1e9 / peak,
                      "peak_source": peak_kind, "kernel": "adamw_mt",
                      "algorithmic_bytes_per_launch": BYTES_UPDATE * shard,
-                     "traffic": committed_traffic("adamw_mt", args.workload)},
+                     # DRAM bytes of one launch: the committed ncu capture of the 124M update,
+                     # scaled by parameter count to the whole model, then to this rank's shard.
+                     "traffic": None if traffic is None else traffic / world,
+                     "traffic_source": None if traffic is None else
+                     "ncu dram read+write of the 124M adamw_mt launch (profiles/adamw_mt_124m.md), scaled by "
+                     "parameter count to 1.3B" + (f" and to the 1/{world} shard" if world > 1 else "")},
         "gpu_launches": launches,
         "clocks": clocks,
     }
     if breakdown:
         result["zero1_breakdown_ms"] = breakdown
-        # Reduce-scatter and all-gather each move (N-1)/N of the 2-byte gradient / model copy
-        # per GPU and direction; against the measured 770 GB/s peer copy per direction.
-        link_bytes = 2 * 2.0 * P * (world - 1) / world
-        result["nvlink"] = {"bytes_per_gpu_per_step": link_bytes, "peak_gbs_per_direction": 770.0,
-                            "floor_ms": link_bytes / 770e9 * 1e3,
-                            "frac_of_step": link_bytes / 770e9 * 1e3 / ms}
-
+        result["nvlink"] = nvlink_section(opt, P, world, ms, breakdown)
     if world == 1:
         result["loop"] = loop_tail(args, opt, scaler, params, loss)
         result["captured"] = captured_tail(opt, scaler, params, loss)
     if not args.no_e2e:
         result["e2e"] = e2e_ours(args, opt, scaler, params, flat_grads, loss, world)
+    if world > 1:
+        result["zero_parity"] = zero_parity(opt, scaler, params, loss)
     # The update alone (the HBM-bound part that shards), for the update-scaling figure
     # t_update(1 GPU, P) / max over ranks t_update(N, P/N). At N > 1 this runs last: it
     # advances the optimizer state without exchanges.
@@ -406,14 +544,264 @@ def run_ours(args):
                              "frac_of_measured_hbm": BYTES_UPDATE * shard / (only_ms / 1e3) / 1e9 / peak}
     if world > 1:
         dist.barrier()
+        opt.close()
+        del opt, scaler, params, flat_grads, plain_step
+        torch.cuda.empty_cache()
+        if args.zero_transport == "auto" and not args.no_nccl_compare:
+            result["nccl_transport"] = nccl_comparison(shape, device, rank, world)
+    else:
+        del opt, scaler, params, flat_grads, plain_step
+        torch.cuda.empty_cache()
+        if args.workload == "1p3b" and not args.no_extra:
+            result.update(extra_workloads(args))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_amp_sample(args.cpu_sample, 3, os.cpu_count() or 1)
+        ref = reference_amp_sample(steps=3)
+        port = cpu_amp_sample(3, len(os.sched_getaffinity(0)))
+        result["cpu_baseline"] = ref if ref is not None else port
+        result["cpu_port"] = port
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.barrier()
-        opt.close()
         dist.destroy_process_group()
+
+
+def pin_host_threads(local_rank: int) -> None:
+    """Restricts this rank's host threads to the CPUs NVML reports as closest to its GPU, so
+    that its pinned host buffers are allocated (first touch) in that GPU's NUMA node. Keeps
+    the current affinity when NVML is unavailable or reports nothing."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(visible.split(",")[local_rank]) if visible else local_rank
+            handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            words = pynvml.nvmlDeviceGetCpuAffinity(handle, 16)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {w * 64 + b for w, word in enumerate(words) for b in range(64) if (int(word) >> b) & 1}
+        cpus &= set(os.sched_getaffinity(0))
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+    except Exception:
+        pass
+
+
+def measure_peer_bandwidth(world: int, rank: int, device, total_bytes: int = 512 << 20, reps: int = 5) -> dict:
+    """SM-driven NVLink bandwidth per GPU and direction, measured in this run with the
+    access pattern of the ZeRO-1 kernels (plain 16-byte loads and stores, no copy engine,
+    no multicast): every rank at once pulls total_bytes / (N - 1) from each peer's buffer
+    (inbound, the reduce-scatter), then pushes as much into each peer's buffer (outbound,
+    the all-gather). Median of `reps` launches, max over ranks of each launch's time."""
+    import torch
+    import torch.distributed as dist
+    from namitorch_b200 import _native as N
+    per = (total_bytes // (world - 1)) // 16 * 16
+    buf = torch.zeros(world * per, dtype=torch.uint8, device=device)   # slot 0: own data; slots 1..N-1: inbox
+    handles = [None] * world
+    dist.all_gather_object(handles, N.ipc_export(buf.data_ptr()))
+    peers = {q: N.ipc_open(*handles[q]) for q in range(world) if q != rank}
+    base = buf.data_ptr()
+    others = [q for q in range(world) if q != rank]
+
+    def inbox(of: int, sender: int) -> int:   # the slot rank `sender` writes in rank `of`'s buffer
+        return 1 + (sender if sender < of else sender - 1)
+
+    pull = ([peers[q] for q in others], [base + inbox(rank, q) * per for q in others])
+    push = ([base] * len(others), [peers[q] + inbox(q, rank) * per for q in others])
+    out = {}
+    for name, (src, dst) in (("pull", pull), ("push", push)):
+        times = []
+        for _ in range(reps + 1):
+            torch.cuda.synchronize()
+            dist.barrier()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            N.peer_copy(src, dst, per)
+            end.record()
+            end.synchronize()
+            t = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            times.append(float(t.item()))
+        ms = statistics.median(times[1:])
+        out[f"{name}_gbs"] = (world - 1) * per / (ms / 1e3) / 1e9
+        out[f"{name}_ms"] = ms
+    torch.cuda.synchronize()
+    dist.barrier()
+    for ptr in peers.values():
+        N.ipc_close(ptr)
+    dist.barrier()
+    del buf
+    out["bytes_per_gpu"] = (world - 1) * per
+    out["how"] = ("nt_peer_copy, every rank at once: pull = (N-1) peer buffers -> local, push = local -> (N-1) peer "
+                  "buffers; 16-byte SM loads/stores; median of %d launches, max over ranks" % reps)
+    return out
+
+
+def nvlink_section(opt, P: int, world: int, ms: float, breakdown: dict) -> dict:
+    """The step's NVLink floor against the peer bandwidth measured in this run: the
+    reduce-scatter pulls and the all-gather pushes (N-1)/N of the 2-byte buffer per GPU."""
+    link_bytes = 2.0 * P * (world - 1) / world          # per phase, per GPU and direction
+    bw = measure_peer_bandwidth(world, opt.rank, opt.device)
+    floor_ms = (link_bytes / (bw["pull_gbs"] * 1e9) + link_bytes / (bw["push_gbs"] * 1e9)) * 1e3
+    rs_gbs = link_bytes / (breakdown["reduce_scatter"] / 1e3) / 1e9
+    push_gbs = link_bytes / (breakdown["update_with_overlapped_all_gather"] / 1e3) / 1e9
+    return {"bytes_per_gpu_per_phase": link_bytes, "measured": bw,
+            "floor_ms": floor_ms, "step_frac_of_floor": floor_ms / ms,
+            "reduce_scatter_gbs": rs_gbs, "reduce_scatter_frac_of_pull": rs_gbs / bw["pull_gbs"],
+            "update_push_gbs": push_gbs, "update_push_frac_of_push": push_gbs / bw["push_gbs"]}
+
+
+def zero_parity(opt, scaler, params, loss) -> dict:
+    """One more ZeRO-1 step, checked on every rank after the timed region.
+
+    * copies_equal: the all-gathered bf16 model copy is byte-identical on every rank (SHA-256
+      of the whole copy, compared across ranks);
+    * reduce_bit_exact: a seeded slice of up to 1M elements of this rank's reduced gradient
+      shard equals the float32 sum of every rank's contribution in rank order, divided by N,
+      rounded once to bf16 (the contributions are exchanged with an all-to-all);
+    * shard_bit_exact: master / exp_avg / exp_avg_sq of that slice after the step equal what
+      the reference's own AdamW(fused=False) (baseline/_ref) computes from the pre-step state
+      and the reduced gradient after the reference's unscale (g / scale) and clip multiply
+      (f32(f64(g) * coef), coef = 1 / (norm + 1e-6)) with the step's global norm. Without
+      the reference install, the single-GPU nt_adamw_f32 kernel is the checker instead.
+    Returns the result summed / AND-ed over ranks."""
+    import hashlib
+    import torch
+    import torch.distributed as dist
+    from namitorch_b200.optim import clip_grad_norm_
+    rank, world, device = opt.rank, opt.world, opt.device
+    # The slice: inside the largest parameter piece this rank owns.
+    if opt.pieces:
+        i, off, n, _ = max(opt.pieces, key=lambda t: t[2])
+    else:
+        i, off, n = 0, 0, 0
+    m = min(n, 1 << 20)
+    rng = np.random.default_rng(1000 + rank)
+    start = off + (int(rng.integers(0, n - m + 1)) if n > m else 0)
+    gstart = opt._global(start) if m else 0
+    meta = [None] * world
+    dist.all_gather_object(meta, (gstart, m))
+    with torch.no_grad():
+        sends = [opt.flat_grads[g:g + k].contiguous() for g, k in meta]
+        recvs = [torch.empty(m, dtype=opt.flat_grads.dtype, device=device) for _ in range(world)]
+        dist.all_to_all(recvs, sends)
+        pre = [t[start:start + m].detach().cpu().numpy().copy() for t in (opt.master, opt.exp_avg, opt.exp_avg_sq)]
+        step_count = int(opt.steps[i].item()) if m else 0
+        contrib = [r.float().cpu().numpy() for r in recvs]
+    scale = scaler.get_scale()
+    scaler.scale(loss)
+    finite = scaler.unscale_(opt)
+    norm_t = clip_grad_norm_(params, 1.0)
+    scaler.step(opt)
+    scaler.update()
+    torch.cuda.synchronize()
+    norm = float(norm_t.item())
+    stepped = bool(finite)
+    with torch.no_grad():
+        reduced_bits = opt.grad_shard[start:start + m].view(torch.int16).cpu().numpy()
+        post = [t[start:start + m].detach().cpu().numpy().copy() for t in (opt.master, opt.exp_avg, opt.exp_avg_sq)]
+        digest = hashlib.sha256()
+        chunk = 1 << 27
+        for lo in range(0, opt.copy.numel(), chunk):
+            digest.update(opt.copy[lo:lo + chunk].view(torch.int16).cpu().numpy().tobytes())
+    digests = [None] * world
+    dist.all_gather_object(digests, digest.hexdigest())
+    # Reduced gradient: f32 rank-order sum, / N (an exact multiply for a power of two), one RNE rounding.
+    total = contrib[0].astype(np.float32)
+    for c in contrib[1:]:
+        total = (total + c).astype(np.float32)
+    total = (total / np.float32(world)).astype(np.float32)
+    want_bits = torch.from_numpy(total).to(torch.bfloat16).view(torch.int16).numpy()
+    reduce_bad = int(np.count_nonzero(want_bits != reduced_bits))
+    reduced = torch.from_numpy(reduced_bits.copy()).view(torch.bfloat16).float().numpy()
+    group = next(g for g in opt.param_groups if any(q is params[i] for q in g["params"]))
+    expect, checker = _shard_reference(pre, reduced, scale, norm, step_count, group, stepped, device)
+    shard_bad = sum(int(np.count_nonzero(a.view(np.uint32) != b.view(np.uint32))) for a, b in zip(post, expect))
+    t = torch.tensor([reduce_bad, shard_bad, m, int(len(set(digests)) == 1), int(stepped)], dtype=torch.float64,
+                     device=device)
+    sums, mins = t[:3].clone(), t[3:].clone()
+    dist.all_reduce(sums, op=dist.ReduceOp.SUM)
+    dist.all_reduce(mins, op=dist.ReduceOp.MIN)
+    reduce_bad, shard_bad, checked = (int(x) for x in sums.tolist())
+    same, stepped_all = (int(x) for x in mins.tolist())
+    return {"copies_equal": bool(same), "reduce_bit_exact": reduce_bad == 0, "shard_bit_exact": shard_bad == 0,
+            "mismatches": reduce_bad + shard_bad, "elements_checked": checked, "stepped": bool(stepped_all),
+            "checker": checker, "copy_sha256": digests[0][:16]}
+
+
+def _shard_reference(pre, reduced, scale, norm, step_count, group, stepped, device):
+    """(expected master, exp_avg, exp_avg_sq of the slice after the step, checker name)."""
+    if not stepped:
+        return [a.copy() for a in pre], "skipped step: state unchanged"
+    g = (reduced.astype(np.float32) / np.float32(scale)).astype(np.float32)
+    coef = 1.0 / (norm + 1e-6)
+    if coef < 1:
+        g = (g.astype(np.float64) * coef).astype(np.float32)
+    lr, (beta1, beta2), eps, wd = group["lr"], group["betas"], group["eps"], group["weight_decay"]
+    ref = load_reference_package()
+    if ref is not None:
+        nt, optim, _, Parameter = ref
+        prm = Parameter(nt.tensor(pre[0].copy()))
+        ropt = optim.AdamW([{"params": [prm], "weight_decay": wd}], lr=lr, betas=(beta1, beta2), eps=eps, fused=False)
+        state = ropt.state_dict()
+        if step_count:
+            state["state"] = {0: {"step": step_count, "exp_avg": pre[1].copy(), "exp_avg_sq": pre[2].copy()}}
+        ropt.load_state_dict(state)
+        prm._grad = nt.tensor(g)
+        ropt.step()
+        st = ropt.state[id(prm)]
+        return ([np.asarray(prm._data), np.asarray(st["exp_avg"]._data), np.asarray(st["exp_avg_sq"]._data)],
+                "reference AdamW(fused=False) from baseline/_ref")
+    import torch
+    from namitorch_b200 import _native as N
+    from namitorch_b200.optim._common import _scalar
+    t = step_count + 1
+    coefs = [_scalar(lr), _scalar(beta1), _scalar(beta2), _scalar(1 - beta1), _scalar(1 - beta2), _scalar(eps, "eps"),
+             _scalar(wd), _scalar(1 - lr * wd, "decay factor"), _scalar(1 - beta1 ** t), _scalar(1 - beta2 ** t)]
+    arrs = [torch.from_numpy(a.copy()).to(device) for a in (pre[0], g, pre[1], pre[2])]
+    c = (N.C.c_float * 10)(*[float(x) for x in coefs])
+    N.call("nt_adamw_f32", arrs[0].data_ptr(), arrs[1].data_ptr(), arrs[2].data_ptr(), arrs[3].data_ptr(), c, 0,
+           int(lr != 0), arrs[0].numel(), N.stream_handle())
+    torch.cuda.synchronize()
+    return [arrs[k].cpu().numpy() for k in (0, 2, 3)], "nt_adamw_f32 (single-GPU kernel)"
+
+
+def nccl_comparison(shape, device, rank, world, steps: int = 10, warmup: int = 3) -> dict:
+    """The same ZeRO-1 step over the NCCL transport (reduce-scatter, statistics all-reduce,
+    per-piece update + all-gather on a side stream), timed the same way, for comparison with
+    the peer-memory kernels of the main line."""
+    import torch
+    opt, scaler, params, flat_grads, loss, step = build_step(shape, device, rank, world, "nccl")
+    ms = device_timed(step, steps, warmup, world)
+    out = {"ms_per_step": ms, "value": shape.numel() / (ms / 1e3), "unit": "params/s", "steps": steps,
+           "warmup": warmup, "pieces": opt._pieces}
+    opt.close()
+    del opt, scaler, params, flat_grads, step
+    torch.cuda.empty_cache()
+    return out
+
+
+def extra_workloads(args) -> dict:
+    """BASELINE configurations 4 (fused cross-entropy, [8192, 50257] bf16) and 2 (the 124M
+    AMP step), timed in the same run and added to the default line."""
+    import torch
+    from namitorch_b200 import workloads as W
+    xent = measure_xent(max(20, args.steps), max(3, args.warmup))
+    device = torch.device("cuda", torch.cuda.current_device())
+    shape = W.CONFIG_124M
+    opt, scaler, params, flat_grads, loss, step = build_step(shape, device, 0, 1, "auto")
+    ms = device_timed(step, 100, 10, 1)
+    peak, _ = measured_peak()
+    del opt, scaler, params, flat_grads, step
+    torch.cuda.empty_cache()
+    return {"xent_ms": xent["ms_per_step"], "xent_frac": xent["roofline"]["frac"],
+            "xent_gbs": xent["roofline"]["achieved"],
+            "cfg2_ms_per_step": ms, "cfg2_params_per_s": shape.numel() / (ms / 1e3),
+            "cfg2_frac": BYTES_STEP * shape.numel() / (ms / 1e3) / 1e9 / peak,
+            "extra_what": "xent: BASELINE config 4 fused softmax-CE fwd+bwd, 4 B/logit + 8 B/row; cfg2: BASELINE "
+                          "config 2 (124M) AMP step at 30 B/param; CUDA events, measured HBM peak"}
 
 
 def loop_tail(args, opt, scaler, params, loss, steps: int = 30):
@@ -489,13 +877,18 @@ def captured_tail(opt, scaler, params, loss, steps: int = 50):
 
 def e2e_ours(args, opt, scaler, params, flat_grads, loss, world):
     """The same step with this step's gradients copied in from pinned host memory and the
-    result (norm, found_inf) read back to the host every step, timed on the host clock.
+    result (norm, found_inf) read back to the host every step, timed on the host clock
+    (max over ranks).
 
-    ``serial``: copy, step and read-back one after the other. At N = 1 the reported value is
+    ``serial``: copy, step and read-back one after the other. The reported value is
     ``pipelined``: two device gradient buffers, and the copy of step i + 1's gradients runs
     on a copy stream while step i computes (the prefetch a data loader does); the host still
-    reads every step's norm and found_inf before it issues the next step. Each step's
-    parameters point their ``.grad`` at the buffer its copy landed in."""
+    reads every step's norm and found_inf before it issues the next step. At N = 1 each
+    step's parameters point their ``.grad`` at the buffer its copy landed in; at N > 1 the
+    ZeRO-1 optimizer switches between two gradient buffers that every peer has mapped
+    (``ZeroAdamW.add_gradient_buffer`` / ``use_gradient_buffer``). Every rank copies its own
+    full gradient (data parallelism: each rank's gradients differ). ``h2d_gbs_per_rank`` is
+    the copy alone on the copy stream, every rank at once (CUDA events, the slowest rank)."""
     import torch
     import torch.distributed as dist
     from namitorch_b200.optim import clip_grad_norm_
@@ -504,6 +897,8 @@ def e2e_ours(args, opt, scaler, params, flat_grads, loss, world):
     out = torch.empty(2, dtype=torch.float64, pin_memory=True)
     nbytes = flat_grads.numel() * flat_grads.element_size()
     P = sum(p.numel() for p in params)
+    main = torch.cuda.current_stream()
+    side = torch.cuda.Stream(device=flat_grads.device)
 
     def run_step():
         scaler.scale(loss)
@@ -513,6 +908,13 @@ def e2e_ours(args, opt, scaler, params, flat_grads, loss, world):
         scaler.update()
         out[0].copy_(norm, non_blocking=True)
         out[1].copy_(found._tensor, non_blocking=True)
+
+    def slowest(t: float) -> float:
+        if world > 1:
+            tt = torch.tensor([t], dtype=torch.float64, device=flat_grads.device)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
 
     times = []
     for i in range(args.e2e_steps + 1):
@@ -525,29 +927,42 @@ def e2e_ours(args, opt, scaler, params, flat_grads, loss, world):
         torch.cuda.current_stream().synchronize()
         if i:
             times.append(time.perf_counter() - t0)
-    t = statistics.median(times)
-    if world > 1:
-        tt = torch.tensor([t], dtype=torch.float64, device=flat_grads.device)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t = float(tt.item())
-    result = {"value": P / t, "unit": "params/s", "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": 16,
-              "ms_per_step": t * 1e3,
-              "path": "pinned host grads -> H2D -> unscale_/clip_grad_norm_/step/update -> D2H norm+found_inf "
-                      "(public API), one after the other"}
-    if world > 1:
-        return result
+    t_serial = slowest(statistics.median(times))
+
+    # The copy alone: every rank at once, as in the steps.
+    copy_ms = []
+    for _ in range(3):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(side):
+            e0.record(side)
+            flat_grads.copy_(host, non_blocking=True)
+            e1.record(side)
+        e1.synchronize()
+        copy_ms.append(e0.elapsed_time(e1))
+    h2d_ms = slowest(statistics.median(copy_ms))
 
     # Pipelined: buffer b = i % 2 receives step i's gradients on the copy stream; the copy of
     # step i + 1 is queued before step i's compute, behind step i - 1's use of that buffer.
-    main = torch.cuda.current_stream()
-    side = torch.cuda.Stream(device=flat_grads.device)
-    bufs = [flat_grads, torch.empty_like(flat_grads)]
-    base = flat_grads.data_ptr()
-    grads = [p.grad for p in params]
-    views = [[g] for g in grads]
-    for g, vs in zip(grads, views):
-        off = (g.data_ptr() - base) // flat_grads.element_size()
-        vs.append(bufs[1][off:off + g.numel()].view(g.shape))
+    if world > 1:
+        other = opt.add_gradient_buffer() if len(opt.gradient_buffers) < 2 else 1
+        bufs = [opt.gradient_buffers[0], opt.gradient_buffers[other]]
+        use = [lambda: opt.use_gradient_buffer(0), lambda: opt.use_gradient_buffer(other)]
+    else:
+        bufs = [flat_grads, torch.empty_like(flat_grads)]
+        base = flat_grads.data_ptr()
+        grads = [p.grad for p in params]
+        views = [[g] for g in grads]
+        for g, vs in zip(grads, views):
+            off = (g.data_ptr() - base) // flat_grads.element_size()
+            vs.append(bufs[1][off:off + g.numel()].view(g.shape))
+
+        def use_views(b):
+            for p, vs in zip(params, views):
+                p.grad = vs[b]
+        use = [lambda: use_views(0), lambda: use_views(1)]
     landed = [torch.cuda.Event() for _ in range(2)]
     released = [torch.cuda.Event() for _ in range(2)]
     steps = args.e2e_steps + 2
@@ -560,9 +975,12 @@ def e2e_ours(args, opt, scaler, params, flat_grads, loss, world):
             landed[b].record(side)
 
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     for b in range(2):
         released[b].record(main)
     copy_in(0)
+    t1 = time.perf_counter()
     for i in range(steps):
         if i == 1:
             t1 = time.perf_counter()   # the first step (pipeline fill) is not counted
@@ -570,52 +988,51 @@ def e2e_ours(args, opt, scaler, params, flat_grads, loss, world):
         if i + 1 < steps:
             copy_in(i + 1)
         main.wait_event(landed[b])
-        for p, vs in zip(params, views):
-            p.grad = vs[b]
+        use[b]()
         run_step()
         released[b].record(main)
         main.synchronize()              # the host reads step i's norm and found_inf
         _ = float(out[0]), float(out[1])
-    t_pipe = (time.perf_counter() - t1) / (steps - 1)
-    for p, g in zip(params, grads):
-        p.grad = g
-    result["serial_ms_per_step"] = result["ms_per_step"]
-    result["serial_value"] = result["value"]
-    result.update({"value": P / t_pipe, "ms_per_step": t_pipe * 1e3,
-                   "path": "pinned host grads -> H2D on a copy stream (double-buffered, step i+1's copy "
-                           "overlaps step i) -> unscale_/clip_grad_norm_/step/update -> D2H norm+found_inf "
-                           "read by the host every step (public API)"})
-    return result
+    t_pipe = slowest((time.perf_counter() - t1) / (steps - 1))
+    use[0]()
+    torch.cuda.synchronize()
+    return {"value": P / t_pipe, "unit": "params/s", "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": 16,
+            "ms_per_step": t_pipe * 1e3, "serial_ms_per_step": t_serial * 1e3, "serial_value": P / t_serial,
+            "h2d_ms": h2d_ms, "h2d_gbs_per_rank": nbytes / (h2d_ms / 1e3) / 1e9,
+            "host": host_info(),
+            "path": "pinned host grads -> H2D on a copy stream (double-buffered, step i+1's copy overlaps step i) "
+                    "-> unscale_/clip_grad_norm_/step/update -> D2H norm+found_inf read by the host every step "
+                    "(public API); every rank copies its own full gradient"}
 
 
-def run_xent(args):
+def measure_xent(steps: int, warmup: int) -> dict:
+    """The fused softmax cross-entropy forward + backward on BASELINE configuration 4."""
     import torch
     from namitorch_b200 import _native as N
     from namitorch_b200 import workloads as W
     from namitorch_b200.nn.functional import softmax_cross_entropy
-    device = torch.device("cuda", 0)
-    torch.cuda.set_device(device)
+    device = torch.device("cuda", torch.cuda.current_device())
     gen = torch.Generator(device=device)
     gen.manual_seed(0)
     rows, classes = W.XENT_ROWS, W.XENT_CLASSES
     x = torch.empty(rows, classes, dtype=torch.float32, device=device).normal_(0, 2.0, generator=gen).to(torch.bfloat16)
     t = torch.randint(0, classes, (rows,), device=device, generator=gen)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         softmax_cross_entropy(x, t, validate=False)
     torch.cuda.synchronize()
     launches0 = N.launch_count
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         loss, dl = softmax_cross_entropy(x, t, validate=False)
     end.record()
     torch.cuda.synchronize()
-    ms = start.elapsed_time(end) / args.steps
+    ms = start.elapsed_time(end) / steps
     peak, kind = measured_peak()
     nbytes = rows * classes * 4 + rows * 8
     result = {"metric": "fused softmax-CE fwd+bwd rows/s", "value": rows / (ms / 1e3), "unit": "rows/s",
-              "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+              "n_gpus": 1, "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True,
               "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
               "config": {"workload": "LM-head logits [8192, 50257] bf16 N(0,2), int64 targets (BASELINE config 4)",
                          "l2": "inputs larger than L2 (823 MB logits + 823 MB dlogits)"},
@@ -623,6 +1040,15 @@ def run_xent(args):
                            "frac": nbytes / (ms / 1e3) / 1e9 / peak, "peak_source": kind,
                            "traffic": committed_traffic("xent", "xent")},
               "gpu_launches": N.launch_count - launches0}
+    del x, t, loss, dl
+    torch.cuda.empty_cache()
+    return result
+
+
+def run_xent(args):
+    import torch
+    torch.cuda.set_device(0)
+    result = measure_xent(args.steps, args.warmup)
     if not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_xent_sample(256, os.cpu_count() or 1)
     print(json.dumps(result), flush=True)
@@ -878,7 +1304,7 @@ def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0))
     if args.workload == "xent":
         times = []
         for i in range(args.warmup + args.steps):
@@ -920,10 +1346,16 @@ def run_reference(args):
         line = {"impl": "reference", "metric": "layer norm fwd+bwd rows/s", "value": value, "unit": "rows/s",
                 "higher_is_better": True}
     else:
-        n = min(args.cpu_sample, 1 << 24)
-        base = cpu_amp_sample(n, args.warmup + args.steps, threads)
+        # The reference's own AMP step (baseline/_ref, its public API and NumPy path) on the
+        # CPU sample; the threaded oracle port of the same step beside it.
+        base = reference_amp_sample(steps=args.steps, warmup=args.warmup)
+        port = cpu_amp_sample(args.steps, threads, warmup=args.warmup)
+        if base is None:
+            base = dict(port, note="baseline/_ref is not installed: the oracle port stands in for the reference")
         value = base["value"]
-        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "params/s", "higher_is_better": True}
+        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "params/s", "higher_is_better": True,
+                "port_threaded": {k: port[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "host": base.get("host")}
     line.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                  "config": {"workload": args.workload, "sample": base["sample"]},
                  "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},

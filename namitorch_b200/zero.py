@@ -225,12 +225,18 @@ class ZeroAdamW(_FirstOrderAdam):
             for p, off in zip(params, self.layout.offsets):
                 view = self.copy[off:off + p.numel()].view(p.shape)
                 view.copy_(p.detach())
-            for p, off in zip(params, self.layout.offsets):
+            views = [self.flat_grads[off:off + p.numel()].view(p.shape) for p, off in zip(params, self.layout.offsets)]
+            for p, off, view in zip(params, self.layout.offsets, views):
                 p.data = self.copy[off:off + p.numel()].view(p.shape)
-                p.grad = self.flat_grads[off:off + p.numel()].view(p.shape)
+                p.grad = view
             self.exp_avg = torch.zeros(shard, dtype=torch.float32, device=device)
             self.exp_avg_sq = torch.zeros(shard, dtype=torch.float32, device=device)
             self.steps = torch.zeros(len(params), dtype=torch.int32, device=device)
+        # Gradient buffers: [0] is flat_grads; add_gradient_buffer adds more (double buffering).
+        self.gradient_buffers = [self.flat_grads]
+        self._buffer_views = [views]
+        self._buffer_sources = [None]
+        self._active_buffer = 0
         self.corrections = CorrectionTable(device)
         self.max_step = 0
         self._reduced = False
@@ -271,31 +277,68 @@ class ZeroAdamW(_FirstOrderAdam):
                                "between every pair of GPUs in the group.")
         return "nccl"
 
-    def _map_peers(self):
-        """Maps every other rank's gradient buffer and model copy into this process."""
-        mine = (N.ipc_export(self.flat_grads.data_ptr()), N.ipc_export(self.copy.data_ptr()))
+    def _map_gradient_buffer(self, buf: torch.Tensor) -> list[int]:
+        """Maps every other rank's gradient buffer of the same index (a collective); returns
+        the rank-ordered addresses of every rank's gradients for this rank's shard."""
         handles = [None] * self.world
-        dist.all_gather_object(handles, mine, group=self._group)
-        grads, copies = [], []
-        for q, ((gh, goff), (ch, coff)) in enumerate(handles):
+        dist.all_gather_object(handles, N.ipc_export(buf.data_ptr()), group=self._group)
+        grads = []
+        for q, (gh, goff) in enumerate(handles):
             if q == self.rank:
-                grads.append(self.flat_grads.data_ptr())
-                copies.append(self.copy.data_ptr())
+                grads.append(buf.data_ptr())
                 continue
             g = N.ipc_open(gh, goff)
             self._peer_maps.append(g)
+            grads.append(g)
+        shard_bytes = self.rank * self.piece_len * buf.element_size()
+        return [g + shard_bytes for g in grads]
+
+    def _map_peers(self):
+        """Maps every other rank's gradient buffer and model copy into this process."""
+        self._sources = self._map_gradient_buffer(self.flat_grads)
+        self._buffer_sources[0] = self._sources
+        handles = [None] * self.world
+        dist.all_gather_object(handles, N.ipc_export(self.copy.data_ptr()), group=self._group)
+        copies = []
+        for q, (ch, coff) in enumerate(handles):
+            if q == self.rank:
+                copies.append(self.copy.data_ptr())
+                continue
             c = N.ipc_open(ch, coff)
             self._peer_maps.append(c)
-            grads.append(g)
             copies.append(c)
-        esize = self.flat_grads.element_size()
-        shard_bytes = self.rank * self.piece_len * esize
-        # Rank q's gradients for this rank's shard, in rank order.
-        self._sources = [g + shard_bytes for g in grads]
+        shard_bytes = self.rank * self.piece_len * self.copy.element_size()
         # Where this rank's shard lands in every other rank's copy, addressed like the local
         # copy base (the kernel adds the shard-local offset).
         self._push = [c + shard_bytes for q, c in enumerate(copies) if q != self.rank]
         dist.barrier(group=self._group)
+
+    def add_gradient_buffer(self) -> int:
+        """Allocates one more full gradient buffer on every rank (a collective call) and, over
+        the p2p transport, maps the peers' buffers of the same index. Returns the index for
+        ``use_gradient_buffer``: a data loader can fill one buffer while a step reduces the
+        other."""
+        with torch.no_grad():
+            buf = torch.zeros_like(self.flat_grads)
+        self.gradient_buffers.append(buf)
+        self._buffer_views.append([buf[off:off + p.numel()].view(p.shape)
+                                   for p, off in zip(self.params_list, self.layout.offsets)])
+        self._buffer_sources.append(self._map_gradient_buffer(buf) if self.transport == "p2p" else None)
+        if self.transport == "p2p":
+            dist.barrier(group=self._group)
+        return len(self.gradient_buffers) - 1
+
+    def use_gradient_buffer(self, index: int) -> None:
+        """Makes gradient buffer `index` the one the next step reduces; the parameters' ``.grad``
+        become its views. Every rank must select the same index for a step."""
+        if self._reduced:
+            raise RuntimeError("use_gradient_buffer cannot switch buffers in the middle of a step.")
+        self._active_buffer = index
+        self.flat_grads = self.gradient_buffers[index]
+        if self._buffer_sources[index] is not None:
+            self._sources = self._buffer_sources[index]
+        for p, view in zip(self.params_list, self._buffer_views[index]):
+            p.grad = view
 
     def close(self) -> None:
         """Unmaps the peers' buffers (collective with the other ranks' close())."""
@@ -341,22 +384,22 @@ class ZeroAdamW(_FirstOrderAdam):
             raise TypeError("set_to_none must be a Python bool.")
         with torch.no_grad():
             self.flat_grads.zero_()
-            for p, off in zip(self.params_list, self.layout.offsets):
-                if p.grad is None or p.grad.data_ptr() != self.flat_grads[off:].data_ptr():
-                    p.grad = self.flat_grads[off:off + p.numel()].view(p.shape)
+            for p, own in zip(self.params_list, self._buffer_views[self._active_buffer]):
+                if p.grad is not own:
+                    p.grad = own
 
     # ---- collectives ---------------------------------------------------------------------------
     def _adopt_foreign_grads(self):
         """Copies gradients that autograd stored outside the flat buffer back into it."""
         with torch.no_grad():
-            for p, off in zip(self.params_list, self.layout.offsets):
-                view = self.flat_grads[off:off + p.numel()]
+            for p, own in zip(self.params_list, self._buffer_views[self._active_buffer]):
+                if p.grad is own:
+                    continue
                 if p.grad is None:
-                    view.zero_()
-                    p.grad = view.view(p.shape)
-                elif p.grad.data_ptr() != view.data_ptr():
-                    view.copy_(p.grad.reshape(-1))
-                    p.grad = view.view(p.shape)
+                    own.zero_()
+                elif p.grad.data_ptr() != own.data_ptr():
+                    own.view(-1).copy_(p.grad.reshape(-1))
+                p.grad = own
 
     def _reduce(self, scale=None):
         """Reduce-scatters the gradients (once per step). Over p2p the shard's pass-0
