@@ -60,13 +60,15 @@ class OracleGradScaler:
 
 
 def amp_step(optimizer: OracleAdamW, scaler: OracleGradScaler, grads: list[np.ndarray | None],
-             max_norm: float | None = None, norm_type: float = 2.0, storage=None) -> dict:
+             max_norm: float | None = None, norm_type: float = 2.0, storage=None, given_norm: float | None = None) -> dict:
     """One AMP iteration on float32 gradients that hold loss-scaled values.
 
     ``storage`` (float32 array -> float32 array) models gradients that live in a narrower
     dtype: ``unscale_`` and ``clip_grad_norm_`` write their results back into the gradient
     tensors in place (amp.py:310-315, clip_grad.py:106-111), so each result is rounded to
     that dtype before the next operation reads it (e.g. ``casts.round_to_bf16``).
+
+    ``given_norm`` is passed to ``clip.clip_grad_norm_`` as the norm to clip with.
 
     Returns the scale that was used, whether the optimizer stepped, the pre-clip norm
     (None when clipping did not run) and the scale after ``update``."""
@@ -82,7 +84,7 @@ def amp_step(optimizer: OracleAdamW, scaler: OracleGradScaler, grads: list[np.nd
     norm = None
     if finite and max_norm is not None:
         norm = float(_clip.clip_grad_norm_([g for g in grads if g is not None], max_norm, norm_type,
-                                           error_if_nonfinite=True))
+                                           error_if_nonfinite=True, norm=given_norm))
         store()
     if finite:
         optimizer.step(grads)

@@ -30,9 +30,13 @@ def total_norm(grads: list[np.ndarray], norm_type: float = 2.0) -> np.float64:
 
 
 def clip_grad_norm_(grads: list[np.ndarray], max_norm: float, norm_type: float = 2.0,
-                    error_if_nonfinite: bool = False) -> np.float64:
-    """In-place clip of float arrays; returns the pre-clip norm (float64)."""
-    norm = total_norm(grads, norm_type)
+                    error_if_nonfinite: bool = False, norm: float | None = None) -> np.float64:
+    """In-place clip of float arrays; returns the pre-clip norm (float64).
+
+    ``norm``, when given, replaces the computed total norm: a test hands the oracle the norm
+    a device reduction produced (equal to the two-pass value to about 1e-15 relative, checked
+    separately) so that the clip coefficient, and every value after it, compare bit for bit."""
+    norm = total_norm(grads, norm_type) if norm is None else np.float64(norm)
     if error_if_nonfinite and not bool(np.isfinite(norm)):
         raise RuntimeError(f"Cannot clip gradients with nonfinite total norm {norm}.")
     coefficient = np.divide(float(max_norm), np.add(norm, 1e-6))
