@@ -2,7 +2,7 @@
  * namitorch_b200 — C ABI of the B200 (sm_100a) optimizer-step / mixed-precision hot path.
  *
  * The reference (renderityai/NamiTorch) reaches its CUDA kernels through CuPy RawKernel
- * objects created from source strings (namitorch/backends/cuda/kernels.py:187-203) and
+ * objects created from source strings (namitorch/backends/cuda/kernels.py:114-130) and
  * launched on CuPy's current stream. This library is what that seam binds instead: plain
  * pointers, element counts and a caller-given cudaStream_t passed as `void*` (NULL = the
  * legacy default stream). No torch, CuPy or Python types cross this boundary.
@@ -149,7 +149,7 @@ typedef struct nt_stats {
   double maxabs;     /* max |g| over non-NaN unscaled gradients */
   double powsum;     /* sum (|g|/maxabs)^p, second pass of a general-p norm */
   double norm;       /* total norm, namitorch/optim/clip_grad.py:63-79 */
-  double found_inf;  /* 1.0 when any unscaled gradient is non-finite (namitorch/amp.py:276-291) */
+  double found_inf;  /* 1.0 when any unscaled gradient is non-finite (namitorch/amp.py:153-167) */
   double error;      /* non-zero when a kernel rejected its input */
 } nt_stats;
 
@@ -170,7 +170,7 @@ typedef struct nt_adamw_mt_args {
                                      capacity until that row holds (1.0f, 1.0f) in every group */
   const float* scale;             /* device GradScaler scale or NULL: gradients are divided by it */
   const nt_stats* stats;     /* device stats or NULL */
-  int32_t skip_nonfinite;         /* skip the whole step when stats->found_inf != 0 (amp.py:334-341) */
+  int32_t skip_nonfinite;         /* skip the whole step when stats->found_inf != 0 (amp.py:210-217) */
   int32_t clip;                   /* multiply by max_norm/(stats->norm+1e-6) when < 1 (clip_grad.py:106-111) */
   double max_norm;
   void* workspace;                /* nt_adamw_workspace_size() bytes, zero-filled once */
@@ -193,7 +193,7 @@ size_t nt_adamw_workspace_size(void);
    two moment updates, bias correction from the device step counter, the parameter update
    and the cast into the low-precision model copy, in one read-once / write-once pass.
    Replaces the chain GradScaler.unscale_ -> clip_grad_norm_ -> GradScaler.step ->
-   _FirstOrderOptimizer.step -> AdamW._update_parameter (namitorch/amp.py:293-341,
+   _FirstOrderOptimizer.step -> AdamW._update_parameter (namitorch/amp.py:169-217,
    namitorch/optim/clip_grad.py:96-112, namitorch/optim/_common.py:133-167,
    namitorch/optim/adam.py:28-42 and :69-94). Step counters of the updated segments advance
    by one inside the same launch (the last block commits them). */
@@ -228,7 +228,7 @@ typedef struct nt_grad_stats_args {
 size_t nt_grad_stats_workspace_size(void);
 
 /* One deterministic two-level reduction over all spans: block partials, then the last
-   block reduces them in a fixed order. Replaces GradScaler._finite (namitorch/amp.py:276-291,
+   block reduces them in a fixed order. Replaces GradScaler._finite (namitorch/amp.py:153-167,
    run after unscale_) and _total_norm (namitorch/optim/clip_grad.py:63-79). Pass 0 gives
    found_inf, the max |g| and, for p = 2, the norm in one read; a general p needs pass 1. */
 int nt_grad_stats(const nt_grad_stats_args* args, void* stream);
@@ -264,7 +264,7 @@ int nt_schedule_step(int32_t* lr_step, const double* const* found_inf, int32_t c
 int nt_grad_stats_finalize(nt_stats* stats, double norm_type, void* stream);
 
 /* Rewrites gradients in place: g = dtype(f32(g) / scale) when scale != NULL
-   (GradScaler.unscale_, namitorch/amp.py:310-315), then g = dtype(f64(g) * coef) with
+   (GradScaler.unscale_, namitorch/amp.py:186-191), then g = dtype(f64(g) * coef) with
    coef = max_norm / (stats->norm + 1e-6) when clip != 0 and coef < 1
    (clip_grad_norm_, namitorch/optim/clip_grad.py:106-111). */
 int nt_grad_transform(const nt_span* spans, int32_t num_spans, int32_t chunk_elems,
@@ -275,7 +275,7 @@ int nt_grad_transform(const nt_span* spans, int32_t num_spans, int32_t chunk_ele
 int nt_grad_clip_value(const nt_span* spans, int32_t num_spans, int32_t chunk_elems,
                        int64_t num_chunks, int32_t dtype, double clip_value, void* stream);
 
-/* Dynamic loss-scale update on the device (GradScaler.update, namitorch/amp.py:343-358):
+/* Dynamic loss-scale update on the device (GradScaler.update, namitorch/amp.py:219-234):
    any found_inf -> scale = f32(max(tiny, scale*backoff)), tracker = 0; otherwise
    tracker += 1 and, at growth_interval, scale = f32(min(f32max, scale*growth)), tracker = 0.
    `found_inf` is a host array of `count` device pointers (nt_stats.found_inf fields). */

@@ -4,7 +4,7 @@ API of namitorch/amp.py:18-262. Differences that follow from keeping the loss sc
 GPU (so that no step of the AMP loop waits for the host):
 
 * the scale and growth tracker are device tensors; ``update()`` is one tiny kernel
-  (``nt_scaler_update``) implementing namitorch/amp.py:343-358 bit for bit;
+  (``nt_scaler_update``) implementing namitorch/amp.py:219-234 bit for bit;
 * ``unscale_`` computes found_inf and the gradient norm with one reduction kernel. With
   deferred transforms (the default, see ``optim.defer_gradient_transforms``) it leaves the
   gradient storage untouched and the optimizer's fused update divides by the scale as it
@@ -54,7 +54,7 @@ def _normalize_dtype(dtype) -> torch.dtype:
 
 @contextmanager
 def autocast(device_type="cuda", dtype=torch.float16, enabled=True):
-    """namitorch/amp.py:150-172 (plus bfloat16)."""
+    """namitorch/amp.py:26-48 (plus bfloat16)."""
     if device_type not in ("cpu", "cuda"):
         raise ValueError("autocast device_type must be 'cuda' or 'cpu'.")
     if type(enabled) is not bool:
@@ -73,7 +73,7 @@ def autocast(device_type="cuda", dtype=torch.float16, enabled=True):
 
 
 def autocast_dtype(operation, *operands):
-    """The low-precision dtype an operation runs in under autocast, or None (namitorch/amp.py:175-185)."""
+    """The low-precision dtype an operation runs in under autocast, or None (namitorch/amp.py:51-61)."""
     enabled, dtype = _autocast_state.get()
     values = tuple(v for v in operands if v is not None)
     if not enabled or OPERATION_POLICIES.get(operation) != "low" or not values:
@@ -84,7 +84,7 @@ def autocast_dtype(operation, *operands):
 
 
 def float32_function(function):
-    """Promotes float16 / bfloat16 tensor arguments to float32 (namitorch/amp.py:188-199)."""
+    """Promotes float16 / bfloat16 tensor arguments to float32 (namitorch/amp.py:64-75)."""
     if OPERATION_POLICIES.get(function.__name__) != "float32":
         raise ValueError(f"No float32 policy for {function.__name__}.")
 
@@ -129,7 +129,7 @@ class GradScaler:
     _MAX_SCALE = float(np.finfo(np.float32).max)
 
     def __init__(self, init_scale=65536.0, growth_factor=2.0, backoff_factor=0.5, growth_interval=2000, enabled=True):
-        """namitorch/amp.py:206-224."""
+        """namitorch/amp.py:82-100."""
         if type(enabled) is not bool:
             raise TypeError("GradScaler enabled must be a Python bool.")
         self._init_value = self._scale_value(init_scale)
@@ -165,7 +165,7 @@ class GradScaler:
 
     @classmethod
     def _scale_value(cls, value):
-        """namitorch/amp.py:238-243."""
+        """namitorch/amp.py:115-119."""
         scale = cls._real(value, "scale")
         if not cls._MIN_SCALE <= scale <= cls._MAX_SCALE:
             raise ValueError(f"scale must be between {cls._MIN_SCALE} and {cls._MAX_SCALE}.")
@@ -195,7 +195,7 @@ class GradScaler:
         return float(self._scale_dev.item())
 
     def scale(self, loss):
-        """namitorch/amp.py:251-264: loss * scale, on the device."""
+        """namitorch/amp.py:127-140: loss * scale, on the device."""
         if not isinstance(loss, torch.Tensor) or not loss.dtype.is_floating_point:
             raise TypeError("GradScaler.scale requires a floating NamiTorch Tensor.")
         if not self._enabled:
@@ -232,7 +232,7 @@ class GradScaler:
         return gradients
 
     def unscale_(self, optimizer):
-        """namitorch/amp.py:293-318."""
+        """namitorch/amp.py:169-194."""
         if not self._enabled:
             return True
         if not self._scale_used:
@@ -256,7 +256,7 @@ class GradScaler:
         return DeviceFlag(stats[N.STATS_FIELDS.index("found_inf")], invert=True)
 
     def step(self, optimizer):
-        """namitorch/amp.py:320-341; the skip decision stays on the device."""
+        """namitorch/amp.py:196-217; the skip decision stays on the device."""
         if not self._enabled:
             optimizer.step()
             return True
@@ -278,7 +278,7 @@ class GradScaler:
         return DeviceFlag(state["stats"][N.STATS_FIELDS.index("found_inf")], invert=True)
 
     def update(self):
-        """namitorch/amp.py:343-358 as one device kernel."""
+        """namitorch/amp.py:219-234 as one device kernel."""
         if not self._enabled:
             return
         if not self._optimizer_states or any(s["stage"] != "stepped" for s in self._optimizer_states.values()):
@@ -298,7 +298,7 @@ class GradScaler:
             raise RuntimeError("GradScaler state can be saved or loaded only between iterations, after update().")
 
     def state_dict(self):
-        """namitorch/amp.py:364-366 (host values; synchronises)."""
+        """namitorch/amp.py:240-242 (host values; synchronises)."""
         self._ensure_idle()
         scale = self._init_value if self._scale_dev is None else float(self._scale_dev.item())
         tracker = self._init_tracker if self._tracker_dev is None else int(self._tracker_dev.item())
@@ -306,7 +306,7 @@ class GradScaler:
                     growth_interval=self._growth_interval, enabled=self._enabled, growth_tracker=tracker)
 
     def load_state_dict(self, state):
-        """namitorch/amp.py:368-383."""
+        """namitorch/amp.py:244-262."""
         self._ensure_idle()
         if type(state) is not dict or set(state) != {"version", "scale", "growth_factor", "backoff_factor",
                                                      "growth_interval", "enabled", "growth_tracker"}:

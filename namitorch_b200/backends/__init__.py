@@ -1,7 +1,7 @@
 """Backend seam: the fused-kernel switch and the per-device CUDA backend object.
 
 Mirrors namitorch/backends/__init__.py:32-48 (``get_backend``) and
-namitorch/backends/_settings.py:1-14 (``enable_fused_kernels``). This build has one backend,
+namitorch/backends/_settings.py:1-12 (``enable_fused_kernels``). This build has one backend,
 CUDA on sm_100a; asking for a CPU backend raises instead of falling back to NumPy.
 """
 from __future__ import annotations

@@ -1,6 +1,6 @@
 """GradScaler arithmetic and the AMP optimizer step, restated — TEST INFRASTRUCTURE ONLY.
 
-Follows ``GradScaler`` (namitorch/amp.py:202-383): ``_scale_value`` (:238-243),
+Follows ``GradScaler`` (namitorch/amp.py:78-262): ``_scale_value`` (:238-243),
 ``unscale_`` (:293-318: g = f32(g) / scale written back in the gradient dtype),
 ``_finite`` (:276-291), ``step`` (:320-341) and ``update`` (:343-358), plus the training
 loop order of namitorch/training/runner.py:247-254 (unscale_, clip only when finite,
@@ -65,7 +65,7 @@ def amp_step(optimizer: OracleAdamW, scaler: OracleGradScaler, grads: list[np.nd
 
     ``storage`` (float32 array -> float32 array) models gradients that live in a narrower
     dtype: ``unscale_`` and ``clip_grad_norm_`` write their results back into the gradient
-    tensors in place (amp.py:310-315, clip_grad.py:106-111), so each result is rounded to
+    tensors in place (amp.py:186-191, clip_grad.py:106-111), so each result is rounded to
     that dtype before the next operation reads it (e.g. ``casts.round_to_bf16``).
 
     ``given_norm`` is passed to ``clip.clip_grad_norm_`` as the norm to clip with.

@@ -7,7 +7,7 @@ applies the chain the reference autograd builds: mean / sum reduction, label smo
 (confidence * loss + epsilon * smooth), class weights, the gather backward and the
 log_softmax backward ``g - exp(out) * sum(g)`` with all-(-inf) rows zeroed
 (namitorch/autograd.py:538-564). Everything is float32, as under ``float32_function``
-(namitorch/amp.py:188-199).
+(namitorch/amp.py:64-75).
 """
 from __future__ import annotations
 

@@ -35,5 +35,14 @@ def cuda_device():
     return torch.device("cuda", 0)
 
 
+def reference_root() -> Path | None:
+    """The reference checkout (renderityai/NamiTorch): $NAMITORCH_REFERENCE, else a
+    checkout named ``reference`` beside this repository; None when neither holds the
+    ``namitorch`` package."""
+    env = os.environ.get("NAMITORCH_REFERENCE")
+    root = Path(env) if env else REPO.parent / "reference"
+    return root if (root / "namitorch").is_dir() else None
+
+
 def reference_available() -> bool:
-    return Path(os.environ.get("NAMITORCH_REFERENCE", "/root/reference"), "namitorch").is_dir()
+    return reference_root() is not None

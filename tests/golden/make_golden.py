@@ -15,6 +15,7 @@ Usage (needs the reference checkout; not run by the tests):
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import json
 import sys
@@ -305,7 +306,9 @@ def xent_cases(ref) -> tuple[dict, dict]:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("reference", nargs="?", default="/root/reference")
+    parser.add_argument("reference", nargs="?", default=os.environ.get("NAMITORCH_REFERENCE",
+                                                                       str(REPO.parent / "reference")),
+                        help="reference checkout (default: $NAMITORCH_REFERENCE, else ../reference beside this repo)")
     parser.add_argument("--full", action="store_true")
     args = parser.parse_args()
     ref = load_reference(args.reference)
