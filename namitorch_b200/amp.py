@@ -83,6 +83,19 @@ def autocast_dtype(operation, *operands):
     return dtype
 
 
+def autocast_operands(operation, *operands):
+    """The operands an operation computes with under autocast (namitorch/nn/functional.py:57-60):
+    each non-None operand converted to ``autocast_dtype(operation, ...)`` when that is not None,
+    else returned as given. A conversion to the dtype a tensor already has returns the tensor
+    itself, so the parameters of an optimizer built with ``model_dtype`` (views of its
+    persistent low-precision copy) pass through without the per-forward weight cast the
+    reference makes."""
+    dtype = autocast_dtype(operation, *operands)
+    if dtype is None:
+        return operands
+    return tuple(None if value is None else value.to(dtype) for value in operands)
+
+
 def float32_function(function):
     """Promotes float16 / bfloat16 tensor arguments to float32 (namitorch/amp.py:64-75)."""
     if OPERATION_POLICIES.get(function.__name__) != "float32":
@@ -329,4 +342,4 @@ class GradScaler:
             self._tracker_dev.fill_(tracker)
 
 
-__all__ = ["autocast", "autocast_dtype", "float32_function", "GradScaler", "DeviceFlag", "OPERATION_POLICIES"]
+__all__ = ["autocast", "autocast_dtype", "autocast_operands", "float32_function", "GradScaler", "DeviceFlag", "OPERATION_POLICIES"]

@@ -17,6 +17,30 @@ import numpy as np
 import torch
 
 from . import _native as N
+from .errors import NamiTorchCUDAOutOfMemoryError
+
+def arena(numel: int, dtype: torch.dtype, device) -> torch.Tensor:
+    """A zero-filled flat device buffer. An allocation failure raises the reference's
+    NamiTorchCUDAOutOfMemoryError (namitorch/backends/_cuda_memory.py:8-21) with the requested
+    bytes, the bytes the allocator holds (allocated / reserved) and the device's free / total
+    bytes, in place of torch's own out-of-memory error."""
+    try:
+        return torch.zeros(int(numel), dtype=dtype, device=device)
+    except torch.OutOfMemoryError as error:
+        raise out_of_memory(torch.device(device), int(numel) * torch.empty((), dtype=dtype).element_size()) from error
+
+
+def out_of_memory(device: torch.device, requested: int) -> NamiTorchCUDAOutOfMemoryError:
+    """The reference's out-of-memory error for a failed request of `requested` bytes."""
+    allocated = reserved = free = total = None
+    try:
+        allocated = int(torch.cuda.memory_allocated(device))
+        reserved = int(torch.cuda.memory_reserved(device))
+        free, total = (int(x) for x in torch.cuda.mem_get_info(device))
+    except Exception:   # the error still carries what could be read
+        pass
+    return NamiTorchCUDAOutOfMemoryError(str(device), requested, allocated, reserved, free, total)
+
 
 ALIGN = 64          # elements: every segment starts on a 256-byte boundary of an fp32 arena
 CHUNK = 8192        # elements per work chunk of the multi-tensor kernels

@@ -151,4 +151,35 @@ def cross_entropy(input: torch.Tensor, target: torch.Tensor, weight: torch.Tenso
     return loss.reshape(target.shape) if red == N.NT_REDUCTION_NONE else loss
 
 
-__all__ = ["cross_entropy", "softmax_cross_entropy"]
+def linear(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """``input @ weight.T + bias`` with the reference's checks and autocast rule
+    (namitorch/nn/functional.py:44-65): inside an enabled autocast context the operands are
+    converted to the autocast dtype (``amp.autocast_operands``), which for parameters held in
+    an optimizer's ``model_dtype`` copy is no conversion at all. Operands of different dtypes
+    outside autocast are promoted, as the reference's matmul promotes them. The product is a
+    library GEMM (torch / cuBLAS); it is not part of this package's kernels."""
+    from ..amp import autocast_operands
+    if not isinstance(input, torch.Tensor) or not isinstance(weight, torch.Tensor):
+        raise TypeError("linear input and weight must be NamiTorch Tensors.")
+    if weight.ndim != 2:
+        raise ValueError(f"linear weight must have rank 2, got shape {tuple(weight.shape)}.")
+    if input.ndim < 1 or input.shape[-1] != weight.shape[1]:
+        raise ValueError(f"linear input must have rank >= 1 and last dimension {weight.shape[1]}, got shape "
+                         f"{tuple(input.shape)}.")
+    if bias is not None:
+        if not isinstance(bias, torch.Tensor):
+            raise TypeError("linear bias must be a NamiTorch Tensor or None.")
+        if tuple(bias.shape) != (weight.shape[0],):
+            raise ValueError(f"linear bias must have shape {(weight.shape[0],)}, got {tuple(bias.shape)}.")
+    if weight.device != input.device or (bias is not None and bias.device != input.device):
+        raise RuntimeError("linear operands must be on the same device.")
+    input, weight, bias = autocast_operands("linear", input, weight, bias)
+    common = torch.promote_types(input.dtype, weight.dtype)
+    if bias is not None:
+        common = torch.promote_types(common, bias.dtype)
+    input, weight = input.to(common), weight.to(common)
+    bias = None if bias is None else bias.to(common)
+    return torch.nn.functional.linear(input, weight, bias)
+
+
+__all__ = ["cross_entropy", "linear", "softmax_cross_entropy"]
