@@ -22,6 +22,7 @@ import math
 import os
 import tempfile
 import zipfile
+from contextlib import contextmanager
 from numbers import Integral
 from pathlib import Path
 
@@ -115,30 +116,45 @@ def metadata_bytes(obj) -> tuple[bytes, list]:
     return encoded, arrays
 
 
-def save(obj, path) -> None:
-    """Writes `obj` as an archive at `path` (atomically: a temporary file, then a rename)."""
-    encoded, arrays = metadata_bytes(obj)
-    target = Path(path)
-    tmp_name = None
+@contextmanager
+def _replacing(target: Path):
+    """A temporary file beside `target`, open for writing. When the block ends normally it is
+    flushed to disk and renamed over `target` (readers see the old or the new archive, never
+    a partial one); when it raises, the temporary file is removed."""
+    handle, name = tempfile.mkstemp(dir=target.parent, prefix=f".{target.name}.", suffix=".tmp")
+    staged = Path(name)
     try:
-        with tempfile.NamedTemporaryFile("w+b", dir=target.parent, prefix=f".{target.name}.", suffix=".tmp",
-                                         delete=False) as out:
-            tmp_name = Path(out.name)
-            with zipfile.ZipFile(out, "w", compression=zipfile.ZIP_STORED, allowZip64=True) as archive:
-                archive.writestr("metadata.json", encoded)
-                with archive.open("arrays.npz", "w", force_zip64=True) as payload:
-                    with zipfile.ZipFile(payload, "w", compression=zipfile.ZIP_STORED, allowZip64=True) as npz:
-                        for ident, array in arrays:
-                            with npz.open(f"{ident}.npy", "w", force_zip64=True) as entry:
-                                np.lib.format.write_array(entry, np.array(array, copy=True, order="C"),
-                                                          version=(1, 0), allow_pickle=False)
+        with os.fdopen(handle, "w+b") as out:
+            yield out
             out.flush()
             os.fsync(out.fileno())
-        os.replace(tmp_name, target)
-        tmp_name = None
-    finally:
-        if tmp_name is not None:
-            tmp_name.unlink(missing_ok=True)
+        os.replace(staged, target)
+    except BaseException:
+        staged.unlink(missing_ok=True)
+        raise
+
+
+def _stored_zip(handle) -> zipfile.ZipFile:
+    """A ZIP writer without compression (the format stores every member as is)."""
+    return zipfile.ZipFile(handle, "w", compression=zipfile.ZIP_STORED, allowZip64=True)
+
+
+def _write_arrays(npz: zipfile.ZipFile, arrays) -> None:
+    """One NPY 1.0 member per array, from a C-ordered snapshot taken as it is written."""
+    for ident, array in arrays:
+        with npz.open(f"{ident}.npy", "w", force_zip64=True) as member:
+            np.lib.format.write_array(member, np.ascontiguousarray(array).copy(), version=(1, 0),
+                                      allow_pickle=False)
+
+
+def save(obj, path) -> None:
+    """Writes `obj` as an archive at `path`: metadata.json, then arrays.npz (itself a stored
+    ZIP of NPY members), replacing any previous file atomically."""
+    encoded, arrays = metadata_bytes(obj)
+    with _replacing(Path(path)) as out, _stored_zip(out) as archive:
+        archive.writestr("metadata.json", encoded)
+        with archive.open("arrays.npz", "w", force_zip64=True) as payload, _stored_zip(payload) as npz:
+            _write_arrays(npz, arrays)
 
 
 # ---- reading ---------------------------------------------------------------------------------

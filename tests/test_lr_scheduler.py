@@ -1,9 +1,11 @@
-"""Learning-rate schedulers on the host path, against the reference's own sequences.
+"""Learning-rate schedules on the host path, against the reference's own sequences.
 
 ``tests/golden/schedules.json`` holds the lr of both parameter groups after construction
 and after each of 40 steps for every scheduler class of the reference, with its final
-state_dict (``tests/golden/make_schedule_golden.py``). The host path and the oracle must
-reproduce every value bit for bit.
+state_dict (``tests/golden/make_schedule_golden.py``). WarmupCosine (built in) must
+reproduce its sequences bit for bit; every other reference scheduler runs through the
+generic ``Schedule`` with the oracle's restatement of its formula as ``lr_at``, which
+exercises the same stepping, state and table machinery. The oracle must match every case.
 """
 import json
 
@@ -27,8 +29,13 @@ def _optimizer():
 @pytest.mark.parametrize("case", CASES, ids=[f"{c['name']}-{i}" for i, c in enumerate(CASES)])
 def test_host_schedule_matches_reference_bit_for_bit(case):
     opt = _optimizer()
-    cls = getattr(lr_scheduler, case["name"])
-    sched = cls(opt, **case["config"], last_step=case["last_step"])
+    if case["name"] == "WarmupCosine":
+        sched = lr_scheduler.WarmupCosine(opt, **case["config"], last_step=case["last_step"])
+    else:
+        def lr_at(step, base, name=case["name"], config=case["config"]):
+            return O.lrs(name, step, [base], config)[0]
+        sched = lr_scheduler.Schedule(opt, lr_at, last_step=case["last_step"], name=case["name"],
+                                      config=case["config"])
     seq = [[float(g["lr"]).hex() for g in opt.param_groups]]
     for _ in range(40):
         sched.step()
@@ -64,10 +71,30 @@ def test_validation_follows_reference():
     with pytest.raises(ValueError, match="warmup_steps must be smaller"):
         lr_scheduler.WarmupCosine(_optimizer(), warmup_steps=5, total_steps=5)
     with pytest.raises(ValueError, match="Minimum learning rate"):
-        lr_scheduler.CosineAnnealingLR(_optimizer(), T_max=3, eta_min=1.0)
-    with pytest.raises(TypeError, match="step_size must be an integer"):
-        lr_scheduler.StepLR(_optimizer(), step_size=1.5)
-    with pytest.raises(TypeError, match="milestones"):
-        lr_scheduler.MultiStepLR(_optimizer(), milestones={1, 2})
+        lr_scheduler.WarmupCosine(_optimizer(), warmup_steps=1, total_steps=3, min_lr=1.0)
+    with pytest.raises(TypeError, match="warmup_steps must be an integer"):
+        lr_scheduler.WarmupCosine(_optimizer(), warmup_steps=1.5, total_steps=3)
+    with pytest.raises(ValueError, match="total_steps must be at least 1"):
+        lr_scheduler.WarmupCosine(_optimizer(), warmup_steps=0, total_steps=0)
+    with pytest.raises(ValueError, match="min_lr must be finite and nonnegative"):
+        lr_scheduler.WarmupCosine(_optimizer(), warmup_steps=0, total_steps=2, min_lr=-1.0)
     with pytest.raises(TypeError, match="NamiTorch Optimizer"):
-        lr_scheduler.StepLR(object(), step_size=1)
+        lr_scheduler.WarmupCosine(object(), warmup_steps=0, total_steps=2)
+    with pytest.raises(TypeError, match="lr_at must be a callable"):
+        lr_scheduler.Schedule(_optimizer(), 0.5)
+
+
+def test_state_loads_only_into_the_same_schedule():
+    sched = lr_scheduler.WarmupCosine(_optimizer(), warmup_steps=2, total_steps=9)
+    sched.step()
+    state = sched.state_dict()
+    other = lr_scheduler.Schedule(_optimizer(), lambda step, base: base)
+    with pytest.raises(ValueError, match="does not match"):
+        other.load_state_dict(state)
+    bad = dict(state, config={"warmup_steps": 9, "total_steps": 9, "min_lr": 0.0})
+    target = lr_scheduler.WarmupCosine(_optimizer(), warmup_steps=2, total_steps=9)
+    with pytest.raises(ValueError, match="warmup_steps must be smaller"):
+        target.load_state_dict(bad)
+    assert target.config == {"warmup_steps": 2, "total_steps": 9, "min_lr": 0.0} and target.last_step == 0
+    target.load_state_dict(state)
+    assert target.last_step == 1 and target.get_last_lr() == sched.get_last_lr()
