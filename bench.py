@@ -525,6 +525,7 @@ def run_ours(args):
     if world == 1:
         result["loop"] = loop_tail(args, opt, scaler, params, loss)
         result["captured"] = captured_tail(opt, scaler, params, loss)
+        result["step_parity"] = single_parity(opt, scaler, params, loss)
     if not args.no_e2e:
         result["e2e"] = e2e_ours(args, opt, scaler, params, flat_grads, loss, world)
     if world > 1:
@@ -729,6 +730,45 @@ def zero_parity(opt, scaler, params, loss) -> dict:
     return {"copies_equal": bool(same), "reduce_bit_exact": reduce_bad == 0, "shard_bit_exact": shard_bad == 0,
             "mismatches": reduce_bad + shard_bad, "elements_checked": checked, "stepped": bool(stepped_all),
             "checker": checker, "copy_sha256": digests[0][:16]}
+
+
+def single_parity(opt, scaler, params, loss, count: int = 1 << 16) -> dict:
+    """One more single-GPU step after the timed region, checked on a seeded slice of `count`
+    elements of the largest parameter: master / exp_avg / exp_avg_sq after the step must equal
+    what the reference's own AdamW(fused=False) (baseline/_ref) computes from the pre-step
+    state and gradient, after the reference's unscale and clip multiply with the step's norm;
+    and the bf16 model copy must be the round-to-nearest-even of the new master."""
+    import torch
+    from namitorch_b200.optim import clip_grad_norm_
+    engine = opt._engine
+    i = max(range(len(engine.params)), key=lambda k: engine.params[k].numel())
+    prm = engine.params[i]
+    n = min(count, prm.numel())
+    start = int(np.random.default_rng(7).integers(0, prm.numel() - n + 1))
+    views = [engine.master_view(i), engine.view(engine.exp_avg, i), engine.view(engine.exp_avg_sq, i)]
+    with torch.no_grad():
+        pre = [v.reshape(-1)[start:start + n].cpu().numpy().copy() for v in views]
+        grad = prm.grad.reshape(-1)[start:start + n].float().cpu().numpy()
+        step_count = int(engine.steps[i].item())
+    scale = scaler.get_scale()
+    scaler.scale(loss)
+    finite = scaler.unscale_(opt)
+    norm_t = clip_grad_norm_(params, 1.0)
+    scaler.step(opt)
+    scaler.update()
+    torch.cuda.synchronize()
+    stepped = bool(finite)
+    with torch.no_grad():
+        post = [v.reshape(-1)[start:start + n].cpu().numpy().copy() for v in views]
+        copy_bits = prm.detach().reshape(-1)[start:start + n].view(torch.int16).cpu().numpy()
+    group = next(g for g in opt.param_groups if any(q is prm for q in g["params"]))
+    expect, checker = _shard_reference(pre, grad, scale, float(norm_t.item()), step_count, group, stepped,
+                                       prm.device)
+    bad = sum(int(np.count_nonzero(a.view(np.uint32) != b.view(np.uint32))) for a, b in zip(post, expect))
+    want_copy = torch.from_numpy(post[0]).to(torch.bfloat16).view(torch.int16).numpy()
+    copy_bad = int(np.count_nonzero(want_copy != copy_bits))
+    return {"bit_exact": bad == 0 and copy_bad == 0, "mismatches": bad, "copy_mismatches": copy_bad,
+            "elements_checked": n, "parameter_index": i, "stepped": stepped, "checker": checker}
 
 
 def _shard_reference(pre, reduced, scale, norm, step_count, group, stepped, device):

@@ -1,0 +1,46 @@
+"""The checker bench.py runs after its timed region (the reference's own AdamW from the
+baseline/_ref install, fed the unscaled and clipped gradient) agrees with the oracle's
+restatement bit for bit, with and without a prior state and for both weight-decay groups.
+Skipped when the reference install is absent."""
+import numpy as np
+import pytest
+
+from conftest import REPO
+
+import bench
+from oracle import adamw as oadamw
+
+
+@pytest.fixture(scope="module")
+def reference_install():
+    if bench.load_reference_package() is None:
+        pytest.skip("baseline/_ref (the reference install) is not present")
+
+
+@pytest.mark.parametrize("step_count,wd,norm", [(0, 0.1, 3.5), (7, 0.0, 0.25), (40, 0.1, 1.0 - 1e-6)])
+def test_shard_checker_matches_oracle(reference_install, step_count, wd, norm):
+    rng = np.random.default_rng(step_count)
+    n = 4099
+    pre = [rng.normal(0, 0.02, n).astype(np.float32), rng.normal(0, 1e-3, n).astype(np.float32),
+           np.abs(rng.normal(0, 1e-6, n)).astype(np.float32)]
+    if step_count == 0:
+        pre[1][:] = 0
+        pre[2][:] = 0
+    reduced = (rng.normal(0, 1e-3, n) * 65536).astype(np.float32)
+    group = {"lr": 3e-4, "betas": (0.9, 0.999), "eps": 1e-8, "weight_decay": wd}
+    got, checker = bench._shard_reference(pre, reduced, 65536.0, norm, step_count, group, True, "cpu")
+    assert checker.startswith("reference AdamW")
+    g = (reduced / np.float32(65536.0)).astype(np.float32)
+    coef = 1.0 / (norm + 1e-6)
+    if coef < 1:
+        g = (g.astype(np.float64) * coef).astype(np.float32)
+    p, m, v = (a.copy() for a in pre)
+    oadamw.adam_update(p, g, m, v, step_count, lr=3e-4, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=wd)
+    for ours, want in zip(got, (p, m, v)):
+        np.testing.assert_array_equal(np.asarray(ours).view(np.uint32), want.view(np.uint32))
+
+
+def test_skipped_step_expects_the_state_unchanged(reference_install):
+    pre = [np.arange(5, dtype=np.float32)] * 3
+    got, checker = bench._shard_reference(pre, np.ones(5, np.float32), 2.0, 1.0, 3, {}, False, "cpu")
+    assert checker.startswith("skipped") and all(np.array_equal(a, b) for a, b in zip(got, pre))
