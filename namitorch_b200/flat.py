@@ -19,7 +19,7 @@ import torch
 from . import _native as N
 from .errors import NamiTorchCUDAOutOfMemoryError
 
-def arena(numel: int, dtype: torch.dtype, device) -> torch.Tensor:
+def zeroed_arena(numel: int, dtype: torch.dtype, device) -> torch.Tensor:
     """A zero-filled flat device buffer. An allocation failure raises the reference's
     NamiTorchCUDAOutOfMemoryError (namitorch/backends/_cuda_memory.py:8-21) with the requested
     bytes, the bytes the allocator holds (allocated / reserved) and the device's free / total

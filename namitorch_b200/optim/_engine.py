@@ -15,7 +15,7 @@ import numpy as np
 import torch
 
 from .. import _native as N
-from ..flat import CHUNK, FlatLayout, arena, segment_table, upload
+from ..flat import CHUNK, FlatLayout, segment_table, upload, zeroed_arena
 from ._common import _scalar
 
 
@@ -92,11 +92,11 @@ class FusedAdamEngine:
         self.model_dtype = model_dtype
         total = self.layout.total
         with torch.no_grad(), torch.cuda.device(device):
-            self.master = arena(total, torch.float32, device)
+            self.master = zeroed_arena(total, torch.float32, device)
             for p, off in zip(self.params, self.layout.offsets):
                 self.master[off:off + p.numel()].copy_(p.detach().reshape(-1))
             if model_dtype is not None:
-                self.copy = arena(total, model_dtype, device)
+                self.copy = zeroed_arena(total, model_dtype, device)
                 N.call("nt_cast", self.copy.data_ptr(), N.dtype_code(model_dtype), self.master.data_ptr(),
                        N.NT_F32, total, N.stream_handle())
             else:
@@ -134,8 +134,8 @@ class FusedAdamEngine:
     def ensure_moments(self) -> None:
         if self.exp_avg is None:
             with torch.cuda.device(self.device):
-                self.exp_avg = arena(self.master.numel(), torch.float32, self.device)
-                self.exp_avg_sq = arena(self.master.numel(), torch.float32, self.device)
+                self.exp_avg = zeroed_arena(self.master.numel(), torch.float32, self.device)
+                self.exp_avg_sq = zeroed_arena(self.master.numel(), torch.float32, self.device)
 
     @property
     def grad_dtype(self) -> torch.dtype:

@@ -40,7 +40,7 @@ import torch
 import torch.distributed as dist
 
 from . import _native as N
-from .flat import ALIGN, CHUNK, FlatLayout, arena, round_up, segment_table, span_table, stats_tensor, upload
+from .flat import ALIGN, CHUNK, FlatLayout, round_up, segment_table, span_table, stats_tensor, upload, zeroed_arena
 from .optim._engine import CorrectionTable
 from .optim.adam import _AmpPending, _FirstOrderAdam, _OWNERS
 from .optim._common import _scalar
@@ -214,10 +214,10 @@ class ZeroAdamW(_FirstOrderAdam):
         shard = self._pieces * c
         self.pieces = shard_pieces(offsets, numels, self.ranges)
         with torch.no_grad():
-            self.copy = arena(total, self._copy_dtype, device)
-            self.flat_grads = arena(total, self._copy_dtype, device)
-            self.grad_shard = arena(shard, self._copy_dtype, device)
-            self.master = arena(shard, torch.float32, device)
+            self.copy = zeroed_arena(total, self._copy_dtype, device)
+            self.flat_grads = zeroed_arena(total, self._copy_dtype, device)
+            self.grad_shard = zeroed_arena(shard, self._copy_dtype, device)
+            self.master = zeroed_arena(shard, torch.float32, device)
             for i, off, n, j in self.pieces:
                 src = params[i].detach().reshape(-1)
                 lo = self._global(off) - self.layout.offsets[i]
@@ -229,8 +229,8 @@ class ZeroAdamW(_FirstOrderAdam):
             for p, off, view in zip(params, self.layout.offsets, views):
                 p.data = self.copy[off:off + p.numel()].view(p.shape)
                 p.grad = view
-            self.exp_avg = arena(shard, torch.float32, device)
-            self.exp_avg_sq = arena(shard, torch.float32, device)
+            self.exp_avg = zeroed_arena(shard, torch.float32, device)
+            self.exp_avg_sq = zeroed_arena(shard, torch.float32, device)
             self.steps = torch.zeros(len(params), dtype=torch.int32, device=device)
         # Gradient buffers: [0] is flat_grads; add_gradient_buffer adds more (double buffering).
         self.gradient_buffers = [self.flat_grads]
@@ -319,7 +319,7 @@ class ZeroAdamW(_FirstOrderAdam):
         ``use_gradient_buffer``: a data loader can fill one buffer while a step reduces the
         other."""
         with torch.no_grad():
-            buf = arena(self.flat_grads.numel(), self.flat_grads.dtype, self.device)
+            buf = zeroed_arena(self.flat_grads.numel(), self.flat_grads.dtype, self.device)
         self.gradient_buffers.append(buf)
         self._buffer_views.append([buf[off:off + p.numel()].view(p.shape)
                                    for p, off in zip(self.params_list, self.layout.offsets)])

@@ -114,7 +114,7 @@ def test_arena_out_of_memory_raises_the_reference_error(monkeypatch):
 
     monkeypatch.setattr(flat.torch, "zeros", failing)
     with pytest.raises(NamiTorchCUDAOutOfMemoryError) as info:
-        flat.arena(1 << 20, torch.float32, "cpu")
+        flat.zeroed_arena(1 << 20, torch.float32, "cpu")
     assert info.value.requested_bytes == 4 << 20
     assert "requested=4194304 bytes" in str(info.value)
     assert isinstance(info.value, MemoryError)
@@ -151,7 +151,7 @@ def test_arena_larger_than_the_device_raises_the_reference_error(cuda_device):
     from namitorch_b200 import flat
     total = torch.cuda.mem_get_info(cuda_device)[1]
     with pytest.raises(NamiTorchCUDAOutOfMemoryError) as info:
-        flat.arena(4 * total, torch.float32, cuda_device)
+        flat.zeroed_arena(4 * total, torch.float32, cuda_device)
     err = info.value
     assert err.requested_bytes == 16 * total
     assert err.total_bytes == total and err.free_bytes is not None and err.free_bytes <= total
