@@ -523,9 +523,10 @@ def run_ours(args):
         result["zero1_breakdown_ms"] = breakdown
         result["nvlink"] = nvlink_section(opt, P, world, ms, breakdown)
     if world == 1:
+        # Before the loop measurements below attach a learning-rate schedule to the optimizer.
+        result["step_parity"] = single_parity(opt, scaler, params, loss)
         result["loop"] = loop_tail(args, opt, scaler, params, loss)
         result["captured"] = captured_tail(opt, scaler, params, loss)
-        result["step_parity"] = single_parity(opt, scaler, params, loss)
     if not args.no_e2e:
         result["e2e"] = e2e_ours(args, opt, scaler, params, flat_grads, loss, world)
     if world > 1:
