@@ -647,10 +647,19 @@ def nvlink_section(opt, P: int, world: int, ms: float, breakdown: dict) -> dict:
     link_bytes = 2.0 * P * (world - 1) / world          # per phase, per GPU and direction
     bw = measure_peer_bandwidth(world, opt.rank, opt.device)
     floor_ms = (link_bytes / (bw["pull_gbs"] * 1e9) + link_bytes / (bw["push_gbs"] * 1e9)) * 1e3
+    # With HBM: the reduce-scatter phase reads the local shard and serves the peers' pulls
+    # (2 B x P/N x N) and writes the reduced shard (2 B x P/N); the update phase moves 28 B per
+    # shard parameter plus the peers' pushed copies (2 B x P/N x (N - 1)). Each phase takes the
+    # longer of its link time and its HBM time at the measured copy bandwidth.
+    hbm, _ = measured_peak()
+    shard = P / world
+    rs_ms = max(link_bytes / (bw["pull_gbs"] * 1e9), 2.0 * shard * (world + 1) / (hbm * 1e9)) * 1e3
+    up_ms = max(link_bytes / (bw["push_gbs"] * 1e9), (BYTES_UPDATE + 2.0 * (world - 1)) * shard / (hbm * 1e9)) * 1e3
     rs_gbs = link_bytes / (breakdown["reduce_scatter"] / 1e3) / 1e9
     push_gbs = link_bytes / (breakdown["update_with_overlapped_all_gather"] / 1e3) / 1e9
     return {"bytes_per_gpu_per_phase": link_bytes, "measured": bw,
             "floor_ms": floor_ms, "step_frac_of_floor": floor_ms / ms,
+            "floor_with_hbm_ms": rs_ms + up_ms, "step_frac_of_floor_with_hbm": (rs_ms + up_ms) / ms,
             "reduce_scatter_gbs": rs_gbs, "reduce_scatter_frac_of_pull": rs_gbs / bw["pull_gbs"],
             "update_push_gbs": push_gbs, "update_push_frac_of_push": push_gbs / bw["push_gbs"]}
 
