@@ -346,7 +346,7 @@ def group_params(shape, params, wd=0.1):
             {"params": [params[i] for i in no_decay], "weight_decay": 0.0}]
 
 
-def build_step(shape, device, rank, world, transport, seed_params=0):
+def build_step(shape, device, rank, world, transport, seed_params=0, exchange="flags"):
     """(optimizer, scaler, params, flat gradient buffer, loss, step function) of the AMP step
     on `shape`: AdamW (ZeroAdamW over the process group at N > 1) with a bf16 model copy and
     bf16 gradients N(0, 1e-3) x 65536, GradScaler(65536), clip_grad_norm_ 1.0."""
@@ -358,7 +358,7 @@ def build_step(shape, device, rank, world, transport, seed_params=0):
     if world > 1:
         from namitorch_b200.zero import ZeroAdamW
         opt = ZeroAdamW(group_params(shape, params), lr=3e-4, betas=(0.9, 0.999), eps=1e-8,
-                        model_dtype=torch.bfloat16, transport=transport)
+                        model_dtype=torch.bfloat16, transport=transport, exchange=exchange)
         flat_grads = opt.flat_grads
         with torch.no_grad():
             gen = torch.Generator(device=device)
@@ -501,7 +501,8 @@ def run_ours(args):
         "config": {"workload": f"{shape.name} AdamW+AMP step (BASELINE config 3; fp32 master/moments, bf16 grads "
                                "and model copy, GradScaler, clip_grad_norm_ 1.0, 2 param groups)",
                    "params": P, "tensors": len(params),
-                   "parallelism": f"zero1-dp{world}-{opt.transport}" if world > 1 else "single",
+                   "parallelism": (f"zero1-dp{world}-{opt.transport}" + ("-flags" if opt._uses_flags() else ""))
+                   if world > 1 else "single",
                    "l2": "inputs larger than L2 (30 B/param x 1.3B per step)", "grad_dtype": "bf16",
                    "model_dtype": "bf16"},
         "hbm_gbs_step": BYTES_STEP * shard / (ms / 1e3) / 1e9,
@@ -737,8 +738,11 @@ def zero_parity(opt, scaler, params, loss) -> dict:
     dist.all_reduce(mins, op=dist.ReduceOp.MIN)
     reduce_bad, shard_bad, checked = (int(x) for x in sums.tolist())
     same, stepped_all = (int(x) for x in mins.tolist())
+    errors = torch.tensor([opt.exchange_error()], dtype=torch.int32, device=device)
+    dist.all_reduce(errors, op=dist.ReduceOp.MAX)
     return {"copies_equal": bool(same), "reduce_bit_exact": reduce_bad == 0, "shard_bit_exact": shard_bad == 0,
             "mismatches": reduce_bad + shard_bad, "elements_checked": checked, "stepped": bool(stepped_all),
+            "exchange_errors": int(errors.item()), "exchange": opt._exchange if opt.transport == "p2p" else "nccl",
             "checker": checker, "copy_sha256": digests[0][:16]}
 
 
@@ -819,17 +823,22 @@ def _shard_reference(pre, reduced, scale, norm, step_count, group, stepped, devi
 
 
 def nccl_comparison(shape, device, rank, world, steps: int = 10, warmup: int = 3) -> dict:
-    """The same ZeRO-1 step over the NCCL transport (reduce-scatter, statistics all-reduce,
-    per-piece update + all-gather on a side stream), timed the same way, for comparison with
-    the peer-memory kernels of the main line."""
+    """The same ZeRO-1 step two more ways, timed the same way, for comparison with the main
+    line (peer-memory kernels ordered by in-kernel flags): ``nccl`` is the NCCL transport
+    (reduce-scatter, statistics all-reduce, per-piece update + all-gather on a side stream);
+    ``p2p_nccl_barriers`` is the peer-memory kernels ordered by NCCL calls between them (two
+    4-byte all-reduce barriers and the statistics all-reduce)."""
     import torch
-    opt, scaler, params, flat_grads, loss, step = build_step(shape, device, rank, world, "nccl")
-    ms = device_timed(step, steps, warmup, world)
-    out = {"ms_per_step": ms, "value": shape.numel() / (ms / 1e3), "unit": "params/s", "steps": steps,
-           "warmup": warmup, "pieces": opt._pieces}
-    opt.close()
-    del opt, scaler, params, flat_grads, step
-    torch.cuda.empty_cache()
+    out = {}
+    for name, transport, exchange in (("nccl", "nccl", "flags"), ("p2p_nccl_barriers", "p2p", "nccl")):
+        opt, scaler, params, flat_grads, loss, step = build_step(shape, device, rank, world, transport,
+                                                                 exchange=exchange)
+        ms = device_timed(step, steps, warmup, world)
+        out[name] = {"ms_per_step": ms, "value": shape.numel() / (ms / 1e3), "unit": "params/s", "steps": steps,
+                     "warmup": warmup, "pieces": opt._pieces, "transport": opt.transport}
+        opt.close()
+        del opt, scaler, params, flat_grads, step
+        torch.cuda.empty_cache()
     return out
 
 

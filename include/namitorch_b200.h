@@ -468,6 +468,46 @@ int nt_zero_reduce_scatter_stats(const nt_zero_reduce_args* args, void* stream);
    copy into the update. `peer_copies` is a host array of device pointers. */
 int nt_adamw_mt_push(const nt_adamw_mt_args* args, void* const* peer_copies, int32_t num_peers, void* stream);
 
+/* Cross-GPU ordering of the two ZeRO-1 kernels without NCCL: every rank owns one mailbox in
+   its device memory (zero-filled once, exported with nt_ipc_export, mapped by the others);
+   ranks write epochs into each other's mailboxes and wait on their own. No counterpart in
+   the reference (it has no distributed code). */
+#define NT_ZERO_READY 0   /* the rank's gradients are final: its shard may be pulled */
+#define NT_ZERO_STATS 1   /* the rank's shard statistics are in stats[rank] */
+#define NT_ZERO_DONE 2    /* the rank's pushes have landed and its pulls have ended */
+typedef struct nt_zero_mailbox {
+  uint64_t flags[3][NT_MAX_RANKS];  /* flags[k][q]: the last epoch at which rank q signalled k */
+  double stats[NT_MAX_RANKS][4];    /* rank q's {sum g^2, #non-finite, #NaN, max|g|} of its shard */
+} nt_zero_mailbox;
+
+typedef struct nt_zero_sync {
+  nt_zero_mailbox* mailboxes[NT_MAX_RANKS]; /* rank-ordered: this rank's own and every peer's */
+  int32_t rank;
+  int32_t reserved;
+  uint64_t epoch;       /* this step's number: above every earlier one, the same on every rank */
+  uint64_t timeout_ns;  /* bound of every wait on another rank */
+  int32_t* error;       /* device word, sticky: |= 1 when a wait of the reduce-scatter ran out
+                           (the statistics then report found_inf, so the update skips), |= 2
+                           when the update's final wait ran out */
+} nt_zero_sync;
+
+/* nt_zero_reduce_scatter_stats plus the exchanges around it, in the same kernel: every rank
+   signals READY and waits for every other rank's READY (all gradients final) before
+   pulling; after the pull the last block sends the shard's statistics to every rank, waits
+   for everyone's, adds them in rank order and finalizes with `norm_type` (2 or inf): every
+   rank then holds the same global found_inf and norm, with no NCCL call. Every wait is
+   bounded by sync->timeout_ns. */
+int nt_zero_reduce_scatter_exchange(const nt_zero_reduce_args* args, const nt_zero_sync* sync, double norm_type,
+                                    void* stream);
+
+/* nt_adamw_mt_push followed, in the same kernel, by the closing exchange: once every block's
+   stores (its own copy and the peers') are complete, the last block signals DONE to every
+   rank and waits for everyone's DONE, so when the kernel ends every peer's push into this
+   rank's copy has landed and no peer still reads this rank's gradients. Launched even when
+   the shard holds no parameter, and when the GradScaler skips the step. */
+int nt_adamw_mt_push_exchange(const nt_adamw_mt_args* args, void* const* peer_copies, int32_t num_peers,
+                              const nt_zero_sync* sync, void* stream);
+
 /* No counterpart in the reference: copies `count` (1..NT_MAX_RANKS) independent ranges of
    `bytes_each` bytes (a multiple of 16; 16-byte aligned pointers), src[k] -> dst[k], with
    the plain 16-byte SM loads and stores that the two ZeRO-1 kernels above use (no copy

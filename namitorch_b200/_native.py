@@ -132,6 +132,18 @@ class ZeroReduceArgs(C.Structure):
                 ("stats", C.c_void_p), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
 
 
+NT_ZERO_READY, NT_ZERO_STATS, NT_ZERO_DONE = 0, 1, 2
+
+
+class ZeroMailbox(C.Structure):
+    _fields_ = [("flags", (C.c_uint64 * NT_MAX_RANKS) * 3), ("stats", (C.c_double * 4) * NT_MAX_RANKS)]
+
+
+class ZeroSync(C.Structure):
+    _fields_ = [("mailboxes", C.c_void_p * NT_MAX_RANKS), ("rank", C.c_int32), ("reserved", C.c_int32),
+                ("epoch", C.c_uint64), ("timeout_ns", C.c_uint64), ("error", C.c_void_p)]
+
+
 # name -> (restype, argtypes). Every symbol of include/namitorch_b200.h.
 SIGNATURES: dict[str, tuple] = {
     "nt_abi_version": (C.c_int, []),
@@ -170,6 +182,10 @@ SIGNATURES: dict[str, tuple] = {
     "nt_zero_reduce_scatter_stats": (C.c_int, [C.POINTER(ZeroReduceArgs), C.c_void_p]),
     "nt_adamw_mt_push": (C.c_int, [C.POINTER(AdamWMtArgs), C.POINTER(C.c_void_p), C.c_int32, C.c_void_p]),
     "nt_peer_copy": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int32, C.c_uint64, C.c_void_p]),
+    "nt_zero_reduce_scatter_exchange": (C.c_int, [C.POINTER(ZeroReduceArgs), C.POINTER(ZeroSync), C.c_double,
+                                                   C.c_void_p]),
+    "nt_adamw_mt_push_exchange": (C.c_int, [C.POINTER(AdamWMtArgs), C.POINTER(C.c_void_p), C.c_int32,
+                                            C.POINTER(ZeroSync), C.c_void_p]),
     "nt_row_softmax": (C.c_int, [C.POINTER(SoftmaxArgs), C.c_void_p]),
     "nt_norm_workspace_size": (C.c_size_t, [C.c_int64, C.c_int64]),
     "nt_norm_forward": (C.c_int, [C.POINTER(NormArgs), C.c_void_p]),
@@ -231,6 +247,7 @@ def check(status: int, what: str = "") -> None:
 # Kernel launches issued per successful call of each launching entry point (for the
 # benchmark's launch count; the statistics entry point launches one kernel per call).
 LAUNCHES_PER_CALL = {"nt_adamw_f32": 1, "nt_adamw_mt": 1, "nt_adamw_mt_push": 1, "nt_zero_reduce_scatter_stats": 1, "nt_peer_copy": 1,
+                     "nt_zero_reduce_scatter_exchange": 1, "nt_adamw_mt_push_exchange": 1,
                      "nt_grad_stats": 1, "nt_grad_stats_finalize": 1, "nt_schedule_step": 1, "nt_row_softmax": 1, "nt_norm_forward": 1,
                      "nt_grad_transform": 1, "nt_grad_clip_value": 1, "nt_scaler_update": 1,
                      "nt_softmax_xent": 2, "nt_xent_backward_scale": 1, "nt_cast": 1, "nt_fused_elementwise": 1}

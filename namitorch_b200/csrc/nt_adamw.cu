@@ -11,6 +11,7 @@
 // with c1 = f32(1-b1^t), c2 = f32(1-b2^t) computed on the host exactly as the reference.
 // A division by a correction that has reached exactly 1.0f is skipped (x / 1 == x).
 #include "nt_common.cuh"
+#include "nt_peer_sync.cuh"
 
 namespace nt {
 
@@ -126,6 +127,7 @@ struct MtParams {
   int sched_rows;
   int sched_cols;
   const int32_t* sched_step;
+  PeerSync sync;                     // the closing exchange (nt_adamw_mt_push_exchange only)
   nt_adamw_group groups[NT_MAX_GROUPS];
 };
 
@@ -195,10 +197,11 @@ __device__ __forceinline__ void mt_elem(const MtParams& P, int64_t ai, const voi
   }
 }
 
-template <int GDT, int CDT, bool PUSH>
+template <int GDT, int CDT, bool PUSH, bool SYNC>
 __global__ void __launch_bounds__(256) adamw_mt_kernel(const __grid_constant__ MtParams P) {
   __shared__ bool last;
-  if (P.stats != nullptr && P.skip_nonfinite && P.stats->found_inf != 0.0) return;  // GradScaler skip
+  const bool skip = P.stats != nullptr && P.skip_nonfinite && P.stats->found_inf != 0.0;   // GradScaler skip
+  if (!SYNC && skip) return;   // with SYNC the blocks still reach the closing exchange
   Unscale un;
   un.init(P.scale);
   bool clip = false;
@@ -219,7 +222,7 @@ __global__ void __launch_bounds__(256) adamw_mt_kernel(const __grid_constant__ M
   // chunks cross into the next segment.
   const int64_t per = (P.nchunks + gridDim.x - 1) / gridDim.x;
   const int64_t c0 = (int64_t)blockIdx.x * per;
-  const int64_t c1 = c0 + per < P.nchunks ? c0 + per : P.nchunks;
+  const int64_t c1 = skip ? c0 : (c0 + per < P.nchunks ? c0 + per : P.nchunks);
   int s = c0 < c1 ? find_owner([&](int i) { return P.segs[i].chunk_begin; }, P.nseg, c0) : 0;
   int64_t next_begin = -1;  // forces a load of segment s at the first chunk
   nt_segment seg{};
@@ -268,30 +271,59 @@ __global__ void __launch_bounds__(256) adamw_mt_kernel(const __grid_constant__ M
       mt_elem<GDT, CDT, PUSH>(P, abase + i, seg.grad, i, c, un, clip, coef);
   }
 
-  // The last block advances the step counter of every updated segment.
-  if (last_block_ticket(P.counter, &last)) {
-    for (int i = threadIdx.x; i < P.nseg; i += blockDim.x) {
-      const int slot = P.segs[i].step_slot;
-      if (slot >= 0) P.steps[slot] += 1;  // negative: another launch advances this counter
+  // The last block advances the step counter of every updated segment. With SYNC the ticket
+  // is taken at system scope (every block's stores, the pushes to the peers included, are
+  // then visible everywhere) and the last block closes the step: DONE to every rank, then
+  // a bounded wait for every rank's DONE.
+  if (SYNC ? last_block_ticket_sys(P.counter, &last) : last_block_ticket(P.counter, &last)) {
+    if (!skip) {
+      for (int i = threadIdx.x; i < P.nseg; i += blockDim.x) {
+        const int slot = P.segs[i].step_slot;
+        if (slot >= 0) P.steps[slot] += 1;  // negative: another launch advances this counter
+      }
     }
     __syncthreads();
-    if (threadIdx.x == 0) *P.counter = 0u;
+    if (threadIdx.x == 0) {
+      *P.counter = 0u;
+      if constexpr (SYNC) {
+        signal_all(P.sync, NT_ZERO_DONE);
+        if (!wait_all(P.sync, NT_ZERO_DONE)) atomicOr(P.sync.error, 2);
+      }
+    }
   }
 }
 
-template <int GDT, int CDT, bool PUSH>
+// The closing exchange alone, for a rank with nothing to update (an empty shard).
+__global__ void zero_done_kernel(const __grid_constant__ PeerSync S) {
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    signal_all(S, NT_ZERO_DONE);
+    if (!wait_all(S, NT_ZERO_DONE)) atomicOr(S.error, 2);
+  }
+}
+
+template <int GDT, int CDT, bool PUSH, bool SYNC = false>
 static int launch_mt(const MtParams& P, cudaStream_t stream) {
   static int per_sm = 0;
   if (per_sm == 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adamw_mt_kernel<GDT, CDT, PUSH>, 256, 0) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adamw_mt_kernel<GDT, CDT, PUSH, SYNC>, 256, 0) !=
+            cudaSuccess ||
         per_sm <= 0)
       per_sm = 2;
   }
   int64_t grid = (int64_t)current_sm_count() * per_sm;
   if (grid > P.nchunks) grid = P.nchunks;
   if (grid < 1) grid = 1;
-  adamw_mt_kernel<GDT, CDT, PUSH><<<(unsigned)grid, 256, 0, stream>>>(P);
+  adamw_mt_kernel<GDT, CDT, PUSH, SYNC><<<(unsigned)grid, 256, 0, stream>>>(P);
   return launch_status("nt_adamw_mt launch");
+}
+
+template <int GDT>
+static int dispatch_copy_sync(const MtParams& P, int copy_dtype, cudaStream_t stream) {
+  if (copy_dtype == NT_BF16) return launch_mt<GDT, NT_BF16, true, true>(P, stream);
+  if (copy_dtype == NT_F16) return launch_mt<GDT, NT_F16, true, true>(P, stream);
+  set_error("nt_adamw_mt_push_exchange: model copy dtype must be NT_F16 or NT_BF16 (got %d)", copy_dtype);
+  return NT_EUNSUPPORTED;
 }
 
 template <int GDT>
@@ -375,6 +407,39 @@ static int build_mt_params(const nt_adamw_mt_args* args, MtParams& P) {
   return NT_OK;
 }
 
+static int dispatch_mt_sync(const MtParams& P, const nt_adamw_mt_args& a, cudaStream_t s) {
+  switch (a.grad_dtype) {
+    case NT_F32: return dispatch_copy_sync<NT_F32>(P, a.model_dtype, s);
+    case NT_F16: return dispatch_copy_sync<NT_F16>(P, a.model_dtype, s);
+    case NT_BF16: return dispatch_copy_sync<NT_BF16>(P, a.model_dtype, s);
+    default:
+      set_error("nt_adamw_mt_push_exchange: unsupported gradient dtype %d", a.grad_dtype);
+      return NT_EUNSUPPORTED;
+  }
+}
+
+// Checks the peer copies of a push and stores them in P.
+static int set_push_peers(const nt_adamw_mt_args* args, void* const* peer_copies, int32_t num_peers, MtParams& P,
+                          const char* what) {
+  if (num_peers < 0 || num_peers > NT_MAX_RANKS - 1 || (num_peers > 0 && !peer_copies)) {
+    set_error("%s: num_peers must be in [0, %d] with a peer array (got %d)", what, NT_MAX_RANKS - 1, num_peers);
+    return NT_EINVAL;
+  }
+  if (num_peers > 0 && !args->model_copy) {
+    set_error("%s: peer copies need a model copy", what);
+    return NT_EINVAL;
+  }
+  for (int q = 0; q < num_peers; ++q) {
+    if (!peer_copies[q] || !aligned16(peer_copies[q])) {
+      set_error("%s: peer copy %d is NULL or not 16-byte aligned", what, q);
+      return NT_EINVAL;
+    }
+    P.peers[q] = peer_copies[q];
+  }
+  P.npeers = num_peers;
+  return NT_OK;
+}
+
 static int dispatch_mt(const MtParams& P, const nt_adamw_mt_args& a, cudaStream_t s) {
   switch (a.grad_dtype) {
     case NT_F32: return dispatch_copy<NT_F32>(P, a.model_dtype, s);
@@ -440,26 +505,35 @@ int nt_adamw_mt(const nt_adamw_mt_args* args, void* stream) {
 int nt_adamw_mt_push(const nt_adamw_mt_args* args, void* const* peer_copies, int32_t num_peers, void* stream) {
   nt::TraceRange trace("nt_adamw_mt_push");
   MtParams P;
-  const int rc = build_mt_params(args, P);
+  int rc = build_mt_params(args, P);
   if (rc != NT_OK || P.nchunks == 0) return rc;
-  if (num_peers < 0 || num_peers > NT_MAX_RANKS - 1 || (num_peers > 0 && !peer_copies)) {
-    set_error("nt_adamw_mt_push: num_peers must be in [0, %d] with a peer array (got %d)", NT_MAX_RANKS - 1,
-              num_peers);
-    return NT_EINVAL;
-  }
-  if (num_peers > 0 && !args->model_copy) {
-    set_error("nt_adamw_mt_push: peer copies need a model copy");
-    return NT_EINVAL;
-  }
-  for (int q = 0; q < num_peers; ++q) {
-    if (!peer_copies[q] || !aligned16(peer_copies[q])) {
-      set_error("nt_adamw_mt_push: peer copy %d is NULL or not 16-byte aligned", q);
-      return NT_EINVAL;
-    }
-    P.peers[q] = peer_copies[q];
-  }
-  P.npeers = num_peers;
+  rc = set_push_peers(args, peer_copies, num_peers, P, "nt_adamw_mt_push");
+  if (rc) return rc;
   return dispatch_mt(P, *args, as_stream(stream));
+}
+
+int nt_adamw_mt_push_exchange(const nt_adamw_mt_args* args, void* const* peer_copies, int32_t num_peers,
+                              const nt_zero_sync* sync, void* stream) {
+  nt::TraceRange trace("nt_adamw_mt_push_exchange");
+  const char* what = "nt_adamw_mt_push_exchange";
+  MtParams P;
+  int rc = build_mt_params(args, P);
+  if (rc != NT_OK) return rc;
+  if (num_peers < 0 || num_peers > NT_MAX_RANKS - 1) {
+    set_error("%s: num_peers must be in [0, %d] (got %d)", what, NT_MAX_RANKS - 1, num_peers);
+    return NT_EINVAL;
+  }
+  PeerSync S;
+  rc = build_peer_sync(sync, num_peers + 1, S, what);
+  if (rc) return rc;
+  if (P.nchunks == 0) {   // nothing to update on this rank: the closing exchange only
+    zero_done_kernel<<<1, 32, 0, as_stream(stream)>>>(S);
+    return launch_status("nt_adamw_mt_push_exchange launch");
+  }
+  rc = set_push_peers(args, peer_copies, num_peers, P, what);
+  if (rc) return rc;
+  P.sync = S;
+  return dispatch_mt_sync(P, *args, as_stream(stream));
 }
 
 }  // extern "C"

@@ -14,6 +14,7 @@
 #include <mutex>
 #include <unordered_map>
 
+#include "nt_peer_sync.cuh"
 #include "nt_stats.cuh"
 
 namespace nt {
@@ -29,6 +30,8 @@ struct ZeroReduceParams {
   const float* scale;
   nt_stats* stats;
   StatsWorkspace* ws;
+  PeerSync sync;      // used by the exchange variant only
+  double norm_type;   // exchange variant: 2 or inf
 };
 
 constexpr int kZeroThreads = kStatsThreads;
@@ -110,36 +113,150 @@ __device__ __forceinline__ void zero_reduce_body(const ZeroReduceParams& P, cons
   }
 }
 
-template <int DT, int NR>
+// The exchange variant's end: the block partials are reduced in a fixed order by the last
+// block, which sends the shard's totals to every rank's mailbox, waits for every rank's,
+// adds them in rank order (the same doubles in the same order on every rank, so every rank
+// finalizes the same found_inf and norm) and finalizes. If any wait ran out (READY in some
+// block, STATS here), the record reports found_inf with a NaN norm, so the update skips.
+__device__ __forceinline__ void zero_exchange_stats(const StatsAcc& a, const ZeroReduceParams& P) {
+  __shared__ double red_d[kZeroThreads / 32];
+  __shared__ float red_f[kZeroThreads / 32];
+  __shared__ unsigned red_u[kZeroThreads / 32];
+  __shared__ bool last;
+  double ss = block_reduce(a.ss0 + a.ss1, red_d, SumOp(), 0.0);
+  float mx = block_reduce(a.mx, red_f, MaxOp(), 0.0f);
+  unsigned nf = block_reduce(a.nf, red_u, SumOp(), 0u);
+  unsigned nn = block_reduce(a.nn, red_u, SumOp(), 0u);
+  if (threadIdx.x == 0) {
+    StatsPartial& out = P.ws->partials[blockIdx.x];
+    out.sumsq = ss; out.powsum = 0.0; out.maxabs = mx; out.nonfinite = nf; out.nan = nn;
+  }
+  if (!last_block_ticket(&P.ws->counter, &last)) return;
+  ss = 0.0; mx = 0.0f;
+  double nfd = 0.0, nnd = 0.0;
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
+    const StatsPartial q = P.ws->partials[b];
+    ss += q.sumsq; mx = fmaxf(mx, q.maxabs); nfd += q.nonfinite; nnd += q.nan;
+  }
+  ss = block_reduce(ss, red_d, SumOp(), 0.0);
+  nfd = block_reduce(nfd, red_d, SumOp(), 0.0);
+  nnd = block_reduce(nnd, red_d, SumOp(), 0.0);
+  mx = block_reduce(mx, red_f, MaxOp(), 0.0f);
+  if (threadIdx.x != 0) return;
+  const PeerSync& S = P.sync;
+  bool ok = *reinterpret_cast<volatile unsigned*>(&P.ws->pad[0]) == 0u;   // every block saw every rank READY
+  if (ok) {
+    for (int q = 0; q < S.nranks; ++q) {
+      double* slot = S.box[q]->stats[S.rank];
+      slot[0] = ss; slot[1] = nfd; slot[2] = nnd; slot[3] = (double)mx;
+    }
+    signal_all(S, NT_ZERO_STATS);   // the release orders the four stores above before it
+    ok = wait_all(S, NT_ZERO_STATS);
+  }
+  nt_stats* st = P.stats;
+  if (ok) {
+    const volatile nt_zero_mailbox* own = S.box[S.rank];
+    double gs = 0.0, gnf = 0.0, gnn = 0.0, gmx = 0.0;
+    for (int q = 0; q < S.nranks; ++q) {
+      gs += own->stats[q][0]; gnf += own->stats[q][1]; gnn += own->stats[q][2];
+      gmx = fmax(gmx, own->stats[q][3]);
+    }
+    st->sumsq = gs; st->nonfinite = gnf; st->nan = gnn; st->maxabs = gmx;
+    stats_finalize(st, P.norm_type);
+  } else {
+    atomicOr(S.error, 1);
+    const double nan = __longlong_as_double(0x7ff8000000000000ll);
+    st->sumsq = nan; st->nonfinite = 1.0; st->nan = 1.0; st->maxabs = nan; st->norm = nan; st->found_inf = 1.0;
+  }
+  P.ws->pad[0] = 0u;
+  P.ws->counter = 0u;
+}
+
+template <int DT, int NR, bool SYNC>
 __global__ void __launch_bounds__(kZeroThreads, 2) zero_reduce_stats_kernel(const __grid_constant__ ZeroReduceParams P) {
+  bool run = true;
+  if constexpr (SYNC) {
+    // Any block may run first, so every block signals READY (the same epoch) and waits for
+    // every rank's before it pulls. This rank's gradients were written by earlier kernels of
+    // its stream, so they are final when any block of this kernel runs.
+    __shared__ bool ready;
+    if (threadIdx.x == 0) {
+      signal_all(P.sync, NT_ZERO_READY);
+      ready = wait_all(P.sync, NT_ZERO_READY);
+      if (!ready) atomicOr(&P.ws->pad[0], 1u);
+    }
+    __syncthreads();
+    run = ready;
+  }
   Unscale un;
   un.init(P.scale);
   StatsAcc a{0.0, 0.0, 0.0, 0.0f, 0u, 0u};
-  if (!un.active) zero_reduce_body<DT, NR, kScaleNone>(P, un, a);
-  else if (un.pow2) zero_reduce_body<DT, NR, kScaleMul>(P, un, a);
-  else zero_reduce_body<DT, NR, kScaleDiv>(P, un, a);
-  stats_reduce_pass0(a, P.ws, P.stats);
+  if (run) {
+    if (!un.active) zero_reduce_body<DT, NR, kScaleNone>(P, un, a);
+    else if (un.pow2) zero_reduce_body<DT, NR, kScaleMul>(P, un, a);
+    else zero_reduce_body<DT, NR, kScaleDiv>(P, un, a);
+  }
+  if constexpr (SYNC) zero_exchange_stats(a, P);
+  else stats_reduce_pass0(a, P.ws, P.stats);
 }
 
-template <int DT, int NR>
+template <int DT, int NR, bool SYNC>
 static int launch_zero_reduce(const ZeroReduceParams& P, cudaStream_t s) {
   int grid = current_sm_count() * 2;   // two 256-thread blocks per SM, 8 vectors in flight per thread
   if (grid > kStatsMaxBlocks) grid = kStatsMaxBlocks;
   const int64_t epv = DT == NT_F32 ? 4 : 8;
   const int64_t want = (P.count / epv + kZeroThreads - 1) / kZeroThreads;
   if (want < grid) grid = want > 0 ? (int)want : 1;
-  zero_reduce_stats_kernel<DT, NR><<<grid, kZeroThreads, 0, s>>>(P);
+  zero_reduce_stats_kernel<DT, NR, SYNC><<<grid, kZeroThreads, 0, s>>>(P);
   return launch_status("nt_zero_reduce_scatter_stats launch");
 }
 
-template <int DT>
+template <int DT, bool SYNC>
 static int dispatch_ranks(const ZeroReduceParams& P, cudaStream_t s) {
   switch (P.nranks) {
-    case 2: return launch_zero_reduce<DT, 2>(P, s);
-    case 4: return launch_zero_reduce<DT, 4>(P, s);
-    case 8: return launch_zero_reduce<DT, 8>(P, s);
-    default: return launch_zero_reduce<DT, 0>(P, s);
+    case 2: return launch_zero_reduce<DT, 2, SYNC>(P, s);
+    case 4: return launch_zero_reduce<DT, 4, SYNC>(P, s);
+    case 8: return launch_zero_reduce<DT, 8, SYNC>(P, s);
+    default: return launch_zero_reduce<DT, 0, SYNC>(P, s);
   }
+}
+
+template <bool SYNC>
+static int dispatch_dtype(const ZeroReduceParams& P, int dtype, cudaStream_t s, const char* what) {
+  switch (dtype) {
+    case NT_F32: return dispatch_ranks<NT_F32, SYNC>(P, s);
+    case NT_F16: return dispatch_ranks<NT_F16, SYNC>(P, s);
+    case NT_BF16: return dispatch_ranks<NT_BF16, SYNC>(P, s);
+    default:
+      set_error("%s: unsupported dtype %d", what, dtype);
+      return NT_EUNSUPPORTED;
+  }
+}
+
+// Checks an nt_zero_sync and copies it into the kernel's parameters.
+int build_peer_sync(const nt_zero_sync* sync, int nranks, PeerSync& S, const char* what) {
+  if (!sync) { set_error("%s: sync is NULL", what); return NT_EINVAL; }
+  if (sync->rank < 0 || sync->rank >= nranks) {
+    set_error("%s: rank %d outside [0, %d)", what, sync->rank, nranks);
+    return NT_EINVAL;
+  }
+  if (sync->epoch == 0 || sync->timeout_ns == 0 || !sync->error) {
+    set_error("%s: epoch and timeout_ns must be positive and error non-NULL", what);
+    return NT_EINVAL;
+  }
+  for (int q = 0; q < NT_MAX_RANKS; ++q) {
+    if (q < nranks && (!sync->mailboxes[q] || (reinterpret_cast<uintptr_t>(sync->mailboxes[q]) & 7u))) {
+      set_error("%s: mailbox %d is NULL or not 8-byte aligned", what, q);
+      return NT_EINVAL;
+    }
+    S.box[q] = q < nranks ? sync->mailboxes[q] : nullptr;
+  }
+  S.nranks = nranks;
+  S.rank = sync->rank;
+  S.epoch = sync->epoch;
+  S.timeout_ns = sync->timeout_ns;
+  S.error = sync->error;
+  return NT_OK;
 }
 
 
@@ -195,6 +312,44 @@ static GetAddressRangeFn address_range_fn() {
 // Pointer handed out by nt_ipc_open -> the mapping's base, which cudaIpcCloseMemHandle wants.
 static std::mutex g_ipc_lock;
 static std::unordered_map<void*, void*> g_ipc_bases;
+
+static int build_zero_reduce(const nt_zero_reduce_args* args, ZeroReduceParams& P, const char* what) {
+  if (!args) { set_error("%s: args is NULL", what); return NT_EINVAL; }
+  const nt_zero_reduce_args& a = *args;
+  if (a.num_ranks < 1 || a.num_ranks > NT_MAX_RANKS) {
+    set_error("%s: num_ranks must be in [1, %d] (got %d)", what, NT_MAX_RANKS, a.num_ranks);
+    return NT_EINVAL;
+  }
+  if (a.count < 0) { set_error("%s: negative count", what); return NT_EINVAL; }
+  if (!a.stats || !a.workspace || (a.count > 0 && !a.dest)) {
+    set_error("%s: NULL dest/stats/workspace", what);
+    return NT_EINVAL;
+  }
+  if (a.workspace_bytes < sizeof(StatsWorkspace)) {
+    set_error("%s: workspace needs %zu bytes (got %zu)", what, sizeof(StatsWorkspace), a.workspace_bytes);
+    return NT_EINVAL;
+  }
+  if (!aligned16(a.dest)) { set_error("%s: dest must be 16-byte aligned", what); return NT_EINVAL; }
+  for (int q = 0; q < a.num_ranks && a.count > 0; ++q) {   // an empty shard reads nothing
+    if (!a.sources[q] || !aligned16(a.sources[q])) {
+      set_error("%s: source %d is NULL or not 16-byte aligned", what, q);
+      return NT_EINVAL;
+    }
+  }
+  for (int q = 0; q < NT_MAX_RANKS; ++q) P.src[q] = q < a.num_ranks ? a.sources[q] : a.sources[0];
+  P.nranks = a.num_ranks;
+  P.count = a.count;
+  P.average = a.average != 0;
+  P.n_f = (float)a.num_ranks;
+  P.inv_n = (a.num_ranks & (a.num_ranks - 1)) == 0 ? 1.0f / (float)a.num_ranks : 0.0f;
+  P.dst = a.dest;
+  P.scale = a.scale;
+  P.stats = a.stats;
+  P.ws = static_cast<StatsWorkspace*>(a.workspace);
+  P.norm_type = 2.0;
+  memset(&P.sync, 0, sizeof(P.sync));
+  return NT_OK;
+}
 
 }  // namespace nt
 
@@ -266,49 +421,27 @@ int nt_can_access_peer(int32_t peer, int32_t* ok) {
 
 int nt_zero_reduce_scatter_stats(const nt_zero_reduce_args* args, void* stream) {
   nt::TraceRange trace("nt_zero_reduce_scatter_stats");
-  if (!args) { set_error("nt_zero_reduce_scatter_stats: args is NULL"); return NT_EINVAL; }
-  const nt_zero_reduce_args& a = *args;
-  if (a.num_ranks < 1 || a.num_ranks > NT_MAX_RANKS) {
-    set_error("nt_zero_reduce_scatter_stats: num_ranks must be in [1, %d] (got %d)", NT_MAX_RANKS, a.num_ranks);
-    return NT_EINVAL;
-  }
-  if (a.count < 0) { set_error("nt_zero_reduce_scatter_stats: negative count"); return NT_EINVAL; }
-  if (!a.stats || !a.workspace || (a.count > 0 && !a.dest)) {
-    set_error("nt_zero_reduce_scatter_stats: NULL dest/stats/workspace");
-    return NT_EINVAL;
-  }
-  if (a.workspace_bytes < sizeof(StatsWorkspace)) {
-    set_error("nt_zero_reduce_scatter_stats: workspace needs %zu bytes (got %zu)", sizeof(StatsWorkspace),
-              a.workspace_bytes);
-    return NT_EINVAL;
-  }
-  if (!aligned16(a.dest)) { set_error("nt_zero_reduce_scatter_stats: dest must be 16-byte aligned"); return NT_EINVAL; }
-  for (int q = 0; q < a.num_ranks && a.count > 0; ++q) {   // an empty shard reads nothing
-    if (!a.sources[q] || !aligned16(a.sources[q])) {
-      set_error("nt_zero_reduce_scatter_stats: source %d is NULL or not 16-byte aligned", q);
-      return NT_EINVAL;
-    }
-  }
   ZeroReduceParams P;
-  for (int q = 0; q < NT_MAX_RANKS; ++q) P.src[q] = q < a.num_ranks ? a.sources[q] : a.sources[0];
-  P.nranks = a.num_ranks;
-  P.count = a.count;
-  P.average = a.average != 0;
-  P.n_f = (float)a.num_ranks;
-  P.inv_n = (a.num_ranks & (a.num_ranks - 1)) == 0 ? 1.0f / (float)a.num_ranks : 0.0f;
-  P.dst = a.dest;
-  P.scale = a.scale;
-  P.stats = a.stats;
-  P.ws = static_cast<StatsWorkspace*>(a.workspace);
-  cudaStream_t s = as_stream(stream);
-  switch (a.dtype) {
-    case NT_F32: return dispatch_ranks<NT_F32>(P, s);
-    case NT_F16: return dispatch_ranks<NT_F16>(P, s);
-    case NT_BF16: return dispatch_ranks<NT_BF16>(P, s);
-    default:
-      set_error("nt_zero_reduce_scatter_stats: unsupported dtype %d", a.dtype);
-      return NT_EUNSUPPORTED;
+  int rc = build_zero_reduce(args, P, "nt_zero_reduce_scatter_stats");
+  if (rc) return rc;
+  return dispatch_dtype<false>(P, args->dtype, as_stream(stream), "nt_zero_reduce_scatter_stats");
+}
+
+int nt_zero_reduce_scatter_exchange(const nt_zero_reduce_args* args, const nt_zero_sync* sync, double norm_type,
+                                    void* stream) {
+  nt::TraceRange trace("nt_zero_reduce_scatter_exchange");
+  const char* what = "nt_zero_reduce_scatter_exchange";
+  ZeroReduceParams P;
+  int rc = build_zero_reduce(args, P, what);
+  if (rc) return rc;
+  if (!(norm_type == 2.0 || isinf(norm_type))) {
+    set_error("%s: norm_type must be 2 or inf (another norm needs a second pass)", what);
+    return NT_EINVAL;
   }
+  rc = build_peer_sync(sync, args->num_ranks, P.sync, what);
+  if (rc) return rc;
+  P.norm_type = norm_type;
+  return dispatch_dtype<true>(P, args->dtype, as_stream(stream), what);
 }
 
 int nt_peer_copy(const void* const* src, void* const* dst, int32_t count, uint64_t bytes_each, void* stream) {

@@ -129,13 +129,26 @@ class CudaShardKernels:
             args.sources[q] = ptr
         N.call("nt_zero_reduce_scatter_stats", N.C.byref(args), N.stream_handle())
 
+    def reduce_exchange(self, sources, dest, stats, *, scale, average, sync, norm_type=2.0):
+        """reduce_stats with the cross-GPU exchanges inside the kernel: every rank's READY before
+        the pull, then every rank's shard statistics, so `stats` comes back global and final."""
+        args = N.ZeroReduceArgs(num_ranks=len(sources), dtype=N.dtype_code(dest.dtype), count=dest.numel(),
+                                average=int(bool(average)), dest=dest.data_ptr(),
+                                scale=None if scale is None else scale.data_ptr(), stats=stats.data_ptr(),
+                                workspace=self.workspace.data_ptr(), workspace_bytes=self.workspace.numel())
+        for q, ptr in enumerate(sources[:N.NT_MAX_RANKS]):
+            args.sources[q] = ptr
+        N.call("nt_zero_reduce_scatter_exchange", N.C.byref(args), N.C.byref(sync), float(norm_type),
+               N.stream_handle())
+
     def update(self, *, master, exp_avg, exp_avg_sq, copy, grad_dtype, segments, num_segments, num_chunks, steps,
-               corrections, capacity, scale, stats, skip, max_norm, groups, peers=None, schedule=None):
+               corrections, capacity, scale, stats, skip, max_norm, groups, peers=None, schedule=None, sync=None):
         group_array = (N.AdamWGroup * len(groups))(*groups)
         args = N.AdamWMtArgs(
             param=master.data_ptr(), exp_avg=exp_avg.data_ptr(), exp_avg_sq=exp_avg_sq.data_ptr(),
             model_copy=copy.data_ptr(), model_dtype=N.dtype_code(copy.dtype), grad_dtype=N.dtype_code(grad_dtype),
-            segments=segments.data_ptr(), num_segments=num_segments, chunk_elems=CHUNK, num_chunks=num_chunks,
+            segments=None if segments is None else segments.data_ptr(), num_segments=num_segments,
+            chunk_elems=CHUNK, num_chunks=num_chunks,
             steps=steps.data_ptr(), corrections=corrections.data_ptr(), correction_capacity=capacity,
             scale=None if scale is None else scale.data_ptr(), stats=None if stats is None else stats.data_ptr(),
             skip_nonfinite=int(skip), clip=int(max_norm is not None), max_norm=float(max_norm or 0.0),
@@ -143,7 +156,11 @@ class CudaShardKernels:
             num_groups=len(groups))
         if schedule is not None:
             args.lr_schedule, args.lr_schedule_rows, args.lr_schedule_columns, args.lr_step = schedule
-        if peers:
+        if sync is not None:
+            array = (N.C.c_void_p * max(1, len(peers or [])))(*(peers or []))
+            N.call("nt_adamw_mt_push_exchange", N.C.byref(args), array, len(peers or []), N.C.byref(sync),
+                   N.stream_handle())
+        elif peers:
             array = (N.C.c_void_p * len(peers))(*peers)
             N.call("nt_adamw_mt_push", N.C.byref(args), array, len(peers), N.stream_handle())
         else:
@@ -163,7 +180,8 @@ class ZeroAdamW(_FirstOrderAdam):
 
     def __init__(self, params, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 1e-2,
                  *, maximize: bool = False, model_dtype=torch.bfloat16, process_group=None, average_grads: bool = True,
-                 pieces: int = DEFAULT_PIECES, transport: str = "auto", _kernels=None):
+                 pieces: int = DEFAULT_PIECES, transport: str = "auto", exchange: str = "flags",
+                 exchange_timeout: float = 10.0, _kernels=None):
         if model_dtype not in (torch.bfloat16, torch.float16, torch.float32):
             raise TypeError("model_dtype must be torch.bfloat16, torch.float16 or torch.float32.")
         self._group = process_group
@@ -172,6 +190,15 @@ class ZeroAdamW(_FirstOrderAdam):
             raise ValueError("pieces must be a positive integer.")
         if transport not in ("auto", "p2p", "nccl"):
             raise ValueError("transport must be 'auto', 'p2p' or 'nccl'.")
+        if exchange not in ("flags", "nccl"):
+            raise ValueError("exchange must be 'flags' or 'nccl'.")
+        if not (isinstance(exchange_timeout, (int, float)) and 0 < exchange_timeout <= 3600):
+            raise ValueError("exchange_timeout must be a number of seconds in (0, 3600].")
+        self._exchange = exchange
+        self._exchange_timeout_ns = int(exchange_timeout * 1e9)
+        self._epoch = 0
+        self._flag_step = False
+        self._mailboxes: list[int] = []
         self._pieces = pieces
         self._transport_request = transport
         self.transport = "nccl"
@@ -244,6 +271,8 @@ class ZeroAdamW(_FirstOrderAdam):
         self._side = torch.cuda.Stream(device) if device.type == "cuda" else None
         if self.transport == "p2p":
             self._sync = torch.zeros(1, dtype=torch.int32, device=device)
+            self._mailbox = torch.zeros(N.C.sizeof(N.ZeroMailbox), dtype=torch.uint8, device=device)
+            self._exchange_error = torch.zeros(1, dtype=torch.int32, device=device)
             self._map_peers()
         for p in params:
             _OWNERS[id(p)] = self
@@ -311,7 +340,43 @@ class ZeroAdamW(_FirstOrderAdam):
         # Where this rank's shard lands in every other rank's copy, addressed like the local
         # copy base (the kernel adds the shard-local offset).
         self._push = [c + shard_bytes for q, c in enumerate(copies) if q != self.rank]
+        # Every rank's mailbox (the in-kernel exchanges write epochs and statistics there).
+        handles = [None] * self.world
+        dist.all_gather_object(handles, N.ipc_export(self._mailbox.data_ptr()), group=self._group)
+        self._mailboxes = []
+        for q, (mh, moff) in enumerate(handles):
+            if q == self.rank:
+                self._mailboxes.append(self._mailbox.data_ptr())
+                continue
+            m = N.ipc_open(mh, moff)
+            self._peer_maps.append(m)
+            self._mailboxes.append(m)
         dist.barrier(group=self._group)
+
+    def _uses_flags(self) -> bool:
+        return self.transport == "p2p" and self._exchange == "flags"
+
+    def _sync_args(self) -> "N.ZeroSync":
+        sync = N.ZeroSync(rank=self.rank, epoch=self._epoch, timeout_ns=self._exchange_timeout_ns,
+                          error=self._exchange_error.data_ptr())
+        for q, ptr in enumerate(self._mailboxes):
+            sync.mailboxes[q] = ptr
+        return sync
+
+    def exchange_error(self) -> int:
+        """The in-kernel exchanges' sticky error word (synchronises): bit 0 = a wait of the
+        reduce-scatter ran out (that step was skipped as if found_inf), bit 1 = the update's
+        closing wait ran out. 0 over NCCL or when every wait completed."""
+        if not self._uses_flags():
+            return 0
+        return int(self._exchange_error.item())
+
+    def check_exchange(self) -> None:
+        """Raises RuntimeError if any in-kernel wait on another rank has run out."""
+        code = self.exchange_error()
+        if code:
+            raise RuntimeError(f"ZeroAdamW: a wait on another rank ran out (error word {code:#x}); a rank stopped "
+                               "or fell more than exchange_timeout behind.")
 
     def add_gradient_buffer(self) -> int:
         """Allocates one more full gradient buffer on every rank (a collective call) and, over
@@ -412,10 +477,19 @@ class ZeroAdamW(_FirstOrderAdam):
             self.last_events = []
         self._event()
         if self.transport == "p2p":
-            self._barrier()
             stats = stats_tensor(self.device)
-            self._kernels.reduce_stats(self._sources, self.grad_shard, stats, scale=scale, average=self._average)
-            self._local_stats = (scale, stats)
+            if self._uses_flags():
+                # READY, the pull, the statistics exchange and the finalize in one kernel: the
+                # record comes back global (the same on every rank).
+                self._epoch += 1
+                self._kernels.reduce_exchange(self._sources, self.grad_shard, stats, scale=scale,
+                                              average=self._average, sync=self._sync_args())
+                self._local_stats = (scale, stats, True)
+                self._flag_step = True
+            else:
+                self._barrier()
+                self._kernels.reduce_stats(self._sources, self.grad_shard, stats, scale=scale, average=self._average)
+                self._local_stats = (scale, stats, False)
             self._event()
             self._reduced = True
             return
@@ -432,6 +506,18 @@ class ZeroAdamW(_FirstOrderAdam):
         """found_inf and the global norm, identical on every rank."""
         k = self._kernels
         cached, self._local_stats = self._local_stats, None
+        if cached is not None and cached[0] is scale and cached[2]:
+            # Global already (the in-kernel exchange). p = 2 is final; inf only needs the
+            # finalize of the global max; any other p a second pass and one all-reduce.
+            stats = cached[1]
+            if norm_type == 2.0:
+                return stats
+            stats = stats.clone()
+            if norm_type != float("inf"):
+                k.stats(self.grad_shard, stats, scale=scale, norm_type=norm_type, pass_=1, finalize=False)
+                dist.all_reduce(stats[_POWSUM:_POWSUM + 1], op=dist.ReduceOp.SUM, group=self._group)
+            k.finalize(stats, norm_type)
+            return stats
         if cached is not None and cached[0] is scale:
             stats = cached[1]          # pass 0 ran inside the p2p reduce-scatter
         else:
@@ -535,9 +621,16 @@ class ZeroAdamW(_FirstOrderAdam):
         main = torch.cuda.current_stream(self.device) if cuda else None
         self._local_stats = None
         if self.transport == "p2p":
-            self._launch_update(tables[0], structs, amp, 0, self._push)
-            self._event()
-            self._barrier()
+            if self._flag_step:
+                # The update and push, then DONE to every rank and a wait for everyone's, in one
+                # kernel (launched even for an empty shard, which only takes part in DONE).
+                self._launch_update(tables[0], structs, amp, 0, self._push, sync=self._sync_args())
+                self._flag_step = False
+                self._event()
+            else:
+                self._launch_update(tables[0], structs, amp, 0, self._push)
+                self._event()
+                self._barrier()
             self._event()
             if not self.pieces:
                 self._advance_steps_without_update(amp)
@@ -581,10 +674,13 @@ class ZeroAdamW(_FirstOrderAdam):
         self.corrections.ensure(self.max_step + 1)
         return structs, self._piece_tables(local)
 
-    def _launch_update(self, table, structs, amp, j: int, peers):
-        """The fused AdamW kernel over piece j of the shard (pushing into `peers` if given)."""
+    def _launch_update(self, table, structs, amp, j: int, peers, sync=None):
+        """The fused AdamW kernel over piece j of the shard (pushing into `peers` if given; with
+        `sync`, closing the step with the in-kernel DONE exchange, even with no segments)."""
         if table is None:
-            return
+            if sync is None:
+                return
+            table = (None, 0, 0)
         scheduler = getattr(self, "_lr_schedule", None)
         schedule = None if scheduler is None else scheduler._schedule_args()
         segs, nseg, nchunks = table
@@ -594,7 +690,7 @@ class ZeroAdamW(_FirstOrderAdam):
             steps=self.steps, corrections=self.corrections.tensor, capacity=self.corrections.capacity,
             scale=None if amp is None else amp.scale, stats=None if amp is None else amp.stats,
             skip=bool(amp is not None and amp.skip), max_norm=None if amp is None else amp.max_norm,
-            groups=structs, peers=peers, **({"schedule": schedule} if schedule is not None else {}))
+            groups=structs, peers=peers, sync=sync, **({"schedule": schedule} if schedule is not None else {}))
 
     def benchmark_shard_update(self, iters: int) -> float:
         """Mean device time (ms) of the shard's AdamW update alone -- no reduce-scatter, no

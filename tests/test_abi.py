@@ -106,6 +106,8 @@ STRUCTS = {
     "nt_softmax_args": (N.SoftmaxArgs, [f for f, _ in N.SoftmaxArgs._fields_]),
     "nt_norm_args": (N.NormArgs, [f for f, _ in N.NormArgs._fields_]),
     "nt_fused_args": (N.FusedArgs, [f for f, _ in N.FusedArgs._fields_]),
+    "nt_zero_mailbox": (N.ZeroMailbox, [f for f, _ in N.ZeroMailbox._fields_]),
+    "nt_zero_sync": (N.ZeroSync, [f for f, _ in N.ZeroSync._fields_]),
 }
 
 

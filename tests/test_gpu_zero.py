@@ -1,5 +1,6 @@
 """ZeRO-1 on 2+ GPUs: one process per GPU, GradScaler + clip_grad_norm_ + AdamW, over both
-transports (NCCL collectives; the fused kernels over peer memory).
+transports (NCCL collectives; the fused kernels over peer memory, ordered across GPUs by
+flags inside the kernels or by NCCL calls between them).
 
 The oracle receives the gradients as they come out of the reduce-scatter (gathered from
 every rank), so the comparison isolates the sharded update from the bf16 reduction
@@ -25,7 +26,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out_path, transport, lazy):
+def _worker(rank, world, port, out_path, transport, lazy, exchange):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -41,7 +42,7 @@ def _worker(rank, world, port, out_path, transport, lazy):
         decay, no_decay = shape.groups()
         groups = [{"params": [params[i] for i in decay], "weight_decay": 0.1},
                   {"params": [params[i] for i in no_decay], "weight_decay": 0.0}]
-        opt = ZeroAdamW(groups, lr=3e-4, model_dtype=torch.bfloat16, transport=transport)
+        opt = ZeroAdamW(groups, lr=3e-4, model_dtype=torch.bfloat16, transport=transport, exchange=exchange)
         assert opt.transport == transport
         scaler = GradScaler(1024.0, growth_interval=2)
         reduced, local, norms, stepped = [], [], [], []
@@ -66,6 +67,7 @@ def _worker(rank, world, port, out_path, transport, lazy):
             if lazy:
                 # Deferred transforms leave the reduced shard as the reduce-scatter wrote it.
                 reduced.append(opt._gather_shards(opt.grad_shard).float().cpu().numpy())
+        opt.check_exchange()   # no in-kernel wait on another rank ran out
         sd = opt.state_dict()
         copies = [p.detach().float().cpu().numpy() for p in params]
         all_local = [None] * world
@@ -84,8 +86,9 @@ def _worker(rank, world, port, out_path, transport, lazy):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport,lazy", [("nccl", True), ("p2p", True), ("p2p", False)])
-def test_zero1_matches_oracle(tmp_path, transport, lazy):
+@pytest.mark.parametrize("transport,lazy,exchange", [("nccl", True, "flags"), ("p2p", True, "flags"),
+                                                     ("p2p", False, "flags"), ("p2p", True, "nccl")])
+def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange):
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     import torch.multiprocessing as mp
@@ -95,7 +98,8 @@ def test_zero1_matches_oracle(tmp_path, transport, lazy):
     from oracle import clip as oclip
     from oracle.casts import f32_to_bf16_bits, round_to_bf16
     out_path = tmp_path / "zero.npz"
-    mp.spawn(_worker, args=(WORLD, _free_port(), str(out_path), transport, lazy), nprocs=WORLD, join=True)
+    mp.spawn(_worker, args=(WORLD, _free_port(), str(out_path), transport, lazy, exchange), nprocs=WORLD,
+             join=True)
     out = np.load(out_path)
     shape = W.CONFIG_SMALL
     offsets = out["offsets"]
