@@ -690,7 +690,8 @@ class ZeroAdamW(_FirstOrderAdam):
             steps=self.steps, corrections=self.corrections.tensor, capacity=self.corrections.capacity,
             scale=None if amp is None else amp.scale, stats=None if amp is None else amp.stats,
             skip=bool(amp is not None and amp.skip), max_norm=None if amp is None else amp.max_norm,
-            groups=structs, peers=peers, sync=sync, **({"schedule": schedule} if schedule is not None else {}))
+            groups=structs, peers=peers, **({"schedule": schedule} if schedule is not None else {}),
+            **({"sync": sync} if sync is not None else {}))
 
     def benchmark_shard_update(self, iters: int) -> float:
         """Mean device time (ms) of the shard's AdamW update alone -- no reduce-scatter, no
