@@ -511,12 +511,12 @@ def run_ours(args):
                      "unit": "GB/s", "frac": BYTES_UPDATE * shard / (update_ms / 1e3) / 1e9 / peak,
                      "peak_source": peak_kind, "kernel": "adamw_mt",
                      "algorithmic_bytes_per_launch": BYTES_UPDATE * shard,
-                     # DRAM bytes of one launch: the committed ncu capture of the 124M update,
-                     # scaled by parameter count to the whole model, then to this rank's shard.
+                     # DRAM bytes of one launch: the committed ncu capture of the 1.3B update,
+                     # at N > 1 scaled to this rank's shard.
                      "traffic": None if traffic is None else traffic / world,
                      "traffic_source": None if traffic is None else
-                     "ncu dram read+write of the 124M adamw_mt launch (profiles/adamw_mt_124m.md), scaled by "
-                     "parameter count to 1.3B" + (f" and to the 1/{world} shard" if world > 1 else "")},
+                     "ncu dram read+write of one 1.3B adamw_mt launch (profiles/dram_1p3b.md)"
+                     + (f", scaled to the 1/{world} shard" if world > 1 else "")},
         "gpu_launches": launches,
         "clocks": clocks,
     }
