@@ -152,13 +152,7 @@ __device__ __forceinline__ float max_of_pair(uint32_t r) {
 // them after the wait.)
 template <int DT, bool STAGED>
 __device__ __forceinline__ uint4 row_raw(const unsigned char* stage, int k) {
-  // An explicit shared-space load at a 32-bit shared address (LDS.128), whatever the
-  // compiler could infer about `stage`. Volatile keeps it after the mbarrier wait.
-  uint4 r;
-  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "r"(smem_u32(stage) + (uint32_t)k * 16u));
-  return r;
+  return reinterpret_cast<const uint4*>(stage)[k];
 }
 
 template <int DT, bool STAGED>
