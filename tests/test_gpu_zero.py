@@ -104,11 +104,13 @@ def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange):
     shape = W.CONFIG_SMALL
     offsets = out["offsets"]
     numels = [int(np.prod(s)) for _, s in shape.shapes()]
-    # The reduce-scatter (average) agrees with a float32 mean within bf16 rounding.
+    # The reduce-scatter (average) agrees with a float32 mean within bf16 rounding. NCCL's
+    # bf16 reduction rounds a partial sum at each of up to N - 1 steps, each error within
+    # 2^-8 of the partial sum, so its bound grows with the rank count (2^-7 at N = 2).
     local = out["local"]
     with np.errstate(invalid="ignore"):
         mean = local.mean(axis=0)
-        bound = 2 ** -7 * np.abs(local).mean(axis=0) + 1e-30
+        bound = 2 ** -8 * max(2, WORLD) * np.abs(local).mean(axis=0) + 1e-30
         finite = np.isfinite(mean)
         assert np.array_equal(finite, np.isfinite(out["reduced"]))
         assert np.all(np.abs(out["reduced"][finite] - mean[finite]) <= bound[finite])
