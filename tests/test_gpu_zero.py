@@ -26,7 +26,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out_path, transport, lazy, exchange):
+def _worker(rank, world, port, out_path, transport, lazy, exchange, norm_type=2.0):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -61,7 +61,7 @@ def _worker(rank, world, port, out_path, transport, lazy, exchange):
                 reduced.append(opt._gather_shards(opt.grad_shard).float().cpu().numpy())
             scaler.scale(torch.ones((), device="cuda"))
             scaler.unscale_(opt)
-            norms.append(float(clip_grad_norm_(params, 1.0).item()))
+            norms.append(float(clip_grad_norm_(params, 1.0, norm_type=norm_type).item()))
             stepped.append(bool(scaler.step(opt)))
             scaler.update()
             if lazy:
@@ -86,9 +86,10 @@ def _worker(rank, world, port, out_path, transport, lazy, exchange):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport,lazy,exchange", [("nccl", True, "flags"), ("p2p", True, "flags"),
-                                                     ("p2p", False, "flags"), ("p2p", True, "nccl")])
-def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange):
+@pytest.mark.parametrize("transport,lazy,exchange,norm_type", [
+    ("nccl", True, "flags", 2.0), ("p2p", True, "flags", 2.0), ("p2p", False, "flags", 2.0),
+    ("p2p", True, "nccl", 2.0), ("p2p", True, "flags", float("inf")), ("p2p", True, "flags", 3.0)])
+def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange, norm_type):
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     import torch.multiprocessing as mp
@@ -98,7 +99,7 @@ def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange):
     from oracle import clip as oclip
     from oracle.casts import f32_to_bf16_bits, round_to_bf16
     out_path = tmp_path / "zero.npz"
-    mp.spawn(_worker, args=(WORLD, _free_port(), str(out_path), transport, lazy, exchange), nprocs=WORLD,
+    mp.spawn(_worker, args=(WORLD, _free_port(), str(out_path), transport, lazy, exchange, norm_type), nprocs=WORLD,
              join=True)
     out = np.load(out_path)
     shape = W.CONFIG_SMALL
@@ -144,10 +145,10 @@ def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange):
         if oamp.OracleGradScaler(oscaler.scale).unscale(probe):
             if not lazy:
                 probe = [None if g is None else round_to_bf16(g) for g in probe]
-            ref_norm = float(oclip.total_norm([g for g in probe if g is not None]))
+            ref_norm = float(oclip.total_norm([g for g in probe if g is not None], norm_type))
             assert abs(out["norms"][step] - ref_norm) <= 1e-12 * ref_norm
-        r = oamp.amp_step(oracle, oscaler, grads, max_norm=1.0, storage=None if lazy else round_to_bf16,
-                          given_norm=float(out["norms"][step]))
+        r = oamp.amp_step(oracle, oscaler, grads, max_norm=1.0, norm_type=norm_type,
+                          storage=None if lazy else round_to_bf16, given_norm=float(out["norms"][step]))
         assert bool(out["stepped"][step]) == r["stepped"]
     assert float(out["scale"]) == oscaler.scale
     assert out["steps"].tolist() == [3] * len(numels)
@@ -158,3 +159,71 @@ def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange):
                                       oracle.state[orig]["exp_avg"].view(np.uint32))
         # The all-gathered model copy is the bf16 rounding of the gathered master.
         assert np.array_equal(f32_to_bf16_bits(out[f"copy{orig}"]), f32_to_bf16_bits(out[f"master{k}"]))
+
+
+def _stall_worker(rank, world, port, store_port, out_path):
+    """Both ranks take one step; then rank 1 stops taking steps (between steps, nothing of
+    it in flight) but stays alive, so its memory stays mapped, until rank 0 is done. Rank
+    0's next step finds no READY from rank 1: the waits end after exchange_timeout, the
+    step is skipped and the error word says so."""
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    store = dist.TCPStore("127.0.0.1", store_port, world, rank == 0, timeout=datetime.timedelta(seconds=60))
+    try:
+        from namitorch_b200 import GradScaler, workloads as W
+        from namitorch_b200.optim import clip_grad_norm_
+        from namitorch_b200.zero import ZeroAdamW
+        shape = W.CONFIG_SMALL
+        params = [torch.nn.Parameter(torch.from_numpy(a).cuda()) for a in W.init_params(shape, seed=0)]
+        opt = ZeroAdamW(params, lr=3e-4, model_dtype=torch.bfloat16, transport="p2p", exchange_timeout=1.0)
+        scaler = GradScaler(1024.0)
+
+        def step():
+            for p in params:
+                p.grad.fill_(1.0)
+            scaler.scale(torch.ones((), device="cuda"))
+            scaler.unscale_(opt)
+            norm = clip_grad_norm_(params, 1.0)
+            stepped = scaler.step(opt)
+            scaler.update()
+            return norm, stepped
+
+        step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        assert opt.exchange_error() == 0
+        if rank == 0:
+            before = opt.master.clone()
+            norm, stepped = step()
+            torch.cuda.synchronize()
+            error = opt.exchange_error()
+            try:
+                opt.check_exchange()
+                raised = ""
+            except RuntimeError as exc:
+                raised = str(exc)
+            np.savez(out_path, error=error, stepped=bool(stepped), norm=float(norm.item()),
+                     unchanged=bool(torch.equal(before, opt.master)), raised=raised)
+            store.set("done", "1")
+        else:
+            store.wait(["done"])
+        opt.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_a_rank_that_stops_between_steps_makes_the_others_skip_with_an_error(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    out_path = tmp_path / "stall.npz"
+    mp.spawn(_stall_worker, args=(2, _free_port(), _free_port(), str(out_path)), nprocs=2, join=True)
+    out = np.load(out_path)
+    assert int(out["error"]) == 3          # the reduce-scatter's wait and the update's wait both ran out
+    assert not bool(out["stepped"]) and np.isnan(float(out["norm"]))
+    assert bool(out["unchanged"])          # the skipped step left the master weights alone
+    assert "wait on another rank ran out" in str(out["raised"])
