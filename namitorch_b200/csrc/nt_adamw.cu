@@ -128,6 +128,7 @@ struct MtParams {
   int sched_cols;
   const int32_t* sched_step;
   PeerSync sync;                     // the closing exchange (nt_adamw_mt_push_exchange only)
+  int vec32;                         // p, m and v start on 32-byte boundaries: 256-bit accesses
   nt_adamw_group groups[NT_MAX_GROUPS];
 };
 
@@ -164,9 +165,15 @@ template <int GDT, int CDT, bool PUSH>
 __device__ __forceinline__ void mt_vec8(const MtParams& P, int64_t ai, const void* g, int64_t gi,
                                         const Coef& c, const Unscale& un, bool clip, double coef) {
   float pv[8], mv[8], vv[8], gv[8];
-  load8_f32(P.p + ai, pv);
-  load8_f32(P.m + ai, mv);
-  load8_f32(P.v + ai, vv);
+  if (P.vec32) {   // uniform across the grid
+    load8_f32_v8(P.p + ai, pv);
+    load8_f32_v8(P.m + ai, mv);
+    load8_f32_v8(P.v + ai, vv);
+  } else {
+    load8_f32(P.p + ai, pv);
+    load8_f32(P.m + ai, mv);
+    load8_f32(P.v + ai, vv);
+  }
   load8<GDT>(g, gi, gv);
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
@@ -174,10 +181,16 @@ __device__ __forceinline__ void mt_vec8(const MtParams& P, int64_t ai, const voi
     if (clip) gg = __double2float_rn(__dmul_rn((double)gg, coef));
     adam_update(pv[k], gg, mv[k], vv[k], c);
   }
-  store8_f32(P.m + ai, mv);
-  store8_f32(P.v + ai, vv);
+  if (P.vec32) {
+    store8_f32_v8(P.m + ai, mv);
+    store8_f32_v8(P.v + ai, vv);
+  } else {
+    store8_f32(P.m + ai, mv);
+    store8_f32(P.v + ai, vv);
+  }
   if (c.update) {
-    store8_f32(P.p + ai, pv);
+    if (P.vec32) store8_f32_v8(P.p + ai, pv);
+    else store8_f32(P.p + ai, pv);
     if constexpr (CDT != kNoCopy) store_copy8<CDT, PUSH>(P, ai, pv);
   }
 }
@@ -379,6 +392,10 @@ static int build_mt_params(const nt_adamw_mt_args* args, MtParams& P) {
     }
   }
   P.p = a.param; P.m = a.exp_avg; P.v = a.exp_avg_sq; P.copy = a.model_copy;
+  // The vector path runs at element offsets that are multiples of 8 (32 bytes of fp32), so
+  // 32-byte aligned arenas allow one 256-bit access per 8 values.
+  P.vec32 = ((reinterpret_cast<uintptr_t>(a.param) | reinterpret_cast<uintptr_t>(a.exp_avg) |
+              reinterpret_cast<uintptr_t>(a.exp_avg_sq)) & 31u) == 0;
   P.segs = a.segments; P.nseg = a.num_segments; P.chunk_elems = a.chunk_elems; P.nchunks = a.num_chunks;
   P.steps = a.steps; P.corr = reinterpret_cast<const float2*>(a.corrections); P.cap = a.correction_capacity;
   P.scale = a.scale; P.stats = a.stats; P.skip_nonfinite = a.skip_nonfinite; P.clip = a.clip;

@@ -124,6 +124,21 @@ __device__ __forceinline__ void store8_f32(float* p, const float v[8]) {
   __stcs(q + 1, make_float4(v[4], v[5], v[6], v[7]));
 }
 
+// The same 8 values as one 32-byte access (sm_100's 256-bit loads and stores); `p` must be
+// 32-byte aligned.
+__device__ __forceinline__ void load8_f32_v8(const float* p, float out[8]) {
+  asm volatile("ld.global.cs.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=f"(out[0]), "=f"(out[1]), "=f"(out[2]), "=f"(out[3]), "=f"(out[4]), "=f"(out[5]),
+                 "=f"(out[6]), "=f"(out[7])
+               : "l"(p));
+}
+
+__device__ __forceinline__ void store8_f32_v8(float* p, const float v[8]) {
+  asm volatile("st.global.cs.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(v[0]), "f"(v[1]),
+               "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
+}
+
 // ---- loss-scale handling -------------------------------------------------------------
 // Division by the loss scale, bit-identical to IEEE f32 division. When the scale is a
 // normal power of two its reciprocal is exact, and g * 2^-k rounds the same exact real
