@@ -44,3 +44,14 @@ def test_skipped_step_expects_the_state_unchanged(reference_install):
     pre = [np.arange(5, dtype=np.float32)] * 3
     got, checker = bench._shard_reference(pre, np.ones(5, np.float32), 2.0, 1.0, 3, {}, False, "cpu")
     assert checker.startswith("skipped") and all(np.array_equal(a, b) for a, b in zip(got, pre))
+
+
+def test_reference_arm_runs_the_reference_on_the_shared_sample(reference_install):
+    """The reference arm's CPU figure comes from the reference's own AMP step on the same
+    16.8M-parameter sample as the threaded port beside it."""
+    assert bench.CPU_SAMPLE_PARAMS == 16_789_504
+    ref = bench.reference_amp_sample(steps=1, warmup=0)
+    assert ref["kind"] == "reference" and ref["cores"] == 1 and ref["value"] > 0
+    assert str(bench.CPU_SAMPLE_PARAMS) in ref["sample"] and ref["host"]["cpu_count"] >= 1
+    port = bench.cpu_amp_sample(1, 2, warmup=0)
+    assert port["kind"] == "port" and port["cores"] == 2 and str(bench.CPU_SAMPLE_PARAMS) in port["sample"]
