@@ -15,17 +15,22 @@ One step has two exchanges around the update, over one of two transports:
 
 * ``transport="p2p"`` (default when every pair of GPUs can address each other's memory):
   the exchanges run inside the kernels, over NVLink, through CUDA IPC mappings of every
-  rank's gradient buffer and model copy (K = 1: one contiguous shard per rank).
-  1. a 4-byte stream-ordered barrier (NCCL all-reduce): every rank's gradients are final;
-  2. ``nt_zero_reduce_scatter_stats``: the rank pulls its shard range from every rank's
-     gradient buffer, sums in f32 in rank order, writes the reduced shard and, in the same
-     pass, the shard's statistics;
-  3. one all-reduce (SUM) of the 24-byte record {sum g^2, #non-finite, #NaN} (plus a MAX of
-     max|g| for a non-2 norm) and a one-thread finalize kernel: every rank then holds the
-     same found_inf and global norm;
-  4. ``nt_adamw_mt_push``: the fused AdamW kernel (unscale, skip, clip, update) stores each
-     bf16 result into its own model copy and into every peer's, which is the all-gather;
-  5. a second 4-byte barrier: every push has landed and every pull is done.
+  rank's gradient buffer, model copy and mailbox (K = 1: one contiguous shard per rank).
+  With ``exchange="flags"`` (the default) a step is two kernels and no NCCL call:
+  1. ``nt_zero_reduce_scatter_exchange``: every rank signals READY into every mailbox and
+     waits for everyone's (all gradients final); it pulls its shard range from every rank's
+     gradient buffer, sums in f32 in rank order, writes the reduced shard and the shard's
+     statistics; then it sends those statistics to every rank, waits for everyone's, adds
+     them in rank order and finalizes: every rank holds the same found_inf and global norm;
+  2. ``nt_adamw_mt_push_exchange``: the fused AdamW kernel (unscale, skip, clip, update)
+     stores each bf16 result into its own model copy and into every peer's (the
+     all-gather), then signals DONE and waits for everyone's: every push has landed and
+     every pull has ended.
+  Every wait is bounded (``exchange_timeout``); one that runs out sets a sticky error word
+  (``exchange_error`` / ``check_exchange``) and the step is skipped as for found_inf. With
+  ``exchange="nccl"`` the same two kernels (without the flags) are ordered by a 4-byte NCCL
+  all-reduce barrier before the pull, one SUM all-reduce of {sum g^2, #non-finite, #NaN}
+  and a finalize kernel after it, and a second barrier after the push.
 * ``transport="nccl"``: NCCL reduce-scatter of every piece (average over ranks), the
   statistics kernel plus the same all-reduce, then per piece the fused AdamW kernel
   followed by that piece's all-gather on a side stream, overlapping the next piece's update.
@@ -467,9 +472,9 @@ class ZeroAdamW(_FirstOrderAdam):
                 p.grad = own
 
     def _reduce(self, scale=None):
-        """Reduce-scatters the gradients (once per step). Over p2p the shard's pass-0
-        statistics of g / scale come out of the same kernel and are kept for
-        _global_stats."""
+        """Reduce-scatters the gradients (once per step). Over p2p the statistics of g / scale
+        come out of the same kernel and are kept for _global_stats: already global and final
+        with the in-kernel exchange, the shard's own with NCCL ordering."""
         if self._reduced:
             return
         self._adopt_foreign_grads()
