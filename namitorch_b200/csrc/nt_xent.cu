@@ -214,9 +214,9 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint64_t bars[NCH];
   __shared__ unsigned done[NCH];   // warps finished with a chunk of the current row
-  __shared__ float red_f2[2][THREADS / 32];
-  __shared__ float red_s2[2][THREADS / 32];
-  __shared__ double red_d2[2][THREADS / 32];
+  __shared__ float red_f[THREADS / 32];
+  __shared__ float red_s[THREADS / 32];
+  __shared__ float coef[4];   // A, B, G and the row mode of the current row
   __shared__ double red_d[THREADS / 32];
   __shared__ bool last;
   __shared__ int abort_flag;
@@ -356,17 +356,7 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
       }
       if constexpr (DT != NT_F32) m = max_nan(m, max_of_pair<DT>(m2));
     }
-    constexpr int NW = THREADS / 32;
-    float M;
-    {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if (lane == 0) red_f2[parity][threadIdx.x >> 5] = m;
-      __syncthreads();
-      M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < NW; ++w) M = max_nan(M, red_f2[parity][w]);
-    }
+    const float M = block_reduce(m, red_f, [](float a, float b) { return max_nan(a, b); }, -INFINITY);
     if (STAGED && abort_flag) {
       // A copy did not land in time: report it, let this row's other copies land (each wait
       // bounded) and leave. No copy of the next row has been issued yet.
@@ -409,60 +399,64 @@ __global__ void __launch_bounds__(kXentThreads) xent_kernel(const __grid_constan
 #pragma unroll
       for (int q = 0; q < EPV; ++q) s += part[q];
     }
-    // Row sum, row loss and the gradient coefficients: warp partials in shared memory (slots
-    // by row parity, so no barrier guards their reuse); after one barrier every warp adds
-    // them with the same shuffle tree and derives the row's scalars itself.
+    // Row sum, row loss and the gradient coefficients (d_c = e_c * A - G_c, minus B at
+    // c == t): warp partials in shared memory; warp 0 adds them (a fixed shuffle tree),
+    // computes the row's scalars once and broadcasts them.
+    constexpr int NW = THREADS / 32;
     {
       const float sw = warp_sum(s);
       const double dw = smooth ? warp_sum(swx) : 0.0;
       if (lane == 0) {
-        red_s2[parity][threadIdx.x >> 5] = sw;
-        if (smooth) red_d2[parity][threadIdx.x >> 5] = dw;
+        red_s[threadIdx.x >> 5] = sw;
+        if (smooth) red_d[threadIdx.x >> 5] = dw;
       }
     }
     __syncthreads();
-    const float S = warp_sum(lane < NW ? red_s2[parity][lane] : 0.0f);
-    const float wt = valid ? (WEIGHTED ? P.weight[t] : 1.0f) : 0.0f;
-    int mode = 0;  // 0: zero row, 1: NaN row, 2: regular
-    float A = 0.0f, B = 0.0f, G = 0.0f;
-    if (valid && !zero_all && !bad_row && !neg_row) {
-      mode = 2;
-      const float invS = 1.0f / S;
-      const float a_coef = WEIGHTED ? ((1.0f - e) * wt + (float)((double)e * W / (double)V)) * inv_den : inv_den;
-      A = a_coef * invS;
-      B = (1.0f - e) * wt * inv_den;
-      G = smooth ? (float)((double)e / (double)V) * inv_den : 0.0f;
-    } else if (valid && !zero_all && bad_row) {
-      mode = 1;
-    }
-    const double sx = smooth ? warp_sum(lane < NW ? red_d2[parity][lane] : 0.0) : 0.0;
-    if (threadIdx.x == 0) {
-      float loss_i = 0.0f;
-      if (mode == 1) {
-        loss_i = __int_as_float(0x7fc00000);
-      } else if (valid && !zero_all && neg_row) {
-        loss_i = INFINITY;
-      } else if (mode == 2) {
-        float xt;
-        if constexpr (STAGED) {
-          const int off = head + t * ES;
-          if constexpr (DT == NT_F32) xt = *reinterpret_cast<const float*>(smem + off);
-          else if constexpr (DT == NT_BF16) xt = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(smem + off));
-          else xt = __half2float(*reinterpret_cast<const __half*>(smem + off));
-        } else {
-          xt = load1<DT>(P.logits, row_base + t);
+    if (threadIdx.x < 32) {
+      const float S = warp_sum(lane < NW ? red_s[lane] : 0.0f);
+      const double sx = smooth ? warp_sum(lane < NW ? red_d[lane] : 0.0) : 0.0;
+      if (lane == 0) {
+        const float wt = valid ? (WEIGHTED ? P.weight[t] : 1.0f) : 0.0f;
+        int mode = 0;  // 0: zero row, 1: NaN row, 2: regular
+        float loss_i = 0.0f, A = 0.0f, B = 0.0f, G = 0.0f, xt = 0.0f;
+        if (valid && !zero_all) {
+          if (bad_row) {
+            mode = 1;
+            loss_i = __int_as_float(0x7fc00000);
+          } else if (neg_row) {
+            loss_i = INFINITY;
+          } else {
+            mode = 2;
+            if constexpr (STAGED) {
+              const int off = head + t * ES;
+              if constexpr (DT == NT_F32) xt = *reinterpret_cast<const float*>(smem + off);
+              else if constexpr (DT == NT_BF16) xt = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(smem + off));
+              else xt = __half2float(*reinterpret_cast<const __half*>(smem + off));
+            } else {
+              xt = load1<DT>(P.logits, row_base + t);
+            }
+            const float lse = M + logf(S);
+            const float base = -wt * (xt - lse);
+            if (smooth) {
+              const double sm = -(sx - (double)lse * W) / (double)V;
+              loss_i = (1.0f - e) * base + e * (float)sm;
+            } else {
+              loss_i = base;
+            }
+            const float invS = 1.0f / S;
+            const float a_coef = WEIGHTED ? ((1.0f - e) * wt + (float)((double)e * W / (double)V)) * inv_den : inv_den;
+            A = a_coef * invS;
+            B = (1.0f - e) * wt * inv_den;
+            G = smooth ? (float)((double)e / (double)V) * inv_den : 0.0f;
+          }
         }
-        const float lse = M + logf(S);
-        const float base = -wt * (xt - lse);
-        if (smooth) {
-          const double sm = -(sx - (double)lse * W) / (double)V;
-          loss_i = (1.0f - e) * base + e * (float)sm;
-        } else {
-          loss_i = base;
-        }
+        P.row_loss[row] = loss_i;
+        coef[0] = A; coef[1] = B; coef[2] = G; coef[3] = __int_as_float(mode);
       }
-      P.row_loss[row] = loss_i;
     }
+    __syncthreads();
+    const float A = coef[0], B = coef[1], G = coef[2];
+    const int mode = __float_as_int(coef[3]);
 
     // Pass 3: the gradient, chunk by chunk. The last warp to finish a chunk refills it with
     // the CTA's next row (a shared-memory count per chunk; no warp waits for another).
