@@ -593,14 +593,14 @@ def pin_host_threads(local_rank: int) -> None:
 
 def measure_peer_bandwidth(world: int, rank: int, device, total_bytes: int = 512 << 20, reps: int = 5) -> dict:
     """SM-driven NVLink bandwidth per GPU and direction, measured in this run with the
-    access pattern of the ZeRO-1 kernels (plain 16-byte loads and stores, no copy engine,
+    access pattern of the ZeRO-1 kernels (plain 32-byte loads and stores, no copy engine,
     no multicast): every rank at once pulls total_bytes / (N - 1) from each peer's buffer
     (inbound, the reduce-scatter), then pushes as much into each peer's buffer (outbound,
     the all-gather). Median of `reps` launches, max over ranks of each launch's time."""
     import torch
     import torch.distributed as dist
     from namitorch_b200 import _native as N
-    per = (total_bytes // (world - 1)) // 16 * 16
+    per = (total_bytes // (world - 1)) // 32 * 32
     buf = torch.zeros(world * per, dtype=torch.uint8, device=device)   # slot 0: own data; slots 1..N-1: inbox
     handles = [None] * world
     dist.all_gather_object(handles, N.ipc_export(buf.data_ptr()))
@@ -638,7 +638,7 @@ def measure_peer_bandwidth(world: int, rank: int, device, total_bytes: int = 512
     del buf
     out["bytes_per_gpu"] = (world - 1) * per
     out["how"] = ("nt_peer_copy, every rank at once: pull = (N-1) peer buffers -> local, push = local -> (N-1) peer "
-                  "buffers; 16-byte SM loads/stores; median of %d launches, max over ranks" % reps)
+                  "buffers; 32-byte SM loads/stores; median of %d launches, max over ranks" % reps)
     return out
 
 

@@ -510,8 +510,9 @@ int nt_adamw_mt_push_exchange(const nt_adamw_mt_args* args, void* const* peer_co
 
 /* No counterpart in the reference: copies `count` (1..NT_MAX_RANKS) independent ranges of
    `bytes_each` bytes (a multiple of 16; 16-byte aligned pointers), src[k] -> dst[k], with
-   the plain 16-byte SM loads and stores that the two ZeRO-1 kernels above use (no copy
-   engine, no multicast). With src pointing at peers' memory (nt_ipc_open) it measures the
+   plain SM loads and stores as the two ZeRO-1 kernels above issue them (no copy engine, no
+   multicast): 32-byte accesses when every pointer is 32-byte aligned and bytes_each a
+   multiple of 32, else 16-byte. With src pointing at peers' memory (nt_ipc_open) it measures the
    inbound peer bandwidth the reduce-scatter pull sees; with dst at peers, the outbound
    bandwidth of the all-gather push. `src` and `dst` are host arrays of device pointers. */
 int nt_peer_copy(const void* const* src, void* const* dst, int32_t count, uint64_t bytes_each, void* stream);

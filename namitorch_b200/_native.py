@@ -299,7 +299,7 @@ def ipc_close(ptr: int) -> None:
 
 
 def peer_copy(src: list[int], dst: list[int], bytes_each: int, stream=None) -> None:
-    """src[k] -> dst[k] for every k, ``bytes_each`` bytes each, by 16-byte SM loads/stores."""
+    """src[k] -> dst[k] for every k, ``bytes_each`` bytes each, by SM loads/stores (32-byte when every pointer and the size allow, else 16-byte)."""
     n = len(src)
     call("nt_peer_copy", (C.c_void_p * n)(*src), (C.c_void_p * n)(*dst), n, int(bytes_each), stream_handle(stream))
 

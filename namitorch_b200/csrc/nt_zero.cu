@@ -32,6 +32,7 @@ struct ZeroReduceParams {
   StatsWorkspace* ws;
   PeerSync sync;      // used by the exchange variant only
   double norm_type;   // exchange variant: 2 or inf
+  int vec32;          // every source and the destination are 32-byte aligned
 };
 
 constexpr int kZeroThreads = kStatsThreads;
@@ -56,61 +57,92 @@ __device__ __forceinline__ float average(float sum, const ZeroReduceParams& P) {
   return sum;
 }
 
+// 32 bytes from global memory in one access (sm_100), streaming: peer reads over NVLink
+// carry more per request than with 16-byte loads when both directions of a link are busy.
+__device__ __forceinline__ void load32_cs(const void* p, uint4& lo, uint4& hi) {
+  asm volatile("ld.global.cs.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w), "=r"(hi.x), "=r"(hi.y), "=r"(hi.z), "=r"(hi.w)
+               : "l"(p));
+}
+
+__device__ __forceinline__ void store32_cs(void* p, const uint4& lo, const uint4& hi) {
+  asm volatile("st.global.cs.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(lo.x), "r"(lo.y),
+               "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w)
+               : "memory");
+}
+
 // NR > 0: the rank count is a compile-time constant (2, 4, 8); NR == 0: any count up to
-// NT_MAX_RANKS, one vector per source in flight. The statistics see exactly the values
-// stored in the shard (rounded to the gradient dtype, then unscaled).
-template <int DT, int NR, int MODE>
+// NT_MAX_RANKS, one vector per source in flight. H = 2: each access moves 32 bytes (every
+// source and the destination 32-byte aligned); H = 1: 16 bytes. The statistics see exactly
+// the values stored in the shard (rounded to the gradient dtype, then unscaled).
+template <int DT, int NR, int MODE, int H>
 __device__ __forceinline__ void zero_reduce_body(const ZeroReduceParams& P, const Unscale& un, StatsAcc& a) {
   constexpr int ES = DT == NT_F32 ? 4 : 2;
-  constexpr int EPV = 16 / ES;
+  constexpr int EPV = 16 / ES;                 // elements per 16-byte half
   constexpr int R = NR > 0 ? NR : NT_MAX_RANKS;
-  constexpr int U = NR > 0 && NR < 8 ? 8 / NR : 1;  // vectors in flight per source
+  constexpr int U = NR > 0 && NR * H < 8 ? 8 / (NR * H) : 1;   // accesses in flight per source
   const int nr = NR > 0 ? NR : P.nranks;
-  const int64_t nv = P.count / EPV;
+  const int64_t nv = P.count / (EPV * H);
   const int64_t stride = (int64_t)gridDim.x * blockDim.x * U;
-  uint4* dst = static_cast<uint4*>(P.dst);
+  char* dst = static_cast<char*>(P.dst);
 
   for (int64_t v0 = (int64_t)blockIdx.x * blockDim.x * U + threadIdx.x; v0 < nv; v0 += stride) {
-    uint4 raw[U][R];
+    uint4 raw[U][R][H];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t v = v0 + (int64_t)u * blockDim.x;
 #pragma unroll
-      for (int q = 0; q < R; ++q)
-        if (v < nv && q < nr) raw[u][q] = __ldcs(static_cast<const uint4*>(P.src[q]) + v);
+      for (int q = 0; q < R; ++q) {
+        if (v < nv && q < nr) {
+          const char* src = static_cast<const char*>(P.src[q]) + v * (16 * H);
+          if constexpr (H == 2) load32_cs(src, raw[u][q][0], raw[u][q][1]);
+          else raw[u][q][0] = __ldcs(reinterpret_cast<const uint4*>(src));
+        }
+      }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t v = v0 + (int64_t)u * blockDim.x;
       if (v >= nv) continue;
-      float sum[EPV], x[EPV];
-      unpack16<DT>(raw[u][0], sum);
+      uint4 out[H];
 #pragma unroll
-      for (int q = 1; q < R; ++q) {
-        if (q < nr) {
-          unpack16<DT>(raw[u][q], x);
+      for (int h = 0; h < H; ++h) {
+        float sum[EPV], x[EPV];
+        unpack16<DT>(raw[u][0][h], sum);
 #pragma unroll
-          for (int k = 0; k < EPV; ++k) sum[k] = __fadd_rn(sum[k], x[k]);
+        for (int q = 1; q < R; ++q) {
+          if (q < nr) {
+            unpack16<DT>(raw[u][q][h], x);
+#pragma unroll
+            for (int k = 0; k < EPV; ++k) sum[k] = __fadd_rn(sum[k], x[k]);
+          }
         }
+#pragma unroll
+        for (int k = 0; k < EPV; ++k) sum[k] = average(sum[k], P);
+        out[h] = pack_vec<DT>(sum);
+        unpack16<DT>(out[h], x);
+#pragma unroll
+        for (int k = 0; k < EPV; ++k) x[k] = unscale_by<MODE>(x[k], un.scale, un.inv);
+        stats_pass0<EPV>(x, a);
       }
-#pragma unroll
-      for (int k = 0; k < EPV; ++k) sum[k] = average(sum[k], P);
-      const uint4 out = pack_vec<DT>(sum);
-      __stcs(dst + v, out);
-      unpack16<DT>(out, x);
-#pragma unroll
-      for (int k = 0; k < EPV; ++k) x[k] = unscale_by<MODE>(x[k], un.scale, un.inv);
-      stats_pass0<EPV>(x, a);
+      if constexpr (H == 2) store32_cs(dst + v * 32, out[0], out[1]);
+      else __stcs(reinterpret_cast<uint4*>(dst) + v, out[0]);
     }
   }
   // Elements past the last full vector (count not a multiple of the vector width).
-  for (int64_t i = nv * EPV + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < P.count;
+  for (int64_t i = nv * EPV * H + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < P.count;
        i += (int64_t)gridDim.x * blockDim.x) {
     float sum = load1<DT>(P.src[0], i);
     for (int q = 1; q < nr; ++q) sum = __fadd_rn(sum, load1<DT>(P.src[q], i));
     store1<DT>(P.dst, i, average(sum, P));
     stats_one(unscale_by<MODE>(load1<DT>(P.dst, i), un.scale, un.inv), a);
   }
+}
+
+template <int DT, int NR, int MODE>
+__device__ __forceinline__ void zero_reduce_width(const ZeroReduceParams& P, const Unscale& un, StatsAcc& a) {
+  if (P.vec32) zero_reduce_body<DT, NR, MODE, 2>(P, un, a);
+  else zero_reduce_body<DT, NR, MODE, 1>(P, un, a);
 }
 
 // The exchange variant's end: the block partials are reduced in a fixed order by the last
@@ -192,9 +224,9 @@ __global__ void __launch_bounds__(kZeroThreads, 2) zero_reduce_stats_kernel(cons
   un.init(P.scale);
   StatsAcc a{0.0, 0.0, 0.0, 0.0f, 0u, 0u};
   if (run) {
-    if (!un.active) zero_reduce_body<DT, NR, kScaleNone>(P, un, a);
-    else if (un.pow2) zero_reduce_body<DT, NR, kScaleMul>(P, un, a);
-    else zero_reduce_body<DT, NR, kScaleDiv>(P, un, a);
+    if (!un.active) zero_reduce_width<DT, NR, kScaleNone>(P, un, a);
+    else if (un.pow2) zero_reduce_width<DT, NR, kScaleMul>(P, un, a);
+    else zero_reduce_width<DT, NR, kScaleDiv>(P, un, a);
   }
   if constexpr (SYNC) zero_exchange_stats(a, P);
   else stats_reduce_pass0(a, P.ws, P.stats);
@@ -261,11 +293,13 @@ int build_peer_sync(const nt_zero_sync* sync, int nranks, PeerSync& S, const cha
 
 
 // Copies count independent ranges (src[k] -> dst[k], `vectors` 16-byte vectors each) with
-// plain 16-byte loads and stores from the SMs, the access pattern of the ZeRO-1 pull and
-// push: pointing src at peers measures the inbound link, dst at peers the outbound one.
+// plain SM loads and stores, the access pattern of the ZeRO-1 pull and push: pointing src
+// at peers measures the inbound link, dst at peers the outbound one. H = 2: 32-byte
+// accesses (every pointer 32-byte aligned and an even vector count, as the reduce-scatter
+// takes them); H = 1: 16-byte.
 struct PeerCopyParams {
-  const uint4* src[NT_MAX_RANKS];
-  uint4* dst[NT_MAX_RANKS];
+  const char* src[NT_MAX_RANKS];
+  char* dst[NT_MAX_RANKS];
   int count;
   int64_t vectors;
 };
@@ -273,24 +307,32 @@ struct PeerCopyParams {
 constexpr int kPeerCopyThreads = 256;
 constexpr int kPeerCopyUnroll = 4;
 
+template <int H>
 __global__ void __launch_bounds__(kPeerCopyThreads) peer_copy_kernel(const __grid_constant__ PeerCopyParams P) {
   const int k = blockIdx.x % P.count;              // the blocks are dealt round robin to the ranges
   const int64_t block = blockIdx.x / P.count;
   const int64_t blocks = gridDim.x / P.count;
-  const uint4* src = P.src[k];
-  uint4* dst = P.dst[k];
+  const char* src = P.src[k];
+  char* dst = P.dst[k];
+  const int64_t n = P.vectors / H;
   const int64_t step = blocks * kPeerCopyThreads * kPeerCopyUnroll;
-  for (int64_t v0 = block * kPeerCopyThreads * kPeerCopyUnroll + threadIdx.x; v0 < P.vectors; v0 += step) {
-    uint4 r[kPeerCopyUnroll];
+  for (int64_t v0 = block * kPeerCopyThreads * kPeerCopyUnroll + threadIdx.x; v0 < n; v0 += step) {
+    uint4 r[kPeerCopyUnroll][H];
 #pragma unroll
     for (int u = 0; u < kPeerCopyUnroll; ++u) {
       const int64_t v = v0 + (int64_t)u * kPeerCopyThreads;
-      if (v < P.vectors) r[u] = __ldcs(src + v);
+      if (v < n) {
+        if constexpr (H == 2) load32_cs(src + v * 32, r[u][0], r[u][1]);
+        else r[u][0] = __ldcs(reinterpret_cast<const uint4*>(src) + v);
+      }
     }
 #pragma unroll
     for (int u = 0; u < kPeerCopyUnroll; ++u) {
       const int64_t v = v0 + (int64_t)u * kPeerCopyThreads;
-      if (v < P.vectors) __stcs(dst + v, r[u]);
+      if (v < n) {
+        if constexpr (H == 2) store32_cs(dst + v * 32, r[u][0], r[u][1]);
+        else __stcs(reinterpret_cast<uint4*>(dst) + v, r[u][0]);
+      }
     }
   }
 }
@@ -348,6 +390,9 @@ static int build_zero_reduce(const nt_zero_reduce_args* args, ZeroReduceParams& 
   P.ws = static_cast<StatsWorkspace*>(a.workspace);
   P.norm_type = 2.0;
   memset(&P.sync, 0, sizeof(P.sync));
+  bool a32 = (reinterpret_cast<uintptr_t>(a.dest) & 31u) == 0;
+  for (int q = 0; q < a.num_ranks && a.count > 0; ++q) a32 = a32 && (reinterpret_cast<uintptr_t>(a.sources[q]) & 31u) == 0;
+  P.vec32 = a32 ? 1 : 0;
   return NT_OK;
 }
 
@@ -459,17 +504,22 @@ int nt_peer_copy(const void* const* src, void* const* dst, int32_t count, uint64
       set_error("nt_peer_copy: range %d has a NULL or not 16-byte aligned pointer", k);
       return NT_EINVAL;
     }
-    P.src[k] = static_cast<const uint4*>(src[k]);
-    P.dst[k] = static_cast<uint4*>(dst[k]);
+    P.src[k] = static_cast<const char*>(src[k]);
+    P.dst[k] = static_cast<char*>(dst[k]);
   }
   P.count = count;
   P.vectors = (int64_t)(bytes_each / 16);
   if (P.vectors == 0) return NT_OK;
+  bool wide = bytes_each % 32 == 0;
+  for (int k = 0; k < count; ++k)
+    wide = wide && ((reinterpret_cast<uintptr_t>(src[k]) | reinterpret_cast<uintptr_t>(dst[k])) & 31u) == 0;
+  const int H = wide ? 2 : 1;
   int per = current_sm_count() * 4 / count;   // four 256-thread blocks per SM in all
   if (per < 1) per = 1;
-  const int64_t want = (P.vectors + kPeerCopyThreads * kPeerCopyUnroll - 1) / (kPeerCopyThreads * kPeerCopyUnroll);
+  const int64_t want = (P.vectors / H + kPeerCopyThreads * kPeerCopyUnroll - 1) / (kPeerCopyThreads * kPeerCopyUnroll);
   if (want < per) per = (int)want;
-  peer_copy_kernel<<<per * count, kPeerCopyThreads, 0, as_stream(stream)>>>(P);
+  if (wide) peer_copy_kernel<2><<<per * count, kPeerCopyThreads, 0, as_stream(stream)>>>(P);
+  else peer_copy_kernel<1><<<per * count, kPeerCopyThreads, 0, as_stream(stream)>>>(P);
   return launch_status("nt_peer_copy launch");
 }
 

@@ -45,7 +45,7 @@ def _expected(sources: list[np.ndarray], dtype, average: bool, scale):
     return dest, stats
 
 
-def _run_reduce(ranks, dtype, count, *, average=True, scale=None, poison=False, seed=0):
+def _run_reduce(ranks, dtype, count, *, average=True, scale=None, poison=False, seed=0, offset_bytes=0):
     rng = np.random.default_rng(seed)
     host = []
     for q in range(ranks):
@@ -54,8 +54,15 @@ def _run_reduce(ranks, dtype, count, *, average=True, scale=None, poison=False, 
             g[count // 3] = np.inf
             g[count // 2] = np.nan
         host.append(_round(g, dtype))
-    dev = [torch.from_numpy(h).to("cuda").to(dtype) for h in host]
-    dest = torch.full((count,), 7.0, dtype=dtype, device="cuda")
+    # offset_bytes shifts every source and the destination off the allocation's start: 16
+    # leaves them 16- but not 32-byte aligned, so the kernel takes its 16-byte accesses.
+    pad = offset_bytes // torch.empty(0, dtype=dtype).element_size()
+    dev = []
+    for h in host:
+        t = torch.empty(count + pad, dtype=dtype, device="cuda")
+        t[pad:] = torch.from_numpy(h).to("cuda").to(dtype)
+        dev.append(t[pad:])
+    dest = torch.full((count + pad,), 7.0, dtype=dtype, device="cuda")[pad:]
     stats = stats_tensor(torch.device("cuda"))
     scale_t = None if scale is None else torch.tensor([scale], dtype=torch.float32, device="cuda")
     k = CudaShardKernels(torch.device("cuda"))
@@ -76,6 +83,17 @@ def test_reduce_scatter_stats_matches_rank_order_f32_sum(cuda_device, ranks, dty
     assert s["nonfinite"] == ref["nonfinite"] == 0 and s["nan"] == ref["nan"] == 0
     assert s["maxabs"] == ref["maxabs"]
     assert abs(s["sumsq"] - ref["sumsq"]) <= 1e-12 * ref["sumsq"]
+
+
+@pytest.mark.parametrize("dtype", list(DTYPES), ids=list(DTYPES.values()))
+@pytest.mark.parametrize("ranks", [2, 4, 8])
+def test_reduce_scatter_stats_16_byte_aligned_sources(cuda_device, ranks, dtype):
+    """Sources and destination 16 bytes past a 32-byte boundary: the 16-byte access path,
+    with the same results as the 32-byte one."""
+    got, want, stats, ref = _run_reduce(ranks, dtype, 500_009, scale=1024.0, seed=10 + ranks, offset_bytes=16)
+    np.testing.assert_array_equal(got, want)
+    s = dict(zip(N.STATS_FIELDS, stats))
+    assert s["maxabs"] == ref["maxabs"] and abs(s["sumsq"] - ref["sumsq"]) <= 1e-12 * ref["sumsq"]
 
 
 @pytest.mark.parametrize("average,scale", [(False, None), (True, 3.0), (False, 65536.0)])
@@ -175,3 +193,28 @@ def test_adamw_push_skips_with_found_inf(cuda_device):
     assert int(steps[0]) == 0
     for peer in peers:
         assert not torch.any(peer.float() != 0)
+
+
+@pytest.mark.parametrize("count,bytes_each,offset", [(1, 1 << 20, 0), (2, (1 << 20) + 64, 0), (3, (1 << 20) + 48, 0), (2, 4096 + 32, 16),
+                                                     (4, 16, 0)])
+def test_peer_copy_copies_every_range(cuda_device, count, bytes_each, offset):
+    """nt_peer_copy on local buffers: 32-byte accesses (aligned pointers, size a multiple of
+    32) and 16-byte ones (pointers 16 bytes past a 32-byte boundary, or an odd 16-byte
+    count) copy every byte of every range and nothing past it."""
+    src = [torch.randint(0, 256, (bytes_each + offset + 64,), dtype=torch.uint8, device="cuda") for _ in range(count)]
+    dst = [torch.zeros(bytes_each + offset + 64, dtype=torch.uint8, device="cuda") for _ in range(count)]
+    N.peer_copy([s.data_ptr() + offset for s in src], [d.data_ptr() + offset for d in dst], bytes_each)
+    torch.cuda.synchronize()
+    for s, d in zip(src, dst):
+        assert torch.equal(d[offset:offset + bytes_each], s[offset:offset + bytes_each])
+        assert not torch.any(d[:offset]) and not torch.any(d[offset + bytes_each:])
+
+
+def test_peer_copy_rejects_bad_arguments(cuda_device):
+    buf = torch.zeros(256, dtype=torch.uint8, device="cuda")
+    with pytest.raises(ValueError, match="multiple of 16"):
+        N.peer_copy([buf.data_ptr()], [buf.data_ptr() + 128], 24)
+    with pytest.raises(ValueError, match="16-byte aligned"):
+        N.peer_copy([buf.data_ptr() + 8], [buf.data_ptr() + 128], 32)
+    with pytest.raises(ValueError, match="count"):
+        N.peer_copy([], [], 32)
