@@ -523,6 +523,11 @@ def run_ours(args):
     if breakdown:
         result["zero1_breakdown_ms"] = breakdown
         result["nvlink"] = nvlink_section(opt, P, world, ms, breakdown)
+        if opt.transport == "p2p":
+            # At N > 1 the update kernel also stores the bf16 copy into N - 1 peers: its floor
+            # is the longer of its HBM time and its outbound-link time at the push bandwidth
+            # measured in this run (the link from N = 4 on).
+            result["roofline"]["with_push"] = dict(result["nvlink"]["update_phase"])
     if world == 1:
         # Before the loop measurements below attach a learning-rate schedule to the optimizer.
         result["step_parity"] = single_parity(opt, scaler, params, loss)
@@ -662,7 +667,20 @@ def nvlink_section(opt, P: int, world: int, ms: float, breakdown: dict) -> dict:
             "floor_ms": floor_ms, "step_frac_of_floor": floor_ms / ms,
             "floor_with_hbm_ms": rs_ms + up_ms, "step_frac_of_floor_with_hbm": (rs_ms + up_ms) / ms,
             "reduce_scatter_gbs": rs_gbs, "reduce_scatter_frac_of_pull": rs_gbs / bw["pull_gbs"],
-            "update_push_gbs": push_gbs, "update_push_frac_of_push": push_gbs / bw["push_gbs"]}
+            "update_push_gbs": push_gbs, "update_push_frac_of_push": push_gbs / bw["push_gbs"],
+            "update_phase": {"floor_ms": up_ms, "frac_of_floor": up_ms / breakdown["update_with_overlapped_all_gather"],
+                             "bound": "nvlink" if link_bytes / (bw["push_gbs"] * 1e9) * 1e3 >= up_ms else "hbm"}}
+
+
+def parity_piece(opt):
+    """The largest parameter piece this rank owns: (index in the optimizer's registration
+    order, shard offset, length, the parameter). The index is the optimizer's own (its
+    parameters group by group), not the model's order, so the parameter and its group's
+    weight decay are looked up in `opt.params_list`."""
+    if not opt.pieces:
+        return 0, 0, 0, None
+    i, off, n, _ = max(opt.pieces, key=lambda t: t[2])
+    return i, off, n, opt.params_list[i]
 
 
 def zero_parity(opt, scaler, params, loss) -> dict:
@@ -684,11 +702,7 @@ def zero_parity(opt, scaler, params, loss) -> dict:
     import torch.distributed as dist
     from namitorch_b200.optim import clip_grad_norm_
     rank, world, device = opt.rank, opt.world, opt.device
-    # The slice: inside the largest parameter piece this rank owns.
-    if opt.pieces:
-        i, off, n, _ = max(opt.pieces, key=lambda t: t[2])
-    else:
-        i, off, n = 0, 0, 0
+    i, off, n, prm = parity_piece(opt)
     m = min(n, 1 << 20)
     rng = np.random.default_rng(1000 + rank)
     start = off + (int(rng.integers(0, n - m + 1)) if n > m else 0)
@@ -728,7 +742,7 @@ def zero_parity(opt, scaler, params, loss) -> dict:
     want_bits = torch.from_numpy(total).to(torch.bfloat16).view(torch.int16).numpy()
     reduce_bad = int(np.count_nonzero(want_bits != reduced_bits))
     reduced = torch.from_numpy(reduced_bits.copy()).view(torch.bfloat16).float().numpy()
-    group = next(g for g in opt.param_groups if any(q is params[i] for q in g["params"]))
+    group = next((g for g in opt.param_groups if any(q is prm for q in g["params"])), opt.param_groups[0])
     expect, checker = _shard_reference(pre, reduced, scale, norm, step_count, group, stepped, device)
     shard_bad = sum(int(np.count_nonzero(a.view(np.uint32) != b.view(np.uint32))) for a, b in zip(post, expect))
     t = torch.tensor([reduce_bad, shard_bad, m, int(len(set(digests)) == 1), int(stepped)], dtype=torch.float64,

@@ -55,3 +55,32 @@ def test_reference_arm_runs_the_reference_on_the_shared_sample(reference_install
     assert str(bench.CPU_SAMPLE_PARAMS) in ref["sample"] and ref["host"]["cpu_count"] >= 1
     port = bench.cpu_amp_sample(1, 2, warmup=0)
     assert port["kind"] == "port" and port["cores"] == 2 and str(bench.CPU_SAMPLE_PARAMS) in port["sample"]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_zero_parity_checks_the_group_the_optimizer_registered(world):
+    """ZeroAdamW indexes its pieces in registration order (the decay group's parameters,
+    then the no-decay group's), which is not the model's order. The slice the multi-GPU
+    self-check takes must be looked up in that order, or its weight decay comes from the
+    wrong group; at N = 4 and 8 on the 1.3B layout some ranks' largest piece is such a
+    parameter, and the check then reported every master element of those ranks wrong."""
+    from types import SimpleNamespace
+    from namitorch_b200 import workloads as W
+    from namitorch_b200.zero import interleaved_layout, owned_ranges, shard_pieces
+    shape = W.CONFIG_1P3B
+    numel = [int(np.prod(s)) for _, s in shape.shapes()]
+    decay, no_decay = shape.groups()
+    order = decay + no_decay
+    model = [SimpleNamespace(index=k) for k in range(len(numel))]
+    registered = [model[k] for k in order]
+    numels = [numel[k] for k in order]
+    offsets, total, c = interleaved_layout(numels, world, 1)
+    differs = 0
+    for rank in range(world):
+        opt = SimpleNamespace(pieces=shard_pieces(offsets, numels, owned_ranges(world, rank, 1, c)),
+                              params_list=registered)
+        i, off, n, prm = bench.parity_piece(opt)
+        assert n > 0 and prm is registered[i]
+        assert (prm.index in decay) == (i < len(decay))
+        differs += (i in decay) != (prm.index in decay)   # model order would pick the other group
+    assert differs == {2: 0, 4: 2, 8: 3}[world]
