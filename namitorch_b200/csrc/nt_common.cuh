@@ -139,6 +139,21 @@ __device__ __forceinline__ void store8_f32_v8(float* p, const float v[8]) {
                : "memory");
 }
 
+// 32 raw bytes in one streaming access (sm_100), as two 16-byte halves; `p` must be
+// 32-byte aligned. Read-only streams and peer reads move more per request than with
+// 16-byte loads.
+__device__ __forceinline__ void load32_cs(const void* p, uint4& lo, uint4& hi) {
+  asm volatile("ld.global.cs.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w), "=r"(hi.x), "=r"(hi.y), "=r"(hi.z), "=r"(hi.w)
+               : "l"(p));
+}
+
+__device__ __forceinline__ void store32_cs(void* p, const uint4& lo, const uint4& hi) {
+  asm volatile("st.global.cs.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(lo.x), "r"(lo.y),
+               "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w)
+               : "memory");
+}
+
 // ---- loss-scale handling -------------------------------------------------------------
 // Division by the loss scale, bit-identical to IEEE f32 division. When the scale is a
 // normal power of two its reciprocal is exact, and g * 2^-k rounds the same exact real

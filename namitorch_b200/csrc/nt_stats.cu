@@ -82,20 +82,46 @@ __device__ __forceinline__ void stats_scalar(float g, float scale, float inv, do
   }
 }
 
-// One chunk of one span: 16-byte vectors, U of them in flight per thread (guard-free full
-// rounds, then the remainder), then the elements after the last 16-byte boundary. T is the
-// block size of the launch (the kernel's shape, whichever path a thread takes).
+// Elements [begin, end) of one span. Thread t takes the vectors whose index is t modulo T,
+// U 16-byte vectors' worth in flight (guard-free full rounds, then the remainder): U / 2
+// 32-byte vectors when the range starts on a 32-byte boundary, else U 16-byte ones when it
+// starts on a 16-byte boundary; then the elements after the last full vector, one by one.
+// Every pass over the same range takes the same vectors in the same threads (the choice
+// depends only on the range), which the sum-of-squares pass relies on when a thread
+// re-reads its own elements.
+// T is the block size of the launch (the kernel's shape, whichever path a thread takes).
 template <int DT, int MODE, int VARIANT, int T, int U>
-__device__ __forceinline__ void stats_chunk(const StatsParams& P, const nt_span& sp, int64_t begin, int64_t end,
+__device__ __forceinline__ void stats_range(const StatsParams& P, const nt_span& sp, int64_t begin, int64_t end,
                                             float scale, float inv, double maxabs, StatsAcc& a) {
   constexpr int ES = DT == NT_F32 ? 4 : 2;
   constexpr int EPV = 16 / ES;
-  const char* base = static_cast<const char*>(sp.ptr);
+  const char* base = static_cast<const char*>(sp.ptr) + begin * ES;
   int64_t e = begin;
-  if (((reinterpret_cast<uintptr_t>(base + begin * ES)) & 15u) == 0) {
-    const uint4* vec = reinterpret_cast<const uint4*>(base + begin * ES);
-    const int nv = (int)((end - begin) / EPV);   // a chunk holds at most 2^31 elements
-    int v0 = threadIdx.x;
+  if ((reinterpret_cast<uintptr_t>(base) & 31u) == 0) {
+    constexpr int U2 = U > 1 ? U / 2 : 1;   // the same bytes in flight as U 16-byte vectors
+    const int64_t nv = (end - begin) / (2 * EPV);
+    int64_t v0 = threadIdx.x;
+    for (; v0 + (U2 - 1) * T < nv; v0 += U2 * T) {
+      uint4 raw[U2][2];
+#pragma unroll
+      for (int u = 0; u < U2; ++u) load32_cs(base + (v0 + u * T) * 32, raw[u][0], raw[u][1]);
+#pragma unroll
+      for (int u = 0; u < U2; ++u) {
+        stats_vector<DT, MODE, VARIANT>(raw[u][0], scale, inv, maxabs, P.p, a);
+        stats_vector<DT, MODE, VARIANT>(raw[u][1], scale, inv, maxabs, P.p, a);
+      }
+    }
+    for (; v0 < nv; v0 += T) {
+      uint4 lo, hi;
+      load32_cs(base + v0 * 32, lo, hi);
+      stats_vector<DT, MODE, VARIANT>(lo, scale, inv, maxabs, P.p, a);
+      stats_vector<DT, MODE, VARIANT>(hi, scale, inv, maxabs, P.p, a);
+    }
+    e = begin + nv * 2 * EPV;
+  } else if ((reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
+    const uint4* vec = reinterpret_cast<const uint4*>(base);
+    const int64_t nv = (end - begin) / EPV;
+    int64_t v0 = threadIdx.x;
     for (; v0 + (U - 1) * T < nv; v0 += U * T) {
       uint4 raw[U];
 #pragma unroll
@@ -104,14 +130,15 @@ __device__ __forceinline__ void stats_chunk(const StatsParams& P, const nt_span&
       for (int u = 0; u < U; ++u) stats_vector<DT, MODE, VARIANT>(raw[u], scale, inv, maxabs, P.p, a);
     }
     for (; v0 < nv; v0 += T) stats_vector<DT, MODE, VARIANT>(__ldcs(vec + v0), scale, inv, maxabs, P.p, a);
-    e = begin + (int64_t)nv * EPV;
+    e = begin + nv * EPV;
   }
   for (int64_t i = e + threadIdx.x; i < end; i += T)
     stats_scalar<DT, MODE, VARIANT>(load1<DT>(sp.ptr, i), scale, inv, maxabs, P.p, a);
 }
 
-// Each block takes a contiguous range of chunks: one span lookup per block, then the span
-// record is carried in registers and advanced as the chunks cross span boundaries.
+// Each block takes a contiguous range of chunks [c0, c1). The chunks of one span inside it
+// are contiguous in memory, so the block reads them as one range (one span lookup per
+// block; empty spans own no chunk and are stepped over).
 template <int DT, int MODE, int VARIANT, int T, int U>
 __device__ __forceinline__ void stats_all_chunks(const StatsParams& P, float scale, float inv, double maxabs,
                                                  StatsAcc& a) {
@@ -120,18 +147,16 @@ __device__ __forceinline__ void stats_all_chunks(const StatsParams& P, float sca
   const int64_t c1 = c0 + per < P.nchunks ? c0 + per : P.nchunks;
   if (c0 >= c1) return;
   int s = find_owner([&](int i) { return P.spans[i].chunk_begin; }, P.nspan, c0);
-  nt_span sp = P.spans[s];
-  int64_t next_begin = s + 1 < P.nspan ? P.spans[s + 1].chunk_begin : INT64_MAX;
-  for (int64_t chunk = c0; chunk < c1; ++chunk) {
-    while (chunk >= next_begin) {
-      ++s;
-      sp = P.spans[s];
-      next_begin = s + 1 < P.nspan ? P.spans[s + 1].chunk_begin : INT64_MAX;
-    }
-    const int64_t begin = (chunk - sp.chunk_begin) * (int64_t)P.chunk_elems;
-    int64_t end = begin + P.chunk_elems;
+  for (int64_t c = c0; c < c1 && s < P.nspan; ++s) {
+    const nt_span sp = P.spans[s];
+    const int64_t next_begin = s + 1 < P.nspan ? P.spans[s + 1].chunk_begin : INT64_MAX;
+    const int64_t stop = c1 < next_begin ? c1 : next_begin;
+    if (stop <= c) continue;
+    const int64_t begin = (c - sp.chunk_begin) * (int64_t)P.chunk_elems;
+    int64_t end = (stop - sp.chunk_begin) * (int64_t)P.chunk_elems;
     if (end > sp.count) end = sp.count;
-    stats_chunk<DT, MODE, VARIANT, T, U>(P, sp, begin, end, scale, inv, maxabs, a);
+    stats_range<DT, MODE, VARIANT, T, U>(P, sp, begin, end, scale, inv, maxabs, a);
+    c = stop;
   }
 }
 

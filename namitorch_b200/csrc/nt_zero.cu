@@ -57,20 +57,6 @@ __device__ __forceinline__ float average(float sum, const ZeroReduceParams& P) {
   return sum;
 }
 
-// 32 bytes from global memory in one access (sm_100), streaming: peer reads over NVLink
-// carry more per request than with 16-byte loads when both directions of a link are busy.
-__device__ __forceinline__ void load32_cs(const void* p, uint4& lo, uint4& hi) {
-  asm volatile("ld.global.cs.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w), "=r"(hi.x), "=r"(hi.y), "=r"(hi.z), "=r"(hi.w)
-               : "l"(p));
-}
-
-__device__ __forceinline__ void store32_cs(void* p, const uint4& lo, const uint4& hi) {
-  asm volatile("st.global.cs.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(lo.x), "r"(lo.y),
-               "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w)
-               : "memory");
-}
-
 // NR > 0: the rank count is a compile-time constant (2, 4, 8); NR == 0: any count up to
 // NT_MAX_RANKS, one vector per source in flight. H = 2: each access moves 32 bytes (every
 // source and the destination 32-byte aligned); H = 1: 16 bytes. The statistics see exactly
