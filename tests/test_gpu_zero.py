@@ -26,7 +26,15 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out_path, transport, lazy, exchange, norm_type=2.0):
+def _round_to(dtype: str):
+    """float32 -> the model dtype (round to nearest even) -> float32."""
+    from oracle.casts import round_to_bf16
+    if dtype == "f16":
+        return lambda x: np.asarray(x, np.float32).astype(np.float16).astype(np.float32)
+    return round_to_bf16
+
+
+def _worker(rank, world, port, out_path, transport, lazy, exchange, norm_type=2.0, dtype="bf16"):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -36,24 +44,25 @@ def _worker(rank, world, port, out_path, transport, lazy, exchange, norm_type=2.
         from namitorch_b200.optim import clip_grad_norm_, defer_gradient_transforms
         from namitorch_b200.zero import ZeroAdamW
         defer_gradient_transforms(lazy)
-        from oracle.casts import round_to_bf16
+        round_grad = _round_to(dtype)
+        model_dtype = torch.float16 if dtype == "f16" else torch.bfloat16
         shape = W.CONFIG_SMALL
         params = [torch.nn.Parameter(torch.from_numpy(a).cuda()) for a in W.init_params(shape, seed=0)]
         decay, no_decay = shape.groups()
         groups = [{"params": [params[i] for i in decay], "weight_decay": 0.1},
                   {"params": [params[i] for i in no_decay], "weight_decay": 0.0}]
-        opt = ZeroAdamW(groups, lr=3e-4, model_dtype=torch.bfloat16, transport=transport, exchange=exchange)
+        opt = ZeroAdamW(groups, lr=3e-4, model_dtype=model_dtype, transport=transport, exchange=exchange)
         assert opt.transport == transport
         scaler = GradScaler(1024.0, growth_interval=2)
         reduced, local, norms, stepped = [], [], [], []
         for step in range(4):
             opt.zero_grad()
-            grads = [round_to_bf16(g * np.float32(scaler.get_scale()))
+            grads = [round_grad(g * np.float32(scaler.get_scale()))
                      for g in W.outlier_grads(shape, seed=10 * step + rank)]
             if step == 2 and rank == 1:
                 grads[5].reshape(-1)[3] = np.inf
             for p, g in zip(params, grads):
-                p.grad.copy_(torch.from_numpy(g).to(torch.bfloat16))
+                p.grad.copy_(torch.from_numpy(g).to(model_dtype))
             local.append(opt.flat_grads.float().cpu().numpy())
             if not lazy:
                 # The eager path rewrites the reduced shard in place: read it before.
@@ -86,10 +95,11 @@ def _worker(rank, world, port, out_path, transport, lazy, exchange, norm_type=2.
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport,lazy,exchange,norm_type", [
-    ("nccl", True, "flags", 2.0), ("p2p", True, "flags", 2.0), ("p2p", False, "flags", 2.0),
-    ("p2p", True, "nccl", 2.0), ("p2p", True, "flags", float("inf")), ("p2p", True, "flags", 3.0)])
-def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange, norm_type):
+@pytest.mark.parametrize("transport,lazy,exchange,norm_type,dtype", [
+    ("nccl", True, "flags", 2.0, "bf16"), ("p2p", True, "flags", 2.0, "bf16"), ("p2p", False, "flags", 2.0, "bf16"),
+    ("p2p", True, "nccl", 2.0, "bf16"), ("p2p", True, "flags", float("inf"), "bf16"),
+    ("p2p", True, "flags", 3.0, "bf16"), ("p2p", False, "flags", 2.0, "f16")])
+def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange, norm_type, dtype):
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     import torch.multiprocessing as mp
@@ -97,10 +107,10 @@ def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange, norm_type):
     from oracle import adamw as oadamw
     from oracle import amp as oamp
     from oracle import clip as oclip
-    from oracle.casts import f32_to_bf16_bits, round_to_bf16
     out_path = tmp_path / "zero.npz"
-    mp.spawn(_worker, args=(WORLD, _free_port(), str(out_path), transport, lazy, exchange, norm_type), nprocs=WORLD,
-             join=True)
+    mp.spawn(_worker, args=(WORLD, _free_port(), str(out_path), transport, lazy, exchange, norm_type, dtype),
+             nprocs=WORLD, join=True)
+    round_model = _round_to(dtype)
     out = np.load(out_path)
     shape = W.CONFIG_SMALL
     offsets = out["offsets"]
@@ -121,8 +131,8 @@ def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange, norm_type):
         for q in range(1, WORLD):
             total = total + local[q].astype(np.float32)
         with np.errstate(invalid="ignore"):
-            expect = round_to_bf16(total * np.float32(1.0 / WORLD))
-        np.testing.assert_array_equal(f32_to_bf16_bits(out["reduced"]), f32_to_bf16_bits(expect))
+            expect = round_model(total * np.float32(1.0 / WORLD))
+        np.testing.assert_array_equal(out["reduced"], expect)
     params = W.init_params(shape, seed=0)
     decay, no_decay = shape.groups()
     base = {"lr": 3e-4, "betas": (0.9, 0.999), "eps": 1e-8, "maximize": False}
@@ -144,11 +154,11 @@ def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange, norm_type):
         probe = [None if g is None else g.copy() for g in grads]
         if oamp.OracleGradScaler(oscaler.scale).unscale(probe):
             if not lazy:
-                probe = [None if g is None else round_to_bf16(g) for g in probe]
+                probe = [None if g is None else round_model(g) for g in probe]
             ref_norm = float(oclip.total_norm([g for g in probe if g is not None], norm_type))
             assert abs(out["norms"][step] - ref_norm) <= 1e-12 * ref_norm
         r = oamp.amp_step(oracle, oscaler, grads, max_norm=1.0, norm_type=norm_type,
-                          storage=None if lazy else round_to_bf16, given_norm=float(out["norms"][step]))
+                          storage=None if lazy else round_model, given_norm=float(out["norms"][step]))
         assert bool(out["stepped"][step]) == r["stepped"]
     assert float(out["scale"]) == oscaler.scale
     assert out["steps"].tolist() == [3] * len(numels)
@@ -157,8 +167,8 @@ def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange, norm_type):
         np.testing.assert_array_equal(out[f"master{k}"].view(np.uint32), params[orig].view(np.uint32))
         np.testing.assert_array_equal(out[f"m{k}"].view(np.uint32),
                                       oracle.state[orig]["exp_avg"].view(np.uint32))
-        # The all-gathered model copy is the bf16 rounding of the gathered master.
-        assert np.array_equal(f32_to_bf16_bits(out[f"copy{orig}"]), f32_to_bf16_bits(out[f"master{k}"]))
+        # The all-gathered model copy is the model-dtype rounding of the gathered master.
+        np.testing.assert_array_equal(out[f"copy{orig}"], round_model(out[f"master{k}"]))
 
 
 def _stall_worker(rank, world, port, store_port, out_path):
