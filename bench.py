@@ -42,6 +42,7 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 METRIC = "AdamW+AMP step params/s (achieved HBM GB/s vs B200 peak)"
+DEFAULT_PULL = "sm"   # how the ZeRO-1 reduce-scatter reads the peers at N > 1: SM loads or copy engines
 FALLBACK_HBM_GBS = 6650.0
 BYTES_UPDATE = 28      # adamw_mt: R p4 g2 m4 v4 + W p4 m4 v4 copy2 per parameter
 BYTES_STATS = 2        # grad_stats: R g2 per parameter
@@ -63,6 +64,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--zero-transport", choices=["auto", "p2p", "nccl"], default="auto",
                     help="ZeRO-1 exchange at N>1: fused kernels over peer memory, or NCCL collectives")
+    ap.add_argument("--zero-pull", choices=["sm", "copy"], default=DEFAULT_PULL,
+                    help="N > 1, p2p transport: the reduce-scatter reads the peers with SM loads or copy engines")
     ap.add_argument("--no-nccl-compare", action="store_true",
                     help="at N>1 with the p2p transport, skip the NCCL-transport comparison run")
     ap.add_argument("--no-extra", action="store_true",
@@ -346,7 +349,7 @@ def group_params(shape, params, wd=0.1):
             {"params": [params[i] for i in no_decay], "weight_decay": 0.0}]
 
 
-def build_step(shape, device, rank, world, transport, seed_params=0, exchange="flags"):
+def build_step(shape, device, rank, world, transport, seed_params=0, exchange="flags", pull="sm"):
     """(optimizer, scaler, params, flat gradient buffer, loss, step function) of the AMP step
     on `shape`: AdamW (ZeroAdamW over the process group at N > 1) with a bf16 model copy and
     bf16 gradients N(0, 1e-3) x 65536, GradScaler(65536), clip_grad_norm_ 1.0."""
@@ -358,7 +361,7 @@ def build_step(shape, device, rank, world, transport, seed_params=0, exchange="f
     if world > 1:
         from namitorch_b200.zero import ZeroAdamW
         opt = ZeroAdamW(group_params(shape, params), lr=3e-4, betas=(0.9, 0.999), eps=1e-8,
-                        model_dtype=torch.bfloat16, transport=transport, exchange=exchange)
+                        model_dtype=torch.bfloat16, transport=transport, exchange=exchange, pull=pull)
         flat_grads = opt.flat_grads
         with torch.no_grad():
             gen = torch.Generator(device=device)
@@ -424,7 +427,8 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
     shape = shape_for(args.workload)
     P = shape.numel()
-    opt, scaler, params, flat_grads, loss, plain_step = build_step(shape, device, rank, world, args.zero_transport)
+    opt, scaler, params, flat_grads, loss, plain_step = build_step(shape, device, rank, world, args.zero_transport,
+                                                                   pull=args.zero_pull)
     stream = torch.cuda.current_stream()
     ev = []
     phases = []   # ZeRO-1: the optimizer's own events (reduce-scatter, stats, update, all-gather tail)
@@ -501,7 +505,8 @@ def run_ours(args):
         "config": {"workload": f"{shape.name} AdamW+AMP step (BASELINE config 3; fp32 master/moments, bf16 grads "
                                "and model copy, GradScaler, clip_grad_norm_ 1.0, 2 param groups)",
                    "params": P, "tensors": len(params),
-                   "parallelism": (f"zero1-dp{world}-{opt.transport}" + ("-flags" if opt._uses_flags() else ""))
+                   "parallelism": (f"zero1-dp{world}-{opt.transport}" + ("-flags" if opt._uses_flags() else "")
+                                   + ("-copy-pull" if opt._uses_flags() and opt._pull == "copy" else ""))
                    if world > 1 else "single",
                    "l2": "inputs larger than L2 (30 B/param x 1.3B per step)", "grad_dtype": "bf16",
                    "model_dtype": "bf16"},
@@ -841,12 +846,14 @@ def nccl_comparison(shape, device, rank, world, steps: int = 10, warmup: int = 3
     line (peer-memory kernels ordered by in-kernel flags): ``nccl`` is the NCCL transport
     (reduce-scatter, statistics all-reduce, per-piece update + all-gather on a side stream);
     ``p2p_nccl_barriers`` is the peer-memory kernels ordered by NCCL calls between them (two
-    4-byte all-reduce barriers and the statistics all-reduce)."""
+    4-byte all-reduce barriers and the statistics all-reduce), reading the peers with SM
+    loads."""
     import torch
     out = {}
-    for name, transport, exchange in (("nccl", "nccl", "flags"), ("p2p_nccl_barriers", "p2p", "nccl")):
+    runs = [("nccl", "nccl", "flags", "sm"), ("p2p_nccl_barriers", "p2p", "nccl", "sm")]
+    for name, transport, exchange, pull in runs:
         opt, scaler, params, flat_grads, loss, step = build_step(shape, device, rank, world, transport,
-                                                                 exchange=exchange)
+                                                                 exchange=exchange, pull=pull)
         ms = device_timed(step, steps, warmup, world)
         out[name] = {"ms_per_step": ms, "value": shape.numel() / (ms / 1e3), "unit": "params/s", "steps": steps,
                      "warmup": warmup, "pieces": opt._pieces, "transport": opt.transport}

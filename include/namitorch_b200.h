@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define NT_ABI_VERSION 7
+#define NT_ABI_VERSION 8
 #define NT_MAX_GROUPS 32      /* coefficient groups per nt_adamw_mt call */
 #define NT_MAX_FOUND_INF 16   /* optimizers combined by one nt_scaler_update call */
 
@@ -499,6 +499,20 @@ typedef struct nt_zero_sync {
    bounded by sync->timeout_ns. */
 int nt_zero_reduce_scatter_exchange(const nt_zero_reduce_args* args, const nt_zero_sync* sync, double norm_type,
                                     void* stream);
+
+/* The exchanges of nt_zero_reduce_scatter_exchange as kernels of their own, for a
+   reduce-scatter whose peer reads are copy-engine copies into local staging buffers (which
+   keep more of each link busy than SM loads when both directions carry data):
+   nt_zero_flag_exchange signals `flag` (NT_ZERO_READY before the copies, NT_ZERO_DONE after
+   the last pushes) and waits for every rank's, bounded by sync->timeout_ns; *status (if
+   given) becomes 0, or 1 if the wait ran out (also error bit 0 for READY / STATS, bit 1 for
+   DONE). nt_zero_stats_exchange adds `count` statistics records in order (the pieces of the
+   shard, each reduced by nt_zero_reduce_scatter_stats from the staged copies), exchanges
+   the totals and finalizes `out` with `norm_type` (2 or inf) as the fused kernel does; a
+   nonzero *ready_status skips the exchange and reports found_inf with a NaN norm. */
+int nt_zero_flag_exchange(const nt_zero_sync* sync, int32_t num_ranks, int32_t flag, uint32_t* status, void* stream);
+int nt_zero_stats_exchange(const nt_stats* records, int32_t count, const nt_zero_sync* sync, int32_t num_ranks,
+                           const uint32_t* ready_status, double norm_type, nt_stats* out, void* stream);
 
 /* nt_adamw_mt_push followed, in the same kernel, by the closing exchange: once every block's
    stores (its own copy and the peers') are complete, the last block signals DONE to every

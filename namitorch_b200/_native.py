@@ -22,7 +22,7 @@ NT_DECAY_NONE, NT_DECAY_DECOUPLED, NT_DECAY_COUPLED = 0, 1, 2
 NT_MAX_GROUPS = 32
 NT_MAX_FOUND_INF = 16
 NT_MAX_RANKS = 8
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 
 class Segment(C.Structure):
@@ -182,6 +182,9 @@ SIGNATURES: dict[str, tuple] = {
     "nt_zero_reduce_scatter_stats": (C.c_int, [C.POINTER(ZeroReduceArgs), C.c_void_p]),
     "nt_adamw_mt_push": (C.c_int, [C.POINTER(AdamWMtArgs), C.POINTER(C.c_void_p), C.c_int32, C.c_void_p]),
     "nt_peer_copy": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.c_int32, C.c_uint64, C.c_void_p]),
+    "nt_zero_flag_exchange": (C.c_int, [C.POINTER(ZeroSync), C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
+    "nt_zero_stats_exchange": (C.c_int, [C.c_void_p, C.c_int32, C.POINTER(ZeroSync), C.c_int32, C.c_void_p,
+                                         C.c_double, C.c_void_p, C.c_void_p]),
     "nt_zero_reduce_scatter_exchange": (C.c_int, [C.POINTER(ZeroReduceArgs), C.POINTER(ZeroSync), C.c_double,
                                                    C.c_void_p]),
     "nt_adamw_mt_push_exchange": (C.c_int, [C.POINTER(AdamWMtArgs), C.POINTER(C.c_void_p), C.c_int32,
@@ -248,6 +251,7 @@ def check(status: int, what: str = "") -> None:
 # benchmark's launch count; the statistics entry point launches one kernel per call).
 LAUNCHES_PER_CALL = {"nt_adamw_f32": 1, "nt_adamw_mt": 1, "nt_adamw_mt_push": 1, "nt_zero_reduce_scatter_stats": 1, "nt_peer_copy": 1,
                      "nt_zero_reduce_scatter_exchange": 1, "nt_adamw_mt_push_exchange": 1,
+                     "nt_zero_flag_exchange": 1, "nt_zero_stats_exchange": 1,
                      "nt_grad_stats": 1, "nt_grad_stats_finalize": 1, "nt_schedule_step": 1, "nt_row_softmax": 1, "nt_norm_forward": 1,
                      "nt_grad_transform": 1, "nt_grad_clip_value": 1, "nt_scaler_update": 1,
                      "nt_softmax_xent": 2, "nt_xent_backward_scale": 1, "nt_cast": 1, "nt_fused_elementwise": 1}

@@ -131,6 +131,38 @@ __device__ __forceinline__ void zero_reduce_width(const ZeroReduceParams& P, con
   else zero_reduce_body<DT, NR, MODE, 1>(P, un, a);
 }
 
+// One thread: sends this rank's shard totals {sum of squares, non-finite count, NaN count,
+// max |g|} to every rank's mailbox, signals STATS, waits for every rank's (bounded), adds the
+// N totals in rank order (the same doubles in the same order on every rank, so every rank
+// finalizes the same found_inf and norm) and finalizes into `st`. With `ok` false (an
+// earlier wait of this step ran out), or when this wait runs out, the record reports
+// found_inf with a NaN norm, so the update skips, and bit 0 of the error word is set.
+__device__ __forceinline__ void exchange_shard_totals(const PeerSync& S, bool ok, double ss, double nfd, double nnd,
+                                                      double mx, double norm_type, nt_stats* st) {
+  if (ok) {
+    for (int q = 0; q < S.nranks; ++q) {
+      double* slot = S.box[q]->stats[S.rank];
+      slot[0] = ss; slot[1] = nfd; slot[2] = nnd; slot[3] = mx;
+    }
+    signal_all(S, NT_ZERO_STATS);   // the release orders the four stores above before it
+    ok = wait_all(S, NT_ZERO_STATS);
+  }
+  if (ok) {
+    const volatile nt_zero_mailbox* own = S.box[S.rank];
+    double gs = 0.0, gnf = 0.0, gnn = 0.0, gmx = 0.0;
+    for (int q = 0; q < S.nranks; ++q) {
+      gs += own->stats[q][0]; gnf += own->stats[q][1]; gnn += own->stats[q][2];
+      gmx = fmax(gmx, own->stats[q][3]);
+    }
+    st->sumsq = gs; st->nonfinite = gnf; st->nan = gnn; st->maxabs = gmx;
+    stats_finalize(st, norm_type);
+  } else {
+    atomicOr(S.error, 1);
+    const double nan = __longlong_as_double(0x7ff8000000000000ll);
+    st->sumsq = nan; st->nonfinite = 1.0; st->nan = 1.0; st->maxabs = nan; st->norm = nan; st->found_inf = 1.0;
+  }
+}
+
 // The exchange variant's end: the block partials are reduced in a fixed order by the last
 // block, which sends the shard's totals to every rank's mailbox, waits for every rank's,
 // adds them in rank order (the same doubles in the same order on every rank, so every rank
@@ -161,31 +193,8 @@ __device__ __forceinline__ void zero_exchange_stats(const StatsAcc& a, const Zer
   nnd = block_reduce(nnd, red_d, SumOp(), 0.0);
   mx = block_reduce(mx, red_f, MaxOp(), 0.0f);
   if (threadIdx.x != 0) return;
-  const PeerSync& S = P.sync;
-  bool ok = *reinterpret_cast<volatile unsigned*>(&P.ws->pad[0]) == 0u;   // every block saw every rank READY
-  if (ok) {
-    for (int q = 0; q < S.nranks; ++q) {
-      double* slot = S.box[q]->stats[S.rank];
-      slot[0] = ss; slot[1] = nfd; slot[2] = nnd; slot[3] = (double)mx;
-    }
-    signal_all(S, NT_ZERO_STATS);   // the release orders the four stores above before it
-    ok = wait_all(S, NT_ZERO_STATS);
-  }
-  nt_stats* st = P.stats;
-  if (ok) {
-    const volatile nt_zero_mailbox* own = S.box[S.rank];
-    double gs = 0.0, gnf = 0.0, gnn = 0.0, gmx = 0.0;
-    for (int q = 0; q < S.nranks; ++q) {
-      gs += own->stats[q][0]; gnf += own->stats[q][1]; gnn += own->stats[q][2];
-      gmx = fmax(gmx, own->stats[q][3]);
-    }
-    st->sumsq = gs; st->nonfinite = gnf; st->nan = gnn; st->maxabs = gmx;
-    stats_finalize(st, P.norm_type);
-  } else {
-    atomicOr(S.error, 1);
-    const double nan = __longlong_as_double(0x7ff8000000000000ll);
-    st->sumsq = nan; st->nonfinite = 1.0; st->nan = 1.0; st->maxabs = nan; st->norm = nan; st->found_inf = 1.0;
-  }
+  const bool ready = *reinterpret_cast<volatile unsigned*>(&P.ws->pad[0]) == 0u;   // every block saw every rank READY
+  exchange_shard_totals(P.sync, ready, ss, nfd, nnd, (double)mx, P.norm_type, P.stats);
   P.ws->pad[0] = 0u;
   P.ws->counter = 0u;
 }
@@ -216,6 +225,31 @@ __global__ void __launch_bounds__(kZeroThreads, 2) zero_reduce_stats_kernel(cons
   }
   if constexpr (SYNC) zero_exchange_stats(a, P);
   else stats_reduce_pass0(a, P.ws, P.stats);
+}
+
+// One thread: this rank's `flag` for the epoch into every rank's mailbox, then a bounded
+// wait for every rank's. `status` (if given) records 0 (every rank arrived) or 1 (the wait
+// ran out, which also sets `error_bit` in the sticky error word).
+__global__ void zero_flag_kernel(const PeerSync S, int flag, uint32_t* status, int error_bit) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  signal_all(S, flag);
+  const bool ok = wait_all(S, flag);
+  if (status) *status = ok ? 0u : 1u;
+  if (!ok) atomicOr(S.error, error_bit);
+}
+
+// One thread: adds `count` shard statistics records in order (the pieces of this rank's
+// shard, reduced one launch each) and runs the statistics exchange on their totals.
+__global__ void zero_records_exchange_kernel(const nt_stats* records, int count, const PeerSync S,
+                                             const uint32_t* ready_status, double norm_type, nt_stats* out) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  double ss = 0.0, nfd = 0.0, nnd = 0.0, mx = 0.0;
+  for (int k = 0; k < count; ++k) {
+    ss += records[k].sumsq; nfd += records[k].nonfinite; nnd += records[k].nan;
+    mx = fmax(mx, records[k].maxabs);
+  }
+  const bool ready = ready_status == nullptr || *reinterpret_cast<const volatile uint32_t*>(ready_status) == 0u;
+  exchange_shard_totals(S, ready, ss, nfd, nnd, mx, norm_type, out);
 }
 
 template <int DT, int NR, bool SYNC>
@@ -473,6 +507,47 @@ int nt_zero_reduce_scatter_exchange(const nt_zero_reduce_args* args, const nt_ze
   if (rc) return rc;
   P.norm_type = norm_type;
   return dispatch_dtype<true>(P, args->dtype, as_stream(stream), what);
+}
+
+int nt_zero_flag_exchange(const nt_zero_sync* sync, int32_t num_ranks, int32_t flag, uint32_t* status, void* stream) {
+  nt::TraceRange trace("nt_zero_flag_exchange");
+  const char* what = "nt_zero_flag_exchange";
+  if (num_ranks < 1 || num_ranks > NT_MAX_RANKS) {
+    set_error("%s: num_ranks must be in [1, %d] (got %d)", what, NT_MAX_RANKS, num_ranks);
+    return NT_EINVAL;
+  }
+  if (flag < NT_ZERO_READY || flag > NT_ZERO_DONE) {
+    set_error("%s: flag must be NT_ZERO_READY, NT_ZERO_STATS or NT_ZERO_DONE (got %d)", what, flag);
+    return NT_EINVAL;
+  }
+  PeerSync S;
+  int rc = build_peer_sync(sync, num_ranks, S, what);
+  if (rc) return rc;
+  zero_flag_kernel<<<1, 32, 0, as_stream(stream)>>>(S, flag, status, flag == NT_ZERO_DONE ? 2 : 1);
+  return launch_status("nt_zero_flag_exchange launch");
+}
+
+int nt_zero_stats_exchange(const nt_stats* records, int32_t count, const nt_zero_sync* sync, int32_t num_ranks,
+                           const uint32_t* ready_status, double norm_type, nt_stats* out, void* stream) {
+  nt::TraceRange trace("nt_zero_stats_exchange");
+  const char* what = "nt_zero_stats_exchange";
+  if (num_ranks < 1 || num_ranks > NT_MAX_RANKS) {
+    set_error("%s: num_ranks must be in [1, %d] (got %d)", what, NT_MAX_RANKS, num_ranks);
+    return NT_EINVAL;
+  }
+  if (count < 1 || !records || !out) {
+    set_error("%s: needs at least one record and an output record", what);
+    return NT_EINVAL;
+  }
+  if (!(norm_type == 2.0 || isinf(norm_type))) {
+    set_error("%s: norm_type must be 2 or inf (another norm needs a second pass)", what);
+    return NT_EINVAL;
+  }
+  PeerSync S;
+  int rc = build_peer_sync(sync, num_ranks, S, what);
+  if (rc) return rc;
+  zero_records_exchange_kernel<<<1, 32, 0, as_stream(stream)>>>(records, count, S, ready_status, norm_type, out);
+  return launch_status("nt_zero_stats_exchange launch");
 }
 
 int nt_peer_copy(const void* const* src, void* const* dst, int32_t count, uint64_t bytes_each, void* stream) {

@@ -21,7 +21,12 @@ One step has two exchanges around the update, over one of two transports:
      waits for everyone's (all gradients final); it pulls its shard range from every rank's
      gradient buffer, sums in f32 in rank order, writes the reduced shard and the shard's
      statistics; then it sends those statistics to every rank, waits for everyone's, adds
-     them in rank order and finalizes: every rank holds the same found_inf and global norm;
+     them in rank order and finalizes: every rank holds the same found_inf and global norm.
+     With ``pull="copy"`` the copy engines read the peers instead of the SMs: a READY
+     exchange kernel, one cudaMemcpyAsync per peer and range of the shard into local staging
+     on a copy stream, the same reduction per range as each range's copies land, and a
+     STATS exchange kernel over the range statistics (the copy engines keep more of each
+     link busy than SM loads when both directions carry data);
   2. ``nt_adamw_mt_push_exchange``: the fused AdamW kernel (unscale, skip, clip, update)
      stores each bf16 result into its own model copy and into every peer's (the
      all-gather), then signals DONE and waits for everyone's: every push has landed and
@@ -56,6 +61,7 @@ _POWSUM = N.STATS_FIELDS.index("powsum")
 
 
 DEFAULT_PIECES = 8
+COPY_PULL_PIECES = 8   # ranges of the shard in the copy-engine pull (copies of one overlap the reduction of another)
 
 
 def interleaved_layout(numels: list[int], world: int, pieces: int = DEFAULT_PIECES):
@@ -146,6 +152,19 @@ class CudaShardKernels:
         N.call("nt_zero_reduce_scatter_exchange", N.C.byref(args), N.C.byref(sync), float(norm_type),
                N.stream_handle())
 
+    def flag_exchange(self, sync, num_ranks, flag, status=None):
+        """Signals `flag` to every rank and waits (bounded) for every rank's; `status` (int32,
+        one element) records 0 or 1 (the wait ran out)."""
+        N.call("nt_zero_flag_exchange", N.C.byref(sync), int(num_ranks), int(flag),
+               None if status is None else status.data_ptr(), N.stream_handle())
+
+    def stats_exchange(self, records, sync, num_ranks, ready_status, out, norm_type=2.0):
+        """Adds the rows of `records` (statistics of the shard's pieces) in order, exchanges
+        the totals with every rank and finalizes `out` (global and the same on every rank)."""
+        N.call("nt_zero_stats_exchange", records.data_ptr(), int(records.shape[0]), N.C.byref(sync),
+               int(num_ranks), None if ready_status is None else ready_status.data_ptr(), float(norm_type),
+               out.data_ptr(), N.stream_handle())
+
     def update(self, *, master, exp_avg, exp_avg_sq, copy, grad_dtype, segments, num_segments, num_chunks, steps,
                corrections, capacity, scale, stats, skip, max_norm, groups, peers=None, schedule=None, sync=None):
         group_array = (N.AdamWGroup * len(groups))(*groups)
@@ -186,7 +205,7 @@ class ZeroAdamW(_FirstOrderAdam):
     def __init__(self, params, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 1e-2,
                  *, maximize: bool = False, model_dtype=torch.bfloat16, process_group=None, average_grads: bool = True,
                  pieces: int = DEFAULT_PIECES, transport: str = "auto", exchange: str = "flags",
-                 exchange_timeout: float = 10.0, _kernels=None):
+                 exchange_timeout: float = 10.0, pull: str = "sm", _kernels=None):
         if model_dtype not in (torch.bfloat16, torch.float16, torch.float32):
             raise TypeError("model_dtype must be torch.bfloat16, torch.float16 or torch.float32.")
         self._group = process_group
@@ -197,6 +216,11 @@ class ZeroAdamW(_FirstOrderAdam):
             raise ValueError("transport must be 'auto', 'p2p' or 'nccl'.")
         if exchange not in ("flags", "nccl"):
             raise ValueError("exchange must be 'flags' or 'nccl'.")
+        if pull not in ("sm", "copy"):
+            raise ValueError("pull must be 'sm' or 'copy'.")
+        if pull == "copy" and exchange != "flags":
+            raise ValueError("pull='copy' orders its copies with the in-kernel flags: it needs exchange='flags'.")
+        self._pull = pull
         if not (isinstance(exchange_timeout, (int, float)) and 0 < exchange_timeout <= 3600):
             raise ValueError("exchange_timeout must be a number of seconds in (0, 3600].")
         self._exchange = exchange
@@ -278,6 +302,8 @@ class ZeroAdamW(_FirstOrderAdam):
             self._sync = torch.zeros(1, dtype=torch.int32, device=device)
             self._mailbox = torch.zeros(N.C.sizeof(N.ZeroMailbox), dtype=torch.uint8, device=device)
             self._exchange_error = torch.zeros(1, dtype=torch.int32, device=device)
+            if self._pull == "copy":
+                self._build_copy_pull(shard)
             self._map_peers()
         for p in params:
             _OWNERS[id(p)] = self
@@ -357,6 +383,52 @@ class ZeroAdamW(_FirstOrderAdam):
             self._peer_maps.append(m)
             self._mailboxes.append(m)
         dist.barrier(group=self._group)
+
+    def _build_copy_pull(self, shard: int) -> None:
+        """State of the copy-engine pull: one staging buffer per peer for this rank's shard,
+        the shard cut into COPY_PULL_PIECES ranges (64-element multiples) so that the local
+        reduction of one range runs while the copies of the next are in flight, one
+        statistics record per range, and a copy stream with one event per range."""
+        with torch.no_grad():
+            self._staging = zeroed_arena(max(self.world - 1, 1) * shard, self._copy_dtype, self.device)
+        step = round_up(-(-shard // COPY_PULL_PIECES), ALIGN)
+        self._pull_ranges = [(off, min(step, shard - off)) for off in range(0, shard, step)]
+        self._records = torch.zeros((len(self._pull_ranges), len(N.STATS_FIELDS)), dtype=torch.float64,
+                                    device=self.device)
+        self._ready_status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._copy_stream = torch.cuda.Stream(self.device)
+        self._pull_events = [torch.cuda.Event() for _ in self._pull_ranges]
+
+    def _pull_by_copy(self, scale, stats) -> None:
+        """The reduce-scatter with copy-engine reads: READY to and from every rank; the peers'
+        contributions to this rank's shard copied range by range into local staging (one
+        cudaMemcpyAsync per peer and range, on the copy stream); each range reduced in rank
+        order with its statistics as soon as its copies land; then the statistics exchange
+        over the range records. Every rank's gradients are read only after its READY, and
+        this rank's STATS follows the end of its copies, so the closing DONE exchange still
+        means that no peer reads this rank's gradients any more."""
+        k = self._kernels
+        sync = self._sync_args()
+        compute = torch.cuda.current_stream(self.device)
+        k.flag_exchange(sync, self.world, N.NT_ZERO_READY, self._ready_status)
+        self._copy_stream.wait_stream(compute)
+        esize = self.flat_grads.element_size()
+        shard = self.grad_shard.numel()
+        base = self._staging.data_ptr()
+        slot = {q: i for i, q in enumerate(q for q in range(self.world) if q != self.rank)}
+        handle = N.stream_handle(self._copy_stream)
+        for (off, n), event in zip(self._pull_ranges, self._pull_events):
+            for q, i in slot.items():
+                N.call("nt_memcpy_async", base + (i * shard + off) * esize, self._sources[q] + off * esize,
+                       n * esize, handle)
+            event.record(self._copy_stream)
+        for j, ((off, n), event) in enumerate(zip(self._pull_ranges, self._pull_events)):
+            compute.wait_event(event)
+            sources = [self._sources[q] + off * esize if q == self.rank else base + (slot[q] * shard + off) * esize
+                       for q in range(self.world)]
+            k.reduce_stats(sources, self.grad_shard[off:off + n], self._records[j], scale=scale,
+                           average=self._average)
+        k.stats_exchange(self._records, sync, self.world, self._ready_status, stats)
 
     def _uses_flags(self) -> bool:
         return self.transport == "p2p" and self._exchange == "flags"
@@ -484,11 +556,15 @@ class ZeroAdamW(_FirstOrderAdam):
         if self.transport == "p2p":
             stats = stats_tensor(self.device)
             if self._uses_flags():
-                # READY, the pull, the statistics exchange and the finalize in one kernel: the
-                # record comes back global (the same on every rank).
+                # READY, the pull, the statistics exchange and the finalize: the record comes
+                # back global (the same on every rank). With pull='sm' all of it is one
+                # kernel; with pull='copy' the copy engines read the peers.
                 self._epoch += 1
-                self._kernels.reduce_exchange(self._sources, self.grad_shard, stats, scale=scale,
-                                              average=self._average, sync=self._sync_args())
+                if self._pull == "copy":
+                    self._pull_by_copy(scale, stats)
+                else:
+                    self._kernels.reduce_exchange(self._sources, self.grad_shard, stats, scale=scale,
+                                                  average=self._average, sync=self._sync_args())
                 self._local_stats = (scale, stats, True)
                 self._flag_step = True
             else:

@@ -34,7 +34,7 @@ def _round_to(dtype: str):
     return round_to_bf16
 
 
-def _worker(rank, world, port, out_path, transport, lazy, exchange, norm_type=2.0, dtype="bf16"):
+def _worker(rank, world, port, out_path, transport, lazy, exchange, norm_type=2.0, dtype="bf16", pull="sm"):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -51,7 +51,7 @@ def _worker(rank, world, port, out_path, transport, lazy, exchange, norm_type=2.
         decay, no_decay = shape.groups()
         groups = [{"params": [params[i] for i in decay], "weight_decay": 0.1},
                   {"params": [params[i] for i in no_decay], "weight_decay": 0.0}]
-        opt = ZeroAdamW(groups, lr=3e-4, model_dtype=model_dtype, transport=transport, exchange=exchange)
+        opt = ZeroAdamW(groups, lr=3e-4, model_dtype=model_dtype, transport=transport, exchange=exchange, pull=pull)
         assert opt.transport == transport
         scaler = GradScaler(1024.0, growth_interval=2)
         reduced, local, norms, stepped = [], [], [], []
@@ -95,11 +95,13 @@ def _worker(rank, world, port, out_path, transport, lazy, exchange, norm_type=2.
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport,lazy,exchange,norm_type,dtype", [
-    ("nccl", True, "flags", 2.0, "bf16"), ("p2p", True, "flags", 2.0, "bf16"), ("p2p", False, "flags", 2.0, "bf16"),
-    ("p2p", True, "nccl", 2.0, "bf16"), ("p2p", True, "flags", float("inf"), "bf16"),
-    ("p2p", True, "flags", 3.0, "bf16"), ("p2p", False, "flags", 2.0, "f16")])
-def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange, norm_type, dtype):
+@pytest.mark.parametrize("transport,lazy,exchange,norm_type,dtype,pull", [
+    ("nccl", True, "flags", 2.0, "bf16", "sm"), ("p2p", True, "flags", 2.0, "bf16", "sm"),
+    ("p2p", False, "flags", 2.0, "bf16", "sm"), ("p2p", True, "nccl", 2.0, "bf16", "sm"),
+    ("p2p", True, "flags", float("inf"), "bf16", "sm"), ("p2p", True, "flags", 3.0, "bf16", "sm"),
+    ("p2p", False, "flags", 2.0, "f16", "sm"), ("p2p", True, "flags", 2.0, "bf16", "copy"),
+    ("p2p", False, "flags", float("inf"), "f16", "copy")])
+def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange, norm_type, dtype, pull):
     if torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     import torch.multiprocessing as mp
@@ -108,7 +110,7 @@ def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange, norm_type, dt
     from oracle import amp as oamp
     from oracle import clip as oclip
     out_path = tmp_path / "zero.npz"
-    mp.spawn(_worker, args=(WORLD, _free_port(), str(out_path), transport, lazy, exchange, norm_type, dtype),
+    mp.spawn(_worker, args=(WORLD, _free_port(), str(out_path), transport, lazy, exchange, norm_type, dtype, pull),
              nprocs=WORLD, join=True)
     round_model = _round_to(dtype)
     out = np.load(out_path)
@@ -171,7 +173,7 @@ def test_zero1_matches_oracle(tmp_path, transport, lazy, exchange, norm_type, dt
         np.testing.assert_array_equal(out[f"copy{orig}"], round_model(out[f"master{k}"]))
 
 
-def _stall_worker(rank, world, port, store_port, out_path):
+def _stall_worker(rank, world, port, store_port, out_path, pull="sm"):
     """Both ranks take one step; then rank 1 stops taking steps (between steps, nothing of
     it in flight) but stays alive, so its memory stays mapped, until rank 0 is done. Rank
     0's next step finds no READY from rank 1: the waits end after exchange_timeout, the
@@ -189,7 +191,8 @@ def _stall_worker(rank, world, port, store_port, out_path):
         from namitorch_b200.zero import ZeroAdamW
         shape = W.CONFIG_SMALL
         params = [torch.nn.Parameter(torch.from_numpy(a).cuda()) for a in W.init_params(shape, seed=0)]
-        opt = ZeroAdamW(params, lr=3e-4, model_dtype=torch.bfloat16, transport="p2p", exchange_timeout=1.0)
+        opt = ZeroAdamW(params, lr=3e-4, model_dtype=torch.bfloat16, transport="p2p", exchange_timeout=1.0,
+                        pull=pull)
         scaler = GradScaler(1024.0)
 
         def step():
@@ -226,12 +229,13 @@ def _stall_worker(rank, world, port, store_port, out_path):
         dist.destroy_process_group()
 
 
-def test_a_rank_that_stops_between_steps_makes_the_others_skip_with_an_error(tmp_path):
+@pytest.mark.parametrize("pull", ["sm", "copy"])
+def test_a_rank_that_stops_between_steps_makes_the_others_skip_with_an_error(tmp_path, pull):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
     out_path = tmp_path / "stall.npz"
-    mp.spawn(_stall_worker, args=(2, _free_port(), _free_port(), str(out_path)), nprocs=2, join=True)
+    mp.spawn(_stall_worker, args=(2, _free_port(), _free_port(), str(out_path), pull), nprocs=2, join=True)
     out = np.load(out_path)
     assert int(out["error"]) == 3          # the reduce-scatter's wait and the update's wait both ran out
     assert not bool(out["stepped"]) and np.isnan(float(out["norm"]))

@@ -213,3 +213,85 @@ def test_exchange_argument_checks(cuda_device):
     with pytest.raises(ValueError, match="norm_type must be 2 or inf"):
         k.reduce_exchange([s.data_ptr() for s in src], dest, out, scale=None, average=True,
                           sync=_sync([box, box], 0, 1, error), norm_type=3.0)
+
+
+def test_flag_exchange_signals_every_mailbox_and_reports_a_missing_rank(cuda_device):
+    """nt_zero_flag_exchange (the READY / DONE kernel of the copy-engine pull): with the other
+    rank's flag already in this rank's mailbox it returns status 0 and writes this rank's flag
+    into both mailboxes; without it the wait ends after the bound with status 1 and the error
+    bit of that flag (bit 0 for READY, bit 1 for DONE)."""
+    k = CudaShardKernels(cuda_device)
+    boxes = [_mailbox(), _mailbox()]
+    error = torch.zeros(1, dtype=torch.int32, device="cuda")
+    status = torch.full((1,), 7, dtype=torch.int32, device="cuda")
+    _set_flag(boxes[0], N.NT_ZERO_READY, 1, 5)
+    k.flag_exchange(_sync(boxes, 0, 5, error), 2, N.NT_ZERO_READY, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0 and int(error.item()) == 0
+    assert _flag(boxes[0], N.NT_ZERO_READY, 0) == 5 and _flag(boxes[1], N.NT_ZERO_READY, 0) == 5
+    k.flag_exchange(_sync(boxes, 0, 5, error, timeout_ns=20_000_000), 2, N.NT_ZERO_DONE, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 1 and int(error.item()) == 2
+    assert _flag(boxes[1], N.NT_ZERO_DONE, 0) == 5
+    k.flag_exchange(_sync(boxes, 0, 6, error, timeout_ns=20_000_000), 2, N.NT_ZERO_READY, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 1 and int(error.item()) == 3
+    assert torch.zeros(4, device="cuda").sum().item() == 0.0   # the device is still usable
+
+
+def test_stats_exchange_over_piece_records_matches_the_fused_exchange(cuda_device):
+    """nt_zero_stats_exchange adds the records of the shard's pieces in order and exchanges
+    the totals: with one rank, the result equals the fused kernel's record for the whole
+    shard up to the order of the float64 sum; with two ranks (the other's totals and STATS
+    flag preset), the norm covers both; a failed READY (status 1) skips the exchange and
+    reports found_inf with a NaN norm."""
+    k = CudaShardKernels(cuda_device)
+    count = 400_000
+    src = _grads(1, count, 3)[0]
+    scale = torch.tensor([1024.0], device="cuda")
+    whole = stats_tensor(cuda_device)
+    dest = torch.zeros(count, dtype=torch.bfloat16, device="cuda")
+    k.reduce_stats([src.data_ptr()], dest, whole, scale=scale, average=True)
+    k.finalize(whole, 2.0)
+    pieces = [(0, 128_000), (128_000, 128_000), (256_000, 144_000)]
+    records = torch.zeros((len(pieces), len(N.STATS_FIELDS)), dtype=torch.float64, device="cuda")
+    for j, (off, n) in enumerate(pieces):
+        k.reduce_stats([src.data_ptr() + 2 * off], dest[off:off + n], records[j], scale=scale, average=True)
+    ok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    error = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = stats_tensor(cuda_device)
+    k.stats_exchange(records, _sync([_mailbox()], 0, 1, error), 1, ok, out)
+    torch.cuda.synchronize()
+    f = {name: N.STATS_FIELDS.index(name) for name in ("sumsq", "nonfinite", "nan", "maxabs", "norm", "found_inf")}
+    assert abs(float(out[f["sumsq"]]) - float(whole[f["sumsq"]])) <= 1e-12 * float(whole[f["sumsq"]])
+    assert abs(float(out[f["norm"]]) - float(whole[f["norm"]])) <= 1e-12 * float(whole[f["norm"]])
+    for name in ("nonfinite", "nan", "maxabs", "found_inf"):
+        assert float(out[f[name]]) == float(whole[f[name]]), name
+    # Two ranks: the other rank's totals are already in this rank's mailbox.
+    boxes = [_mailbox(), _mailbox()]
+    _stats_slot(boxes[0], 1)[:] = torch.tensor([3.0, 0.0, 0.0, 0.5], dtype=torch.float64)
+    _set_flag(boxes[0], N.NT_ZERO_STATS, 1, 4)
+    k.stats_exchange(records, _sync(boxes, 0, 4, error), 2, ok, out)
+    torch.cuda.synchronize()
+    want = float(records[:, f["sumsq"]].sum().item()) + 3.0
+    assert abs(float(out[f["norm"]]) - math.sqrt(want)) <= 1e-12 * math.sqrt(want)
+    assert _flag(boxes[1], N.NT_ZERO_STATS, 0) == 4 and int(error.item()) == 0
+    # A READY that ran out earlier in the step: no exchange, a skipped step.
+    bad = torch.ones(1, dtype=torch.int32, device="cuda")
+    k.stats_exchange(records, _sync(boxes, 0, 5, error), 2, bad, out)
+    torch.cuda.synchronize()
+    assert math.isnan(float(out[f["norm"]])) and float(out[f["found_inf"]]) == 1.0 and int(error.item()) == 1
+    assert _flag(boxes[1], N.NT_ZERO_STATS, 0) == 4    # nothing was signalled
+
+
+def test_flag_and_stats_exchange_reject_bad_arguments(cuda_device):
+    k = CudaShardKernels(cuda_device)
+    error = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sync = _sync([_mailbox()], 0, 1, error)
+    with pytest.raises(ValueError, match="flag"):
+        k.flag_exchange(sync, 1, 3)
+    with pytest.raises(ValueError, match="num_ranks"):
+        k.flag_exchange(sync, 9, N.NT_ZERO_READY)
+    records = torch.zeros((1, len(N.STATS_FIELDS)), dtype=torch.float64, device="cuda")
+    with pytest.raises(ValueError, match="norm_type"):
+        k.stats_exchange(records, sync, 1, None, stats_tensor(cuda_device), norm_type=3.0)
