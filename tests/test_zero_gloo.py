@@ -236,3 +236,16 @@ def test_zero1_two_ranks_match_single_process_oracle(tmp_path, lazy):
         np.testing.assert_allclose(out[f"master{k}"], arrays[k], rtol=1e-6, atol=1e-9)
         np.testing.assert_allclose(out[f"m{k}"], oracle.state[k]["exp_avg"], rtol=1e-6, atol=1e-9)
         np.testing.assert_array_equal(out[f"copy{k}"], out[f"master{k}"])
+
+
+@pytest.mark.parametrize("kwargs,match", [
+    ({"transport": "tcp"}, "transport"), ({"exchange": "mpi"}, "exchange"), ({"pull": "dma"}, "pull"),
+    ({"pull": "copy", "exchange": "nccl"}, "exchange='flags'"), ({"exchange_timeout": 0}, "exchange_timeout"),
+    ({"pieces": 0}, "pieces"), ({"model_dtype": torch.int8}, "model_dtype")])
+def test_zero_adamw_rejects_bad_options_before_any_collective(kwargs, match):
+    """Option checks come first, so a bad option raises on every rank alike and no rank is
+    left inside a collective."""
+    from namitorch_b200.zero import ZeroAdamW
+    params = [torch.nn.Parameter(torch.zeros(4))]
+    with pytest.raises((ValueError, TypeError), match=match):
+        ZeroAdamW(params, **kwargs)
