@@ -84,3 +84,25 @@ def test_zero_parity_checks_the_group_the_optimizer_registered(world):
         assert (prm.index in decay) == (i < len(decay))
         differs += (i in decay) != (prm.index in decay)   # model order would pick the other group
     assert differs == {2: 0, 4: 2, 8: 3}[world]
+
+
+def test_nvlink_floor_arithmetic(monkeypatch):
+    """The ZeRO-1 floors of the N > 1 line from given link rates: each phase moves
+    (N - 1)/N x 2 B per parameter per GPU and direction; the update phase's floor is the
+    longer of its link time and its HBM time (28 B per shard parameter plus the peers'
+    incoming 2 B copies), so it is HBM-bound at N = 2 and link-bound at N = 8."""
+    from types import SimpleNamespace
+    monkeypatch.setattr(bench, "measure_peer_bandwidth", lambda world, rank, device: {"pull_gbs": 640.0,
+                                                                                       "push_gbs": 630.0})
+    monkeypatch.setattr(bench, "measured_peak", lambda: (6500.0, "measured"))
+    P = 1_315_721_216
+    for world, bound in ((2, "hbm"), (8, "nvlink")):
+        link = 2.0 * P * (world - 1) / world
+        out = bench.nvlink_section(SimpleNamespace(rank=0, device="cpu"), P, world, 7.0,
+                                   {"reduce_scatter": 3.0, "update_with_overlapped_all_gather": 3.5})
+        assert out["bytes_per_gpu_per_phase"] == link
+        assert abs(out["floor_ms"] - (link / 640e9 + link / 630e9) * 1e3) < 1e-9
+        hbm_update = (bench.BYTES_UPDATE + 2.0 * (world - 1)) * (P / world) / 6500e9 * 1e3
+        assert abs(out["update_phase"]["floor_ms"] - max(link / 630e9 * 1e3, hbm_update)) < 1e-9
+        assert out["update_phase"]["bound"] == bound
+        assert abs(out["reduce_scatter_gbs"] - link / 3.0e-3 / 1e9) < 1e-6
